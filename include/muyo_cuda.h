@@ -1,0 +1,306 @@
+/*
+ * muyo_cuda.h - the C-ABI of the B200 (sm_100a) decode-step kernel set.
+ *
+ * One shared library, libmuyo_cuda.so, replaces the reference's per-op Vulkan dispatches
+ * (llama.cpp GLSL shaders driven by Muyo's RenderGraph) behind the reference's op-node interfaces.
+ * Every entry point takes a POD parameter block carrying the same semantic fields as the
+ * reference's push-constant block for that op (src/LlamaContracts.h), plain device pointers and a
+ * CUDA stream (as `void*`, a cudaStream_t; NULL is the legacy default stream).
+ *
+ * Conventions (as in src/LlamaContracts.h:14-19): dimensions and strides are in ELEMENTS, not bytes,
+ * most-minor dimension first. Buffers are owned by the caller; the op entry points allocate nothing.
+ * Ops that need scratch take a caller-owned workspace and export a *_workspace_size query.
+ *
+ * Errors: every call returns MUYO_OK (0) or a negative MUYO_E* code and never throws; the message of
+ * the last failure on the calling thread is muyo_cuda_last_error(). Arguments are validated before
+ * any CUDA call, so a rejected call has no side effect. Kernel launches are asynchronous on the given
+ * stream; device-side faults surface on a later synchronising call as MUYO_ECUDA.
+ *
+ * Reference citations are file:line within the muyo-llm project.
+ */
+#ifndef MUYO_CUDA_H
+#define MUYO_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status ----------------------------------------------------------------------------------- */
+#define MUYO_OK 0
+#define MUYO_EINVAL (-1)       /* a shape, stride, pointer or alignment argument is invalid */
+#define MUYO_ECUDA (-2)        /* a CUDA runtime call failed */
+#define MUYO_ETIMEOUT (-3)     /* a bounded device-side wait gave up */
+#define MUYO_ENOMEM (-4)       /* a set-up allocation failed (model create only) */
+#define MUYO_EUNSUPPORTED (-5) /* a contract field the B200 kernels do not implement */
+#define MUYO_ESTATE (-6)       /* call out of order (e.g. cache full, model not finalised) */
+
+/* Replaces HeadlessContext's device bring-up (src/HeadlessContext.h:25-66): selects the CUDA
+ * device for the calling thread and creates its primary context. */
+int muyo_cuda_init(int device);
+/* Replaces ~HeadlessContext: releases library-owned per-device state (never caller buffers). */
+int muyo_cuda_shutdown(void);
+/* Message of the last failing call on this thread ("" if none). */
+const char* muyo_cuda_last_error(void);
+/* Library version string ("muyo_cuda <semver> sm_100a"). */
+const char* muyo_cuda_version(void);
+
+/* ---- GEMV: mul_mat_vec ------------------------------------------------------------------------
+ * Replaces MatVecExecute + mul_mat_vec_{f16,f32}_f32_f32 (src/FullModel.cpp:133-175,
+ * shaders/llama/mul_mat_vec.comp, mul_mat_vec_base.glsl:49-100). Fields mirror
+ * LlamaMatVecPushConstants (src/LlamaContracts.h:66-84) plus the dispatch the node issued:
+ *   d[b*batch_stride_d + r] = sum_k A[ba*batch_stride_a + r*stride_a + k] * B[b*batch_stride_b + k]
+ *                             (+ fuse0[b*batch_stride_d + r] if BIAS0) (+ fuse1[...] if BIAS1)
+ * for r < rows, b < batches, with ba = (b / ne12 / broadcast3) * ne02 + (b % ne12) / broadcast2
+ * (the GQA broadcast). FP32 accumulation. */
+#define MUYO_MATVEC_BIAS0 0x1u
+#define MUYO_MATVEC_BIAS1 0x2u
+#define MUYO_MATVEC_SCALE0 0x4u /* accepted by the contract, not implemented: MUYO_EUNSUPPORTED */
+#define MUYO_MATVEC_SCALE1 0x8u /* idem */
+
+typedef struct MuyoMatVecParams {
+    uint32_t ncols;    /* K */
+    uint32_t stride_a; /* row stride of A (0 = ncols, as src/FullModel.cpp:158) */
+    uint32_t stride_b; /* 0 = ncols */
+    uint32_t stride_d; /* output row bound per batch (rows must not exceed it) */
+    uint32_t batch_stride_a, batch_stride_b, batch_stride_d;
+    uint32_t fusion_flags;
+    uint32_t ne02, ne12, broadcast2, broadcast3; /* 0 is read as 1 */
+    uint32_t rows;    /* rows computed (the node's dispatch x; src/FullModel.cpp:172) */
+    uint32_t batches; /* the node's dispatch y (0 is read as 1) */
+} MuyoMatVecParams;
+
+/* A is F16 (IEEE binary16 bits). */
+int muyo_cuda_mat_vec_f16(const MuyoMatVecParams* p, const void* a, const float* b, float* d, const float* fuse0,
+                          const float* fuse1, void* stream);
+/* A is F32 (the attention score / value GEMVs, src/FullModel.cpp:793-844). */
+int muyo_cuda_mat_vec_f32(const MuyoMatVecParams* p, const float* a, const float* b, float* d, const float* fuse0,
+                          const float* fuse1, void* stream);
+
+/* ---- generic binary head (add, rms_norm, get_rows) ---------------------------------------------
+ * Mirrors LlamaAddPushConstants (src/LlamaContracts.h:22-38) without the kernel-private
+ * misalign_offsets: A = operand 0, B = operand 1, D = output; ne/nb most-minor first, elements. */
+typedef struct MuyoBinaryParams {
+    uint32_t ne; /* element count of D */
+    uint32_t ne00, ne01, ne02, ne03, nb00, nb01, nb02, nb03;
+    uint32_t ne10, ne11, ne12, ne13, nb10, nb11, nb12, nb13;
+    uint32_t ne20, ne21, ne22, ne23, nb20, nb21, nb22, nb23;
+    float param1; /* rms_norm: eps */
+    float param2;
+    int32_t param3;
+} MuyoBinaryParams;
+
+/* Replaces AddExecute + add.comp (src/FullModel.cpp:250-284): D = A + B, B repeated over A's
+ * shape by modulo (ggml broadcast) when smaller. */
+int muyo_cuda_add(const MuyoBinaryParams* p, const float* a, const float* b, float* d, void* stream);
+/* Replaces RmsNormExecute + rms_norm.comp with do_multiply (src/FullModel.cpp:215-247):
+ * each row of ne00 values: D = A * rsqrt(mean(A^2) + param1) * B[col % ne10]. */
+int muyo_cuda_rms_norm(const MuyoBinaryParams* p, const float* a, const float* w, float* d, void* stream);
+/* Replaces GetRowsExecute + get_rows_{f16_f32,f32} (src/FullModel.cpp:424-458):
+ * D[i10, i11, i12][:] = float(A[B[i10, i11, i12], i11, i12][:]), B int32 row ids. */
+int muyo_cuda_get_rows_f16(const MuyoBinaryParams* p, const void* a, const int32_t* b, float* d, void* stream);
+int muyo_cuda_get_rows_f32(const MuyoBinaryParams* p, const float* a, const int32_t* b, float* d, void* stream);
+
+/* ---- GLU (swiglu) -------------------------------------------------------------------------------
+ * Mirrors LlamaGluPushConstants (src/LlamaContracts.h:182-199) minus the fastdiv magic. Replaces
+ * SwigluExecute + swiglu.comp (src/FullModel.cpp:287-327): D = silu(gate) * up. mode 2 (split):
+ * gate = A, up = B; mode 0: one A row holds [gate | up]; mode 1: [up | gate]. */
+#define MUYO_GLU_HALVES 0u
+#define MUYO_GLU_SWAPPED 1u
+#define MUYO_GLU_SPLIT 2u
+typedef struct MuyoGluParams {
+    uint32_t N;    /* elements of D */
+    uint32_t ne00; /* row length of A */
+    uint32_t ne20; /* row length of D */
+    uint32_t mode;
+    float alpha, limit; /* unused by swiglu */
+    uint32_t nb00, nb01, nb02, nb03;
+    uint32_t nb10, nb11, nb12, nb13;
+    uint32_t nb20, nb21, nb22, nb23;
+    uint32_t ne21, ne22;
+} MuyoGluParams;
+int muyo_cuda_swiglu(const MuyoGluParams* p, const float* a, const float* b, float* d, void* stream);
+
+/* ---- RoPE ---------------------------------------------------------------------------------------
+ * Mirrors LlamaRopePushConstants (src/LlamaContracts.h:125-153) minus the set-rows fusion fields.
+ * Replaces RopeExecute + rope_neox.comp / rope_norm (src/FullModel.cpp:179-212,
+ * shaders/llama/rope_funcs.glsl:14-114). For row (i1, i2, i3): theta = pos[i2] * theta_scale^(i0/2)
+ * (/ freq_factors[i0/2] if has_ff), YaRN-corrected when ext_factor != 0, negated if is_back; NEOX
+ * pairs channels (j, j + n_dims/2), NORMAL pairs (2j, 2j+1); channels outside [n_offs, n_offs +
+ * n_dims) are copied. Output element = d_offset + i1*nb11 + i2*nb12 + i3*nb13 + channel. */
+#define MUYO_ROPE_NORMAL 0u
+#define MUYO_ROPE_NEOX 2u
+typedef struct MuyoRopeParams {
+    uint32_t rope_mode;
+    uint32_t nrows; /* ne01 * ne02 * ne03 */
+    uint32_t n_dims;
+    uint32_t n_offs;
+    float freq_scale, freq_base, ext_factor, attn_factor;
+    float corr_dims[2];
+    float theta_scale;
+    uint32_t has_ff;
+    uint32_t is_back;
+    uint32_t ne00, ne01, ne02;
+    uint32_t nb01, nb02, nb03;
+    uint32_t nb11, nb12, nb13;
+    uint32_t a_offset, d_offset;
+} MuyoRopeParams;
+int muyo_cuda_rope(const MuyoRopeParams* p, const float* x, const int32_t* pos, const float* freq_factors, float* d,
+                   void* stream);
+
+/* ---- soft_max -----------------------------------------------------------------------------------
+ * Mirrors LlamaSoftMaxPushConstants (src/LlamaContracts.h:255-274). Replaces SoftMaxExecute +
+ * soft_max.comp (src/FullModel.cpp:331-349): per row, v = x*scale + slope*mask; D = exp(v - max) /
+ * sum (+ exp(sink - max) in the sum if has_sinks). Rows: nrows_x of KX columns. */
+typedef struct MuyoSoftMaxParams {
+    uint32_t KX, KY;
+    uint32_t ne00, ne01, ne02, ne12, ne13;
+    uint32_t nb11, nb12, nb13;
+    float scale, max_bias, m0, m1;
+    uint32_t n_head_log2;
+    uint32_t nrows_x;
+    uint32_t has_sinks;
+} MuyoSoftMaxParams;
+int muyo_cuda_soft_max(const MuyoSoftMaxParams* p, const float* x, const float* mask, const float* sinks, float* d,
+                       void* stream);
+
+/* ---- argmax -------------------------------------------------------------------------------------
+ * Mirrors LlamaGenericHeadPushConstants (src/LlamaContracts.h:224-232): KY rows of KX logits.
+ * Replaces ArgmaxExecute + argmax.comp (src/FullModel.cpp:461-484) with the tie rule of the host's
+ * greedy pick (src/Sampler.cpp:32-43): the FIRST index of the maximum. Large rows are split across
+ * CTAs; the workspace (muyo_cuda_argmax_workspace_size bytes, any content) holds the partials. */
+typedef struct MuyoGenericParams {
+    uint32_t KX, KY;
+    float param1, param2, param3, param4;
+} MuyoGenericParams;
+size_t muyo_cuda_argmax_workspace_size(const MuyoGenericParams* p);
+int muyo_cuda_argmax(const MuyoGenericParams* p, const float* a, int32_t* d, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/* ---- copy (cpy_f32_f32) -------------------------------------------------------------------------
+ * Mirrors copy.comp's unary head (src/FullModel.cpp:353-362) minus the fastdiv magic: element i of
+ * the ne-element copy is read at A's coordinates of i (ne0x/nb0x) and written at D's coordinates
+ * of i (ne1x/nb1x) plus d_offset. Replaces CopyValueColumnExecute's transposing V append
+ * (src/FullModel.cpp:376-420), where the position travelled in misalign_offsets. */
+typedef struct MuyoUnaryParams {
+    uint32_t ne;
+    uint32_t ne00, ne01, ne02, ne03, nb00, nb01, nb02, nb03;
+    uint32_t ne10, ne11, ne12, ne13, nb10, nb11, nb12, nb13;
+    uint32_t a_offset, d_offset;
+} MuyoUnaryParams;
+int muyo_cuda_copy_f32(const MuyoUnaryParams* p, const float* a, float* d, void* stream);
+
+/* ---- decode attention over the KV cache ---------------------------------------------------------
+ * Replaces the three-node scores GEMV -> soft_max -> value GEMV chain plus the K rope append and the
+ * transposing V copy (src/FullModel.cpp:757-844; checks src/Attention.cpp:75-306 and
+ * src/KvCache.cpp:94-430). One split-K flash-decoding kernel: the query heads of one KV head
+ * (GQA group h / (heads/kv_heads), tools/reference_qwen2.py:133) share each K/V tile read.
+ *
+ * Cache layout (both K and V, row-major, no transpose): [kv_heads][max_seq][head_dim], element
+ * type F32 (kv_dtype 0) or F16 (kv_dtype 1). The keys attended are 0 .. n_keys-1, where
+ * n_keys = *pos + 1 when pos is non-NULL (device int32, read on the device so a captured graph
+ * stays position-invariant) or p->n_keys otherwise. q: [heads][head_dim] F32, already rotated.
+ * out: [heads][head_dim] F32. softmax scale p->scale (1/sqrt(head_dim) in the model). */
+#define MUYO_KV_F32 0u
+#define MUYO_KV_F16 1u
+typedef struct MuyoAttentionParams {
+    uint32_t heads, kv_heads, head_dim;
+    uint32_t max_seq;
+    uint32_t n_keys; /* used when pos == NULL */
+    uint32_t kv_dtype;
+    float scale;
+} MuyoAttentionParams;
+size_t muyo_cuda_attention_workspace_size(const MuyoAttentionParams* p);
+int muyo_cuda_attention_decode(const MuyoAttentionParams* p, const float* q, const void* k_cache, const void* v_cache,
+                               const int32_t* pos, float* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* KV append: rotate the new key (NEOX, theta = pos * base^(-2j/head_dim), in double precision as
+ * tools/reference_qwen2.py:84-93) and store it and the new value at row *pos of each KV head,
+ * rounded to the cache type. k, v: [kv_heads][head_dim] F32 (pre-rope key). Replaces k_rope with
+ * dOffset = pos*headDim plus v_copy (src/FullModel.cpp:771-791). */
+int muyo_cuda_kv_append(const MuyoAttentionParams* p, float rope_base, const float* k, const float* v, void* k_cache,
+                        void* v_cache, const int32_t* pos, void* stream);
+
+/* ---- fused Qwen2 decoder layer (one token) ------------------------------------------------------
+ * One decoder layer of the reference's 18-node layer graph (src/FullModel.cpp:685-953) as five
+ * fused kernels: [rms_norm + QKV GEMV + bias] -> [rope + KV append + split-K GQA attention] ->
+ * [o_proj GEMV + residual] -> [rms_norm + gate/up GEMV + SwiGLU] -> [down GEMV + residual].
+ * Weights F16 row-major [out][in] (GGUF [ne0 = in, ne1 = out]); biases and norms F32. wqkv is the
+ * q, k and v projections stacked by rows ([q_dim + 2*kv_dim][hidden]) and bqkv their biases. */
+typedef struct MuyoQwen2Config {
+    uint32_t layers, hidden, ffn, heads, kv_heads, vocab, max_seq;
+    float rms_eps, rope_base;
+    uint32_t kv_dtype; /* MUYO_KV_F32 or MUYO_KV_F16 */
+} MuyoQwen2Config;
+
+typedef struct MuyoLayerWeights {
+    const float* attn_norm;
+    const void* wqkv;
+    const float* bqkv;
+    const void* wo;
+    const float* ffn_norm;
+    const void* wgate;
+    const void* wup;
+    const void* wdown;
+} MuyoLayerWeights;
+
+size_t muyo_cuda_layer_workspace_size(const MuyoQwen2Config* c);
+/* x_in -> x_out (both [hidden] F32, may not alias); k_cache/v_cache are this layer's caches;
+ * pos: device int32 position of the token. */
+int muyo_cuda_layer_step(const MuyoQwen2Config* c, const MuyoLayerWeights* w, void* k_cache, void* v_cache,
+                         const int32_t* pos, const float* x_in, float* x_out, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
+/* ---- whole model (RunFullModel's engine) ---------------------------------------------------------
+ * Replaces RunFullModel's graph build, weight upload and per-token feedToken/sampleNext loop
+ * (src/FullModel.cpp:487-1291, header src/FullModel.h:34). The model owns its device weights, KV
+ * cache and scratch (allocated once, in create/finalize - never per token). One decode step is one
+ * CUDA-graph replay of 5*layers+1 kernels; the position, the fed token and the greedy pick live in
+ * device memory, so a whole prompt + generation is a loop of replays with no host round trip. */
+typedef struct MuyoModel MuyoModel;
+int muyo_model_create(const MuyoQwen2Config* c, int device, MuyoModel** out);
+/* Upload one tensor by its GGUF name (src/FullModel.cpp:582-601), from host memory: F16 matrices
+ * as binary16 bits, F32 vectors. output.weight may be omitted when tied to token_embd.weight. */
+int muyo_model_set_tensor(MuyoModel* m, const char* name, const void* host, size_t bytes);
+/* Load every tensor from a Qwen2 GGUF file (F16/F32 tensors, src/Gguf.cpp:337-348). */
+int muyo_model_load_gguf(MuyoModel* m, const char* path);
+/* Check every tensor is present and build the step graph. */
+int muyo_model_finalize(MuyoModel* m, void* stream);
+/* Empty the KV cache (positions restart at 0). */
+int muyo_model_reset(MuyoModel* m, void* stream);
+/* Feed prompt[0..n_prompt) then decode n_predict greedy ids (src/FullModel.cpp:1173-1208: every
+ * fed and generated id passes one decode step, the last generated id included). Host buffers:
+ * prompt is copied in, out_tokens (n_predict ids) copied back; blocks until done. Continues from
+ * the current cache position (chat-style append), so call muyo_model_reset for a fresh sequence. */
+int muyo_model_generate(MuyoModel* m, const int32_t* prompt, int n_prompt, int n_predict, int32_t* out_tokens,
+                        void* stream);
+/* Device-buffer variant (asynchronous on stream). */
+int muyo_model_generate_device(MuyoModel* m, const int32_t* prompt_dev, int n_prompt, int n_predict,
+                               int32_t* out_tokens_dev, void* stream);
+/* One decode step for `token` at the current position; logits (vocab F32, device or host pointer,
+ * may be NULL) and the greedy id (host, may be NULL) are returned. */
+int muyo_model_step(MuyoModel* m, int32_t token, float* logits, int32_t* next_token, void* stream);
+/* Current position (tokens in the cache). */
+int muyo_model_position(const MuyoModel* m, int32_t* pos);
+/* Device pointers of the model's buffers, for tests: "logits", "hidden", "k_cache", "v_cache". */
+int muyo_model_buffer(MuyoModel* m, const char* name, void** ptr, size_t* bytes);
+int muyo_model_destroy(MuyoModel* m);
+
+/* ---- row-sharded GEMV + cross-GPU greedy (multi-GPU LM head) --------------------------------------
+ * One GPU's share of a row-sharded GEMV with the argmax folded into its epilogue: rows
+ * [row_begin, row_begin + rows) of A ([rows][ncols] F16 local shard), d = A x, and the shard's
+ * (max value, first global index) written to pair_out[0..1] as {float value, int32 index}.
+ * The pairs of all ranks are exchanged (NCCL all-gather) and muyo_cuda_argmax_pairs picks the
+ * first-index maximum over them. Workspace: muyo_cuda_argmax_workspace_size with KX = rows. */
+int muyo_cuda_mat_vec_f16_argmax(const MuyoMatVecParams* p, const void* a, const float* b, float* d,
+                                 uint32_t row_begin, void* pair_out, void* workspace, size_t workspace_bytes,
+                                 void* stream);
+int muyo_cuda_argmax_pairs(const void* pairs, uint32_t n_pairs, int32_t* d, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MUYO_CUDA_H */

@@ -1,0 +1,1098 @@
+// The fused decode step: the reference's 18-node Qwen2 layer (src/FullModel.cpp:685-953) as five
+// kernels, the LM head with the greedy pick folded in, and the model engine that replays the whole
+// step as one CUDA graph (src/FullModel.cpp:1096-1208 feedToken/sampleNext, without the host).
+//
+//   k_gemv<EMBED_NORM|NORM, BIAS>  rms_norm (+ embedding gather on layer 0) -> stacked QKV GEMV + bias
+//   k_attention<FUSED>             NeoX RoPE of q and k, KV append, split-K GQA attention
+//   k_gemv<PLAIN, RESIDUAL>        o_proj GEMV + residual add
+//   k_gemv<NORM, SWIGLU>           rms_norm -> gate and up GEMVs (one pass, two matrices) -> SwiGLU
+//   k_gemv<PLAIN, RESIDUAL>        down_proj GEMV (K split across warps) + residual add
+//   k_gemv<NORM, LOGITS>           final rms_norm -> LM head GEMV -> logits, argmax, next token
+#include <climits>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "attention.cuh"
+#include "common.cuh"
+#include "gemv.cuh"
+
+namespace muyo {
+
+constexpr int kGemvThreads = 256;  // 8 warps
+constexpr int kGemvWarps = kGemvThreads / 32;
+
+enum Prologue { PRO_PLAIN = 0, PRO_NORM = 1, PRO_EMBED_NORM = 2 };
+enum Epilogue { EPI_BIAS = 1, EPI_RESIDUAL = 2, EPI_SWIGLU = 3, EPI_LOGITS = 4 };
+
+struct Pair {
+    float v;
+    int i;
+};
+
+// Device-resident decode control: the step counter is the position; tokens[] holds every fed and
+// generated id by position (the reference's `fed`, src/FullModel.cpp:1061).
+struct Control {
+    int32_t step;        // position of the token being decoded
+    int32_t prompt_end;  // tokens[s] for s < prompt_end are forced (prompt), later ones are generated
+    int32_t total;       // tokens[] is written for positions < total
+    int32_t greedy;      // the last step's raw argmax
+};
+
+struct GemvFused {
+    // prologue
+    const float* x;        // PLAIN / NORM input
+    const float* norm_w;   // NORM weight
+    float eps;
+    const __half* embd;    // EMBED_NORM table [vocab][K]
+    const int32_t* tokens;
+    const Control* ctrl_ro;
+    float* x_copy;         // EMBED_NORM: CTA 0 stores the embedded row (the residual stream)
+    int K;
+    // matrices
+    const __half* w0;
+    const __half* w1;
+    size_t ldw;
+    int rows;
+    // epilogue
+    const float* bias;
+    const float* res;
+    float* y;
+    Pair* part;         // LOGITS: per-CTA best
+    int32_t* counter;   // LOGITS: arrival counter (self-resetting)
+    Control* ctrl;      // LOGITS: next-token selection and step advance
+    int32_t* tokens_rw;
+};
+
+// Stage the GEMV input vector in shared memory (split layout of gemv.cuh). NORM and EMBED_NORM
+// apply the numpy reference's rms_norm, x / sqrt(mean(x^2) + eps) * w (tools/reference_qwen2.py:81-82),
+// in F32: the sum of squares with per-thread FMA partials and a shuffle tree.
+template <int PRO>
+__device__ __forceinline__ void stage_input(const GemvFused& a, float* xs, float* red)
+{
+    const int K = a.K, K8 = K / 8;
+    if (PRO == PRO_PLAIN) {
+        for (int k = threadIdx.x; k < K; k += blockDim.x)
+            xs[xs_index(k, K8)] = a.x[k];
+        __syncthreads();
+        return;
+    }
+    const float* src = a.x;
+    const __half* erow = nullptr;
+    if (PRO == PRO_EMBED_NORM) {
+        const int token = a.tokens[a.ctrl_ro->step];
+        erow = a.embd + (size_t)token * K;
+    }
+    float ss = 0.0f;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+        const float v = PRO == PRO_EMBED_NORM ? __half2float(erow[k]) : src[k];
+        ss = fmaf(v, v, ss);
+        if (PRO == PRO_EMBED_NORM && blockIdx.x == 0)
+            a.x_copy[k] = v;
+    }
+    ss = block_sum(ss, red);
+    const float s = __fsqrt_rn(__fdiv_rn(ss, (float)K) + a.eps);
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+        const float v = PRO == PRO_EMBED_NORM ? __half2float(erow[k]) : src[k];
+        xs[xs_index(k, K8)] = __fdiv_rn(v, s) * a.norm_w[k];
+    }
+    __syncthreads();
+}
+
+// One CTA = 8 warps = (8 / KSPLIT) row groups of ROWS rows, the K range of each row group split
+// over KSPLIT warps; partial sums meet in shared memory and are added in a fixed order.
+template <int ROWS, int U, int NMAT, int KSPLIT, int PRO, int EPI>
+__global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvFused a)
+{
+    extern __shared__ float xs[];
+    __shared__ float red[32];
+    __shared__ float ksum[kGemvWarps][NMAT][ROWS];
+    __shared__ Pair best_sm[kGemvWarps];
+    __shared__ int last_flag;
+    constexpr int RG = kGemvWarps / KSPLIT;
+
+    stage_input<PRO>(a, xs, red);
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int rg = warp / KSPLIT, ks = warp % KSPLIT;
+    const int K8 = a.K / 8;
+    const int c_begin = (int)((long long)K8 * ks / KSPLIT), c_end = (int)((long long)K8 * (ks + 1) / KSPLIT);
+    const int ntiles = (a.rows + RG * ROWS - 1) / (RG * ROWS);
+    GemvArgs<ROWS, U, NMAT> ga;
+    ga.w[0] = a.w0;
+    if (NMAT > 1)
+        ga.w[NMAT - 1] = a.w1;
+    ga.ldw = a.ldw;
+    float bv = -INFINITY;
+    int bi = INT_MAX;
+
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+        const int row0 = (tile * RG + rg) * ROWS;
+        const int nvalid = min(ROWS, a.rows - row0);
+        float acc[NMAT][ROWS];
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+            for (int r = 0; r < ROWS; ++r)
+                acc[m][r] = 0.0f;
+        if (nvalid > 0) {
+            warp_gemv_f16_range<ROWS, U, NMAT>(ga, row0, nvalid, xs, K8, c_begin, c_end, lane, acc);
+            warp_reduce_acc<ROWS, NMAT>(acc);
+        }
+        if (KSPLIT > 1) {
+            if (lane == 0) {
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+                    for (int r = 0; r < ROWS; ++r)
+                        ksum[warp][m][r] = acc[m][r];
+            }
+            __syncthreads();
+            if (ks == 0 && lane == 0) {
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+                    for (int r = 0; r < ROWS; ++r) {
+                        float t = ksum[warp][m][r];
+#pragma unroll
+                        for (int j = 1; j < KSPLIT; ++j)
+                            t += ksum[warp + j][m][r];
+                        acc[m][r] = t;
+                    }
+            }
+            __syncthreads();
+        }
+        if (ks == 0 && lane == 0 && nvalid > 0) {
+#pragma unroll
+            for (int r = 0; r < ROWS; ++r) {
+                if (r >= nvalid)
+                    break;
+                const int row = row0 + r;
+                if (EPI == EPI_BIAS) {
+                    a.y[row] = acc[0][r] + a.bias[row];
+                } else if (EPI == EPI_RESIDUAL) {
+                    a.y[row] = a.res[row] + acc[0][r];
+                } else if (EPI == EPI_SWIGLU) {
+                    a.y[row] = silu_mul(acc[0][r], acc[NMAT - 1][r]);
+                } else {  // EPI_LOGITS
+                    const float v = acc[0][r];
+                    a.y[row] = v;
+                    if (pair_better(v, row, bv, bi))
+                        bv = v, bi = row;
+                }
+            }
+        }
+    }
+
+    if (EPI != EPI_LOGITS)
+        return;
+    // Greedy pick (src/Sampler.cpp:32-43, first index of the maximum) across the grid: CTA best,
+    // then the last CTA to arrive reduces all of them and advances the decode control block.
+    if (lane == 0)
+        best_sm[warp] = Pair{bv, bi};
+    __syncthreads();
+    if (warp == 0) {
+        Pair p = lane < kGemvWarps ? best_sm[lane] : Pair{-INFINITY, INT_MAX};
+        warp_argmax(p.v, p.i);
+        if (lane == 0) {
+            a.part[blockIdx.x] = p;
+            __threadfence();
+            last_flag = atomicAdd(a.counter, 1) == (int)gridDim.x - 1;
+        }
+    }
+    __syncthreads();
+    if (!last_flag)
+        return;
+    __threadfence();
+    if (warp == 0) {
+        float v = -INFINITY;
+        int i = INT_MAX;
+        for (int k = lane; k < (int)gridDim.x; k += 32) {
+            const Pair q = a.part[k];
+            if (pair_better(q.v, q.i, v, i))
+                v = q.v, i = q.i;
+        }
+        warp_argmax(v, i);
+        if (lane == 0) {
+            const int greedy = i == INT_MAX ? 0 : i;
+            Control* c = a.ctrl;
+            const int s = c->step;
+            const int next = s + 1 < c->prompt_end ? a.tokens_rw[s + 1] : greedy;
+            if (s + 1 < c->total)
+                a.tokens_rw[s + 1] = next;
+            c->greedy = greedy;
+            c->step = s + 1;
+            *a.counter = 0;
+        }
+    }
+}
+
+template <int ROWS, int U, int NMAT, int KSPLIT, int PRO, int EPI>
+static int launch_gemv(const GemvFused& a, int max_ctas, cudaStream_t s)
+{
+    constexpr int RG = kGemvWarps / KSPLIT;
+    const int ntiles = (a.rows + RG * ROWS - 1) / (RG * ROWS);
+    const int grid = ntiles < max_ctas ? ntiles : max_ctas;
+    const size_t smem = (size_t)a.K * sizeof(float);
+    auto k = k_gemv<ROWS, U, NMAT, KSPLIT, PRO, EPI>;
+    if (smem > 48 * 1024)
+        MUYO_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    k<<<grid, kGemvThreads, smem, s>>>(a);
+    MUYO_LAUNCH_CHECK();
+    return MUYO_OK;
+}
+
+// ---- shapes ------------------------------------------------------------------------------------------
+
+struct Shape {
+    int layers, hidden, ffn, heads, kv_heads, vocab, max_seq, head_dim, q_dim, kv_dim, qkv_rows, gqa;
+    float eps, rope_base;
+    bool kv_f16;
+    int max_chunks;
+};
+
+static int make_shape(const MuyoQwen2Config* c, Shape& s, bool need_vocab)
+{
+    MUYO_REQUIRE(c, "config is null");
+    MUYO_REQUIRE(c->hidden > 0 && c->heads > 0 && c->kv_heads > 0 && c->ffn > 0 && c->max_seq > 0,
+                 "config: hidden, heads, kv_heads, ffn and max_seq must be positive");
+    MUYO_REQUIRE(c->hidden % c->heads == 0, "config: hidden %u not divisible by heads %u", c->hidden, c->heads);
+    MUYO_REQUIRE(c->heads % c->kv_heads == 0, "config: heads %u not divisible by kv_heads %u", c->heads, c->kv_heads);
+    s.layers = (int)c->layers;
+    s.hidden = (int)c->hidden;
+    s.ffn = (int)c->ffn;
+    s.heads = (int)c->heads;
+    s.kv_heads = (int)c->kv_heads;
+    s.vocab = (int)c->vocab;
+    s.max_seq = (int)c->max_seq;
+    s.head_dim = s.hidden / s.heads;
+    s.q_dim = s.heads * s.head_dim;
+    s.kv_dim = s.kv_heads * s.head_dim;
+    s.qkv_rows = s.q_dim + 2 * s.kv_dim;
+    s.gqa = s.heads / s.kv_heads;
+    s.eps = c->rms_eps;
+    s.rope_base = c->rope_base;
+    MUYO_REQUIRE(c->kv_dtype == MUYO_KV_F32 || c->kv_dtype == MUYO_KV_F16, "config: kv_dtype %u", c->kv_dtype);
+    s.kv_f16 = c->kv_dtype == MUYO_KV_F16;
+    MUYO_REQUIRE(s.head_dim == 16 || s.head_dim == 32 || s.head_dim == 64 || s.head_dim == 128,
+                 "config: head_dim %d not supported by the fused step (16, 32, 64, 128)", s.head_dim);
+    MUYO_REQUIRE(s.gqa <= kAttnMaxGroup, "config: %d query heads per KV head exceed %d", s.gqa, kAttnMaxGroup);
+    MUYO_REQUIRE(s.hidden % 8 == 0 && s.ffn % 8 == 0, "config: hidden and ffn must be multiples of 8");
+    MUYO_REQUIRE(s.hidden <= 16384 && s.ffn <= 56 * 1024, "config: hidden/ffn too large for the staged input");
+    MUYO_REQUIRE(!need_vocab || c->vocab > 0, "config: vocab must be positive");
+    MUYO_REQUIRE(s.rope_base > 0.0f && s.eps >= 0.0f, "config: rope_base must be > 0 and rms_eps >= 0");
+    s.max_chunks = (s.max_seq + kAttnKeys - 1) / kAttnKeys;
+    return MUYO_OK;
+}
+
+// Scratch of one layer step: counters first (must start at zero; the kernels leave them zero).
+struct LayerScratch {
+    int32_t* counters;  // [kv_heads]
+    float* qkv;         // [qkv_rows]
+    float* attn;        // [q_dim]
+    float* h1;          // [hidden]
+    float* act;         // [ffn]
+    float* part;        // attention partials
+};
+
+static size_t align256(size_t n) { return (n + 255) / 256 * 256; }
+
+static size_t part_floats(const Shape& s) { return (size_t)s.kv_heads * s.max_chunks * s.gqa * (s.head_dim + 2); }
+
+static size_t layer_scratch_bytes(const Shape& s)
+{
+    return align256(sizeof(int32_t) * (size_t)s.kv_heads) + align256(sizeof(float) * s.qkv_rows) +
+           align256(sizeof(float) * s.q_dim) + align256(sizeof(float) * s.hidden) + align256(sizeof(float) * s.ffn) +
+           align256(sizeof(float) * part_floats(s));
+}
+
+static LayerScratch carve_layer_scratch(const Shape& s, void* base)
+{
+    char* p = static_cast<char*>(base);
+    LayerScratch w;
+    w.counters = reinterpret_cast<int32_t*>(p);
+    p += align256(sizeof(int32_t) * (size_t)s.kv_heads);
+    w.qkv = reinterpret_cast<float*>(p);
+    p += align256(sizeof(float) * s.qkv_rows);
+    w.attn = reinterpret_cast<float*>(p);
+    p += align256(sizeof(float) * s.q_dim);
+    w.h1 = reinterpret_cast<float*>(p);
+    p += align256(sizeof(float) * s.hidden);
+    w.act = reinterpret_cast<float*>(p);
+    p += align256(sizeof(float) * s.ffn);
+    w.part = reinterpret_cast<float*>(p);
+    return w;
+}
+
+struct LayerPtrs {
+    const float* attn_norm;
+    const __half* wqkv;
+    const float* bqkv;
+    const __half* wo;
+    const float* ffn_norm;
+    const __half* wgate;
+    const __half* wup;
+    const __half* wdown;
+};
+
+template <typename KV, int HD>
+static int launch_attention_fused(const Shape& s, const float* qkv, void* kc, void* vc, const int32_t* pos,
+                                  float* out, float* part, int32_t* counters, cudaStream_t st)
+{
+    AttnDev p{s.heads, s.kv_heads, s.gqa, s.max_seq, 0, 1.0f / sqrtf((float)s.head_dim), (double)s.rope_base,
+              s.max_chunks};
+    const size_t smem = (size_t)attn_smem_floats(HD, s.gqa) * sizeof(float);
+    auto k = k_attention<KV, HD, true, true>;
+    if (smem > 48 * 1024)
+        MUYO_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    k<<<dim3(s.kv_heads, s.max_chunks), kAttnThreads, smem, st>>>(p, qkv, static_cast<KV*>(kc), static_cast<KV*>(vc),
+                                                                   pos, out, part, counters);
+    MUYO_LAUNCH_CHECK();
+    return MUYO_OK;
+}
+
+static int attention_fused(const Shape& s, const float* qkv, void* kc, void* vc, const int32_t* pos, float* out,
+                           float* part, int32_t* counters, cudaStream_t st)
+{
+    if (s.kv_f16) {
+        switch (s.head_dim) {
+            case 16: return launch_attention_fused<__half, 16>(s, qkv, kc, vc, pos, out, part, counters, st);
+            case 32: return launch_attention_fused<__half, 32>(s, qkv, kc, vc, pos, out, part, counters, st);
+            case 64: return launch_attention_fused<__half, 64>(s, qkv, kc, vc, pos, out, part, counters, st);
+            default: return launch_attention_fused<__half, 128>(s, qkv, kc, vc, pos, out, part, counters, st);
+        }
+    }
+    switch (s.head_dim) {
+        case 16: return launch_attention_fused<float, 16>(s, qkv, kc, vc, pos, out, part, counters, st);
+        case 32: return launch_attention_fused<float, 32>(s, qkv, kc, vc, pos, out, part, counters, st);
+        case 64: return launch_attention_fused<float, 64>(s, qkv, kc, vc, pos, out, part, counters, st);
+        default: return launch_attention_fused<float, 128>(s, qkv, kc, vc, pos, out, part, counters, st);
+    }
+}
+
+// One decoder layer: x_in (or the embedding of tokens[ctrl->step] when embed != nullptr) -> x_out.
+static int layer_forward(const Shape& s, const LayerPtrs& w, void* kc, void* vc, const int32_t* pos,
+                         const float* x_in, float* x_out, const LayerScratch& ws, const __half* embd,
+                         const int32_t* tokens, const Control* ctrl, float* embed_out, cudaStream_t st)
+{
+    const int sms = sm_count();
+    int rc;
+    GemvFused a{};
+    a.eps = s.eps;
+    a.ldw = s.hidden;
+    // 1. rms_norm -> QKV GEMV + bias
+    a.x = x_in;
+    a.norm_w = w.attn_norm;
+    a.K = s.hidden;
+    a.w0 = w.wqkv;
+    a.rows = s.qkv_rows;
+    a.bias = w.bqkv;
+    a.y = ws.qkv;
+    if (embd) {
+        a.embd = embd;
+        a.tokens = tokens;
+        a.ctrl_ro = ctrl;
+        a.x_copy = embed_out;
+        rc = launch_gemv<1, 4, 1, 1, PRO_EMBED_NORM, EPI_BIAS>(a, sms * 8, st);
+    } else {
+        rc = launch_gemv<1, 4, 1, 1, PRO_NORM, EPI_BIAS>(a, sms * 8, st);
+    }
+    if (rc)
+        return rc;
+    const float* residual = embd ? embed_out : x_in;
+    // 2. rope + KV append + attention
+    rc = attention_fused(s, ws.qkv, kc, vc, pos, ws.attn, ws.part, ws.counters, st);
+    if (rc)
+        return rc;
+    // 3. o_proj + residual
+    GemvFused o{};
+    o.x = ws.attn;
+    o.K = s.q_dim;
+    o.w0 = w.wo;
+    o.ldw = s.q_dim;
+    o.rows = s.hidden;
+    o.res = residual;
+    o.y = ws.h1;
+    rc = launch_gemv<1, 4, 1, 2, PRO_PLAIN, EPI_RESIDUAL>(o, sms * 8, st);
+    if (rc)
+        return rc;
+    // 4. rms_norm -> gate, up -> SwiGLU
+    GemvFused g{};
+    g.x = ws.h1;
+    g.norm_w = w.ffn_norm;
+    g.eps = s.eps;
+    g.K = s.hidden;
+    g.w0 = w.wgate;
+    g.w1 = w.wup;
+    g.ldw = s.hidden;
+    g.rows = s.ffn;
+    g.y = ws.act;
+    rc = launch_gemv<1, 4, 2, 1, PRO_NORM, EPI_SWIGLU>(g, sms * 8, st);
+    if (rc)
+        return rc;
+    // 5. down_proj + residual
+    GemvFused d{};
+    d.x = ws.act;
+    d.K = s.ffn;
+    d.w0 = w.wdown;
+    d.ldw = s.ffn;
+    d.rows = s.hidden;
+    d.res = ws.h1;
+    d.y = x_out;
+    return launch_gemv<1, 4, 1, 4, PRO_PLAIN, EPI_RESIDUAL>(d, sms * 8, st);
+}
+
+// ---- model ------------------------------------------------------------------------------------------
+
+struct TensorSlot {
+    size_t offset;  // bytes into the arena
+    size_t bytes;
+    bool f16;
+    bool set;
+};
+
+}  // namespace muyo
+
+struct MuyoModel {
+    muyo::Shape s;
+    int device = 0;
+    char* arena = nullptr;  // weights
+    size_t arena_bytes = 0;
+    std::map<std::string, muyo::TensorSlot> slots;
+    bool tied_output = true;
+    void* kc = nullptr;
+    void* vc = nullptr;
+    size_t kv_layer_bytes = 0;
+    char* scratch = nullptr;  // activations, partials, control (zeroed at create)
+    muyo::LayerScratch ls{};
+    float* h = nullptr;
+    float* logits = nullptr;
+    muyo::Pair* lm_part = nullptr;
+    int32_t* lm_counter = nullptr;
+    muyo::Control* ctrl = nullptr;
+    int32_t* tokens = nullptr;
+    int lm_grid = 0;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    cudaStream_t cap_stream = nullptr;
+    int32_t* pinned = nullptr;  // host staging for control/prompt/output
+    size_t pinned_ints = 0;
+    int32_t host_pos = 0;
+    bool finalized = false;
+};
+
+namespace muyo {
+
+static const __half* W(const MuyoModel* m, const std::string& name)
+{
+    return reinterpret_cast<const __half*>(m->arena + m->slots.at(name).offset);
+}
+static const float* F(const MuyoModel* m, const std::string& name)
+{
+    return reinterpret_cast<const float*>(m->arena + m->slots.at(name).offset);
+}
+
+static LayerPtrs layer_ptrs(const MuyoModel* m, int l)
+{
+    const std::string p = "blk." + std::to_string(l) + ".";
+    LayerPtrs w;
+    w.attn_norm = F(m, p + "attn_norm.weight");
+    w.wqkv = W(m, p + "attn_qkv.weight");
+    w.bqkv = F(m, p + "attn_qkv.bias");
+    w.wo = W(m, p + "attn_output.weight");
+    w.ffn_norm = F(m, p + "ffn_norm.weight");
+    w.wgate = W(m, p + "ffn_gate.weight");
+    w.wup = W(m, p + "ffn_up.weight");
+    w.wdown = W(m, p + "ffn_down.weight");
+    return w;
+}
+
+// Records one whole decode step on stream st (5 kernels per layer + the LM head).
+static int record_step(MuyoModel* m, cudaStream_t st)
+{
+    const Shape& s = m->s;
+    const int32_t* pos = &m->ctrl->step;
+    int rc;
+    for (int l = 0; l < s.layers; ++l) {
+        const LayerPtrs w = layer_ptrs(m, l);
+        char* kc = static_cast<char*>(m->kc) + m->kv_layer_bytes * l;
+        char* vc = static_cast<char*>(m->vc) + m->kv_layer_bytes * l;
+        if (l == 0)
+            rc = layer_forward(s, w, kc, vc, pos, nullptr, m->h, m->ls, W(m, "token_embd.weight"), m->tokens,
+                               m->ctrl, m->ls.h1 /*embedding row lands in h1 first*/, st);
+        else
+            rc = layer_forward(s, w, kc, vc, pos, m->h, m->h, m->ls, nullptr, nullptr, nullptr, nullptr, st);
+        if (rc)
+            return rc;
+    }
+    GemvFused a{};
+    a.x = m->h;
+    a.norm_w = F(m, "output_norm.weight");
+    a.eps = s.eps;
+    a.K = s.hidden;
+    a.w0 = W(m, m->tied_output ? "token_embd.weight" : "output.weight");
+    a.ldw = s.hidden;
+    a.rows = s.vocab;
+    a.y = m->logits;
+    a.part = m->lm_part;
+    a.counter = m->lm_counter;
+    a.ctrl = m->ctrl;
+    a.tokens_rw = m->tokens;
+    return launch_gemv<2, 4, 1, 1, PRO_NORM, EPI_LOGITS>(a, m->lm_grid, st);
+}
+
+}  // namespace muyo
+
+using namespace muyo;
+
+// ---- extern "C": KV append and op-level attention ----------------------------------------------------
+
+template <typename KV, int HD>
+__global__ void k_kv_append(int kv_heads, int max_seq, double base, const float* __restrict__ k,
+                            const float* __restrict__ v, KV* __restrict__ kc, KV* __restrict__ vc,
+                            const int32_t* __restrict__ pos_ptr)
+{
+    const int pos = *pos_ptr;
+    const int h = blockIdx.x;
+    const size_t row = ((size_t)h * max_seq + pos) * HD;
+    for (int j = threadIdx.x; j < HD / 2; j += blockDim.x) {
+        double c, s;
+        rope_cs_f64(pos, j, HD, base, c, s);
+        float y0, y1;
+        rope_pair_f64(k[h * HD + j], k[h * HD + j + HD / 2], c, s, y0, y1);
+        kc[row + j] = kv_round<KV>(y0);
+        kc[row + j + HD / 2] = kv_round<KV>(y1);
+    }
+    for (int d = threadIdx.x; d < HD; d += blockDim.x)
+        vc[row + d] = kv_round<KV>(v[h * HD + d]);
+}
+
+static int check_attn_params(const MuyoAttentionParams* p)
+{
+    MUYO_REQUIRE(p, "attention: null parameter block");
+    MUYO_REQUIRE(p->heads > 0 && p->kv_heads > 0 && p->heads % p->kv_heads == 0,
+                 "attention: heads %u must be a positive multiple of kv_heads %u", p->heads, p->kv_heads);
+    MUYO_REQUIRE(p->heads / p->kv_heads <= (uint32_t)kAttnMaxGroup, "attention: more than %d query heads per KV head",
+                 kAttnMaxGroup);
+    if (!(p->head_dim == 16 || p->head_dim == 32 || p->head_dim == 64 || p->head_dim == 128)) {
+        set_error("attention: head_dim %u not supported (16, 32, 64, 128)", p->head_dim);
+        return MUYO_EUNSUPPORTED;
+    }
+    MUYO_REQUIRE(p->max_seq > 0, "attention: max_seq must be positive");
+    MUYO_REQUIRE(p->kv_dtype == MUYO_KV_F32 || p->kv_dtype == MUYO_KV_F16, "attention: kv_dtype %u", p->kv_dtype);
+    return MUYO_OK;
+}
+
+extern "C" size_t muyo_cuda_attention_workspace_size(const MuyoAttentionParams* p)
+{
+    if (!p || p->kv_heads == 0 || p->heads == 0)
+        return 0;
+    const size_t chunks = (p->max_seq + kAttnKeys - 1) / kAttnKeys;
+    return (size_t)p->kv_heads * chunks * (p->heads / p->kv_heads) * (p->head_dim + 2) * sizeof(float);
+}
+
+template <typename KV, int HD>
+static int launch_attention_op(const MuyoAttentionParams* q, const float* qv, const void* kc, const void* vc,
+                               const int32_t* pos, float* out, float* part, cudaStream_t st)
+{
+    AttnDev p{(int)q->heads, (int)q->kv_heads, (int)(q->heads / q->kv_heads), (int)q->max_seq, (int)q->n_keys,
+              q->scale, 0.0, (int)((q->max_seq + kAttnKeys - 1) / kAttnKeys)};
+    const size_t smem = (size_t)attn_smem_floats(HD, p.gqa) * sizeof(float);
+    auto k = k_attention<KV, HD, false, false>;
+    if (smem > 48 * 1024)
+        MUYO_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    k<<<dim3(p.kv_heads, p.max_chunks), kAttnThreads, smem, st>>>(
+        p, qv, const_cast<KV*>(static_cast<const KV*>(kc)), const_cast<KV*>(static_cast<const KV*>(vc)), pos, out, part,
+        nullptr);
+    MUYO_LAUNCH_CHECK();
+    k_attention_combine<HD><<<p.kv_heads, kAttnThreads, 0, st>>>(p, pos, part, out);
+    MUYO_LAUNCH_CHECK();
+    return MUYO_OK;
+}
+
+extern "C" int muyo_cuda_attention_decode(const MuyoAttentionParams* p, const float* q, const void* k_cache,
+                                          const void* v_cache, const int32_t* pos, float* out, void* workspace,
+                                          size_t workspace_bytes, void* stream)
+{
+    clear_error();
+    int rc = check_attn_params(p);
+    if (rc)
+        return rc;
+    MUYO_REQUIRE(q && k_cache && v_cache && out, "attention: null buffer");
+    MUYO_REQUIRE(pos || (p->n_keys > 0 && p->n_keys <= p->max_seq), "attention: n_keys %u must be in [1, max_seq %u]",
+                 p->n_keys, p->max_seq);
+    const size_t need = muyo_cuda_attention_workspace_size(p);
+    MUYO_REQUIRE(workspace && workspace_bytes >= need, "attention: workspace of %zu bytes needed, %zu given", need,
+                 workspace_bytes);
+    const cudaStream_t st = as_stream(stream);
+    float* part = static_cast<float*>(workspace);
+    if (p->kv_dtype == MUYO_KV_F16) {
+        switch (p->head_dim) {
+            case 16: return launch_attention_op<__half, 16>(p, q, k_cache, v_cache, pos, out, part, st);
+            case 32: return launch_attention_op<__half, 32>(p, q, k_cache, v_cache, pos, out, part, st);
+            case 64: return launch_attention_op<__half, 64>(p, q, k_cache, v_cache, pos, out, part, st);
+            default: return launch_attention_op<__half, 128>(p, q, k_cache, v_cache, pos, out, part, st);
+        }
+    }
+    switch (p->head_dim) {
+        case 16: return launch_attention_op<float, 16>(p, q, k_cache, v_cache, pos, out, part, st);
+        case 32: return launch_attention_op<float, 32>(p, q, k_cache, v_cache, pos, out, part, st);
+        case 64: return launch_attention_op<float, 64>(p, q, k_cache, v_cache, pos, out, part, st);
+        default: return launch_attention_op<float, 128>(p, q, k_cache, v_cache, pos, out, part, st);
+    }
+}
+
+extern "C" int muyo_cuda_kv_append(const MuyoAttentionParams* p, float rope_base, const float* k, const float* v,
+                                   void* k_cache, void* v_cache, const int32_t* pos, void* stream)
+{
+    clear_error();
+    int rc = check_attn_params(p);
+    if (rc)
+        return rc;
+    MUYO_REQUIRE(k && v && k_cache && v_cache && pos, "kv_append: null buffer");
+    MUYO_REQUIRE(rope_base > 0.0f, "kv_append: rope_base must be positive");
+    const cudaStream_t st = as_stream(stream);
+    const int kvh = (int)p->kv_heads, S = (int)p->max_seq;
+#define MUYO_KV_APPEND(KV, HD)                                                                            \
+    k_kv_append<KV, HD><<<kvh, 64, 0, st>>>(kvh, S, (double)rope_base, k, v, static_cast<KV*>(k_cache), \
+                                            static_cast<KV*>(v_cache), pos)
+    if (p->kv_dtype == MUYO_KV_F16) {
+        if (p->head_dim == 16) MUYO_KV_APPEND(__half, 16);
+        else if (p->head_dim == 32) MUYO_KV_APPEND(__half, 32);
+        else if (p->head_dim == 64) MUYO_KV_APPEND(__half, 64);
+        else MUYO_KV_APPEND(__half, 128);
+    } else {
+        if (p->head_dim == 16) MUYO_KV_APPEND(float, 16);
+        else if (p->head_dim == 32) MUYO_KV_APPEND(float, 32);
+        else if (p->head_dim == 64) MUYO_KV_APPEND(float, 64);
+        else MUYO_KV_APPEND(float, 128);
+    }
+#undef MUYO_KV_APPEND
+    MUYO_LAUNCH_CHECK();
+    return MUYO_OK;
+}
+
+// ---- extern "C": one layer -----------------------------------------------------------------------------
+
+extern "C" size_t muyo_cuda_layer_workspace_size(const MuyoQwen2Config* c)
+{
+    Shape s{};
+    if (make_shape(c, s, false) != MUYO_OK)
+        return 0;
+    return layer_scratch_bytes(s);
+}
+
+extern "C" int muyo_cuda_layer_step(const MuyoQwen2Config* c, const MuyoLayerWeights* w, void* k_cache, void* v_cache,
+                                    const int32_t* pos, const float* x_in, float* x_out, void* workspace,
+                                    size_t workspace_bytes, void* stream)
+{
+    clear_error();
+    Shape s{};
+    int rc = make_shape(c, s, false);
+    if (rc)
+        return rc;
+    MUYO_REQUIRE(w && w->attn_norm && w->wqkv && w->bqkv && w->wo && w->ffn_norm && w->wgate && w->wup && w->wdown,
+                 "layer_step: null weight pointer");
+    MUYO_REQUIRE(k_cache && v_cache && pos && x_in && x_out, "layer_step: null buffer");
+    MUYO_REQUIRE(x_in != x_out, "layer_step: x_in and x_out must not alias");
+    MUYO_REQUIRE(aligned16(w->wqkv) && aligned16(w->wo) && aligned16(w->wgate) && aligned16(w->wup) &&
+                     aligned16(w->wdown),
+                 "layer_step: weight matrices must be 16-byte aligned");
+    const size_t need = layer_scratch_bytes(s);
+    MUYO_REQUIRE(workspace && workspace_bytes >= need, "layer_step: workspace of %zu bytes needed, %zu given", need,
+                 workspace_bytes);
+    MUYO_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255u) == 0, "layer_step: workspace must be 256-byte aligned");
+    LayerPtrs lp{w->attn_norm,
+                 static_cast<const __half*>(w->wqkv),
+                 w->bqkv,
+                 static_cast<const __half*>(w->wo),
+                 w->ffn_norm,
+                 static_cast<const __half*>(w->wgate),
+                 static_cast<const __half*>(w->wup),
+                 static_cast<const __half*>(w->wdown)};
+    return layer_forward(s, lp, k_cache, v_cache, pos, x_in, x_out, carve_layer_scratch(s, workspace), nullptr, nullptr,
+                         nullptr, nullptr, as_stream(stream));
+}
+
+// ---- extern "C": model ---------------------------------------------------------------------------------
+
+static void free_model(MuyoModel* m)
+{
+    if (!m)
+        return;
+    if (m->exec)
+        cudaGraphExecDestroy(m->exec);
+    if (m->graph)
+        cudaGraphDestroy(m->graph);
+    if (m->cap_stream)
+        cudaStreamDestroy(m->cap_stream);
+    cudaFree(m->arena);
+    cudaFree(m->kc);
+    cudaFree(m->vc);
+    cudaFree(m->scratch);
+    if (m->pinned)
+        cudaFreeHost(m->pinned);
+    delete m;
+}
+
+extern "C" int muyo_model_create(const MuyoQwen2Config* c, int device, MuyoModel** out)
+{
+    clear_error();
+    MUYO_REQUIRE(out, "model_create: out is null");
+    *out = nullptr;
+    Shape s{};
+    int rc = make_shape(c, s, true);
+    if (rc)
+        return rc;
+    MUYO_REQUIRE(s.layers > 0, "model_create: layers must be positive");
+    MUYO_CUDA_TRY(cudaSetDevice(device));
+    MuyoModel* m = new (std::nothrow) MuyoModel();
+    if (!m) {
+        set_error("model_create: host allocation failed");
+        return MUYO_ENOMEM;
+    }
+    m->s = s;
+    m->device = device;
+    // Weight arena layout (256-byte aligned slots). QKV weights and biases are stacked by rows so one
+    // GEMV produces q, k and v; the GGUF tensors attn_{q,k,v}.{weight,bias} land in row ranges of it.
+    size_t off = 0;
+    auto slot = [&](const std::string& name, size_t elems, bool f16) {
+        m->slots[name] = TensorSlot{off, elems * (f16 ? 2 : 4), f16, false};
+        off += align256(elems * (f16 ? 2 : 4));
+    };
+    const size_t H = s.hidden, Fd = s.ffn, V = s.vocab;
+    slot("token_embd.weight", V * H, true);
+    slot("output.weight", 0, true);  // tied unless set
+    slot("output_norm.weight", H, false);
+    for (int l = 0; l < s.layers; ++l) {
+        const std::string p = "blk." + std::to_string(l) + ".";
+        slot(p + "attn_norm.weight", H, false);
+        slot(p + "attn_qkv.weight", (size_t)s.qkv_rows * H, true);
+        slot(p + "attn_qkv.bias", s.qkv_rows, false);
+        slot(p + "attn_output.weight", H * s.q_dim, true);
+        slot(p + "ffn_norm.weight", H, false);
+        slot(p + "ffn_gate.weight", Fd * H, true);
+        slot(p + "ffn_up.weight", Fd * H, true);
+        slot(p + "ffn_down.weight", H * Fd, true);
+    }
+    m->arena_bytes = off;
+    cudaError_t e = cudaMalloc(&m->arena, off);
+    m->kv_layer_bytes = align256((size_t)s.kv_heads * s.max_seq * s.head_dim * (s.kv_f16 ? 2 : 4));
+    if (e == cudaSuccess)
+        e = cudaMalloc(&m->kc, m->kv_layer_bytes * s.layers);
+    if (e == cudaSuccess)
+        e = cudaMalloc(&m->vc, m->kv_layer_bytes * s.layers);
+    m->lm_grid = sm_count() * 8;
+    const size_t scratch_bytes = layer_scratch_bytes(s) + align256(sizeof(float) * H) + align256(sizeof(float) * V) +
+                                 align256(sizeof(Pair) * m->lm_grid) + align256(sizeof(int32_t)) +
+                                 align256(sizeof(Control)) + align256(sizeof(int32_t) * s.max_seq);
+    if (e == cudaSuccess)
+        e = cudaMalloc(&m->scratch, scratch_bytes);
+    if (e == cudaSuccess)
+        e = cudaMemset(m->scratch, 0, scratch_bytes);
+    if (e == cudaSuccess)
+        e = cudaMemset(m->kc, 0, m->kv_layer_bytes * s.layers);
+    if (e == cudaSuccess)
+        e = cudaMemset(m->vc, 0, m->kv_layer_bytes * s.layers);
+    m->pinned_ints = (size_t)s.max_seq + 16;
+    if (e == cudaSuccess)
+        e = cudaMallocHost(&m->pinned, m->pinned_ints * sizeof(int32_t));
+    if (e == cudaSuccess)
+        e = cudaStreamCreateWithFlags(&m->cap_stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        set_error("model_create: %s", cudaGetErrorString(e));
+        free_model(m);
+        return e == cudaErrorMemoryAllocation ? MUYO_ENOMEM : MUYO_ECUDA;
+    }
+    char* p = m->scratch;
+    m->ls = carve_layer_scratch(s, p);
+    p += layer_scratch_bytes(s);
+    m->h = reinterpret_cast<float*>(p);
+    p += align256(sizeof(float) * H);
+    m->logits = reinterpret_cast<float*>(p);
+    p += align256(sizeof(float) * V);
+    m->lm_part = reinterpret_cast<Pair*>(p);
+    p += align256(sizeof(Pair) * m->lm_grid);
+    m->lm_counter = reinterpret_cast<int32_t*>(p);
+    p += align256(sizeof(int32_t));
+    m->ctrl = reinterpret_cast<Control*>(p);
+    p += align256(sizeof(Control));
+    m->tokens = reinterpret_cast<int32_t*>(p);
+    *out = m;
+    return MUYO_OK;
+}
+
+static bool split_qkv(const std::string& name, std::string& base, int& part, bool& bias)
+{
+    // blk.N.attn_{q,k,v}.{weight,bias} -> blk.N.attn_qkv.{weight,bias}, part 0/1/2
+    const size_t a = name.find(".attn_");
+    if (a == std::string::npos || name.size() < a + 8)
+        return false;
+    const char which = name[a + 6];
+    if (name[a + 7] != '.' || (which != 'q' && which != 'k' && which != 'v'))
+        return false;
+    const std::string rest = name.substr(a + 8);
+    if (rest != "weight" && rest != "bias")
+        return false;
+    bias = rest == "bias";
+    base = name.substr(0, a) + ".attn_qkv." + rest;
+    part = which == 'q' ? 0 : which == 'k' ? 1 : 2;
+    return true;
+}
+
+extern "C" int muyo_model_set_tensor(MuyoModel* m, const char* name, const void* host, size_t bytes)
+{
+    clear_error();
+    MUYO_REQUIRE(m && name && host, "set_tensor: null argument");
+    MUYO_CUDA_TRY(cudaSetDevice(m->device));
+    const Shape& s = m->s;
+    std::string n(name), base;
+    int part = 0;
+    bool bias = false;
+    if (split_qkv(n, base, part, bias)) {
+        auto it = m->slots.find(base);
+        MUYO_REQUIRE(it != m->slots.end(), "set_tensor: unknown tensor %s", name);
+        const size_t per_row = bias ? 4 : (size_t)s.hidden * 2;
+        const size_t row0 = part == 0 ? 0 : part == 1 ? s.q_dim : (size_t)s.q_dim + s.kv_dim;
+        const size_t rows = part == 0 ? s.q_dim : s.kv_dim;
+        MUYO_REQUIRE(bytes == rows * per_row, "set_tensor: %s has %zu bytes, expected %zu", name, bytes, rows * per_row);
+        MUYO_CUDA_TRY(cudaMemcpy(m->arena + it->second.offset + row0 * per_row, host, bytes, cudaMemcpyHostToDevice));
+        // A stacked slot counts as set once all three parts arrived.
+        m->slots[base + "#" + std::to_string(part)] = TensorSlot{0, 0, false, true};
+        return MUYO_OK;
+    }
+    if (n == "output.weight") {
+        const size_t need = (size_t)s.vocab * s.hidden * 2;
+        MUYO_REQUIRE(bytes == need, "set_tensor: output.weight has %zu bytes, expected %zu", bytes, need);
+        // Untie: give the LM head its own copy at the end of a fresh arena slot.
+        char* extra = nullptr;
+        MUYO_CUDA_TRY(cudaMalloc(&extra, m->arena_bytes + align256(need)));
+        MUYO_CUDA_TRY(cudaMemcpy(extra, m->arena, m->arena_bytes, cudaMemcpyDeviceToDevice));
+        cudaFree(m->arena);
+        m->arena = extra;
+        m->slots["output.weight"] = TensorSlot{m->arena_bytes, need, true, true};
+        m->arena_bytes += align256(need);
+        MUYO_CUDA_TRY(cudaMemcpy(m->arena + m->slots["output.weight"].offset, host, bytes, cudaMemcpyHostToDevice));
+        m->tied_output = false;
+        m->finalized = false;
+        return MUYO_OK;
+    }
+    auto it = m->slots.find(n);
+    MUYO_REQUIRE(it != m->slots.end() && n.find("attn_qkv") == std::string::npos, "set_tensor: unknown tensor %s",
+                 name);
+    MUYO_REQUIRE(bytes == it->second.bytes, "set_tensor: %s has %zu bytes, expected %zu", name, bytes,
+                 it->second.bytes);
+    MUYO_CUDA_TRY(cudaMemcpy(m->arena + it->second.offset, host, bytes, cudaMemcpyHostToDevice));
+    it->second.set = true;
+    return MUYO_OK;
+}
+
+extern "C" int muyo_model_finalize(MuyoModel* m, void* stream)
+{
+    clear_error();
+    MUYO_REQUIRE(m, "finalize: null model");
+    MUYO_CUDA_TRY(cudaSetDevice(m->device));
+    for (const auto& kv : m->slots) {
+        const std::string& n = kv.first;
+        if (n.find('#') != std::string::npos || n == "output.weight")
+            continue;
+        if (n.find("attn_qkv") != std::string::npos) {
+            for (int part = 0; part < 3; ++part)
+                MUYO_REQUIRE(m->slots.count(n + "#" + std::to_string(part)), "finalize: %s part %d was never set",
+                             n.c_str(), part);
+            continue;
+        }
+        MUYO_REQUIRE(kv.second.set, "finalize: tensor %s was never set", n.c_str());
+    }
+    (void)stream;
+    if (m->exec) {
+        cudaGraphExecDestroy(m->exec);
+        m->exec = nullptr;
+    }
+    if (m->graph) {
+        cudaGraphDestroy(m->graph);
+        m->graph = nullptr;
+    }
+    MUYO_CUDA_TRY(cudaStreamBeginCapture(m->cap_stream, cudaStreamCaptureModeThreadLocal));
+    int rc = record_step(m, m->cap_stream);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(m->cap_stream, &g);
+    if (rc != MUYO_OK) {
+        if (g)
+            cudaGraphDestroy(g);
+        return rc;
+    }
+    MUYO_CUDA_TRY(e);
+    m->graph = g;
+    MUYO_CUDA_TRY(cudaGraphInstantiate(&m->exec, g, 0));
+    m->finalized = true;
+    return MUYO_OK;
+}
+
+extern "C" int muyo_model_reset(MuyoModel* m, void* stream)
+{
+    clear_error();
+    MUYO_REQUIRE(m, "reset: null model");
+    MUYO_CUDA_TRY(cudaSetDevice(m->device));
+    const cudaStream_t st = as_stream(stream);
+    MUYO_CUDA_TRY(cudaMemsetAsync(m->kc, 0, m->kv_layer_bytes * m->s.layers, st));
+    MUYO_CUDA_TRY(cudaMemsetAsync(m->vc, 0, m->kv_layer_bytes * m->s.layers, st));
+    MUYO_CUDA_TRY(cudaMemsetAsync(m->ctrl, 0, sizeof(Control), st));
+    MUYO_CUDA_TRY(cudaStreamSynchronize(st));
+    m->host_pos = 0;
+    return MUYO_OK;
+}
+
+// Sets the control block for `n_steps` steps starting at the current position, with prompt ids
+// forced up to `prompt_end`, and replays the step graph n_steps times.
+static int run_steps(MuyoModel* m, int prompt_end, int total, int n_steps, cudaStream_t st)
+{
+    Control c{m->host_pos, prompt_end, total, 0};
+    int32_t* staging = m->pinned + m->pinned_ints - 8;
+    std::memcpy(staging, &c, sizeof(c));
+    MUYO_CUDA_TRY(cudaMemcpyAsync(m->ctrl, staging, sizeof(Control), cudaMemcpyHostToDevice, st));
+    for (int i = 0; i < n_steps; ++i)
+        MUYO_CUDA_TRY(cudaGraphLaunch(m->exec, st));
+    m->host_pos += n_steps;
+    return MUYO_OK;
+}
+
+static int check_generate(MuyoModel* m, int n_prompt, int n_predict)
+{
+    MUYO_REQUIRE(m, "generate: null model");
+    if (!m->finalized) {
+        set_error("generate: model not finalized");
+        return MUYO_ESTATE;
+    }
+    MUYO_REQUIRE(n_prompt >= 1 && n_predict >= 0, "generate: need n_prompt >= 1 and n_predict >= 0");
+    if ((long long)m->host_pos + n_prompt + n_predict > m->s.max_seq) {
+        set_error("generate: %d cached + %d prompt + %d predicted exceed the %d-position cache", m->host_pos, n_prompt,
+                  n_predict, m->s.max_seq);
+        return MUYO_ESTATE;
+    }
+    return MUYO_OK;
+}
+
+extern "C" int muyo_model_generate_device(MuyoModel* m, const int32_t* prompt_dev, int n_prompt, int n_predict,
+                                          int32_t* out_tokens_dev, void* stream)
+{
+    clear_error();
+    int rc = check_generate(m, n_prompt, n_predict);
+    if (rc)
+        return rc;
+    MUYO_REQUIRE(prompt_dev && (n_predict == 0 || out_tokens_dev), "generate: null buffer");
+    MUYO_CUDA_TRY(cudaSetDevice(m->device));
+    const cudaStream_t st = as_stream(stream);
+    const int p0 = m->host_pos;
+    MUYO_CUDA_TRY(cudaMemcpyAsync(m->tokens + p0, prompt_dev, sizeof(int32_t) * n_prompt, cudaMemcpyDeviceToDevice, st));
+    const int total = p0 + n_prompt + n_predict;
+    rc = run_steps(m, p0 + n_prompt, total, n_prompt + n_predict, st);
+    if (rc)
+        return rc;
+    if (n_predict > 0)
+        MUYO_CUDA_TRY(cudaMemcpyAsync(out_tokens_dev, m->tokens + p0 + n_prompt, sizeof(int32_t) * n_predict,
+                                      cudaMemcpyDeviceToDevice, st));
+    return MUYO_OK;
+}
+
+extern "C" int muyo_model_generate(MuyoModel* m, const int32_t* prompt, int n_prompt, int n_predict,
+                                   int32_t* out_tokens, void* stream)
+{
+    clear_error();
+    int rc = check_generate(m, n_prompt, n_predict);
+    if (rc)
+        return rc;
+    MUYO_REQUIRE(prompt && (n_predict == 0 || out_tokens), "generate: null buffer");
+    MUYO_CUDA_TRY(cudaSetDevice(m->device));
+    const cudaStream_t st = as_stream(stream);
+    const int p0 = m->host_pos;
+    std::memcpy(m->pinned, prompt, sizeof(int32_t) * n_prompt);
+    MUYO_CUDA_TRY(cudaMemcpyAsync(m->tokens + p0, m->pinned, sizeof(int32_t) * n_prompt, cudaMemcpyHostToDevice, st));
+    const int total = p0 + n_prompt + n_predict;
+    rc = run_steps(m, p0 + n_prompt, total, n_prompt + n_predict, st);
+    if (rc)
+        return rc;
+    if (n_predict > 0) {
+        MUYO_CUDA_TRY(cudaMemcpyAsync(m->pinned, m->tokens + p0 + n_prompt, sizeof(int32_t) * n_predict,
+                                      cudaMemcpyDeviceToHost, st));
+    }
+    MUYO_CUDA_TRY(cudaStreamSynchronize(st));
+    if (n_predict > 0)
+        std::memcpy(out_tokens, m->pinned, sizeof(int32_t) * n_predict);
+    return MUYO_OK;
+}
+
+extern "C" int muyo_model_step(MuyoModel* m, int32_t token, float* logits, int32_t* next_token, void* stream)
+{
+    clear_error();
+    int rc = check_generate(m, 1, 0);
+    if (rc)
+        return rc;
+    MUYO_REQUIRE(token >= 0 && token < m->s.vocab, "step: token %d outside [0, %d)", token, m->s.vocab);
+    MUYO_CUDA_TRY(cudaSetDevice(m->device));
+    const cudaStream_t st = as_stream(stream);
+    const int p0 = m->host_pos;
+    m->pinned[0] = token;
+    MUYO_CUDA_TRY(cudaMemcpyAsync(m->tokens + p0, m->pinned, sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    rc = run_steps(m, p0 + 1, p0 + 1, 1, st);
+    if (rc)
+        return rc;
+    if (logits)
+        MUYO_CUDA_TRY(cudaMemcpyAsync(logits, m->logits, sizeof(float) * m->s.vocab, cudaMemcpyDefault, st));
+    MUYO_CUDA_TRY(cudaMemcpyAsync(m->pinned + 1, &m->ctrl->greedy, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+    MUYO_CUDA_TRY(cudaStreamSynchronize(st));
+    if (next_token)
+        *next_token = m->pinned[1];
+    return MUYO_OK;
+}
+
+extern "C" int muyo_model_position(const MuyoModel* m, int32_t* pos)
+{
+    clear_error();
+    MUYO_REQUIRE(m && pos, "position: null argument");
+    *pos = m->host_pos;
+    return MUYO_OK;
+}
+
+extern "C" int muyo_model_buffer(MuyoModel* m, const char* name, void** ptr, size_t* bytes)
+{
+    clear_error();
+    MUYO_REQUIRE(m && name && ptr, "buffer: null argument");
+    const std::string n(name);
+    size_t b = 0;
+    if (n == "logits") {
+        *ptr = m->logits;
+        b = sizeof(float) * m->s.vocab;
+    } else if (n == "hidden") {
+        *ptr = m->h;
+        b = sizeof(float) * m->s.hidden;
+    } else if (n == "k_cache") {
+        *ptr = m->kc;
+        b = m->kv_layer_bytes * m->s.layers;
+    } else if (n == "v_cache") {
+        *ptr = m->vc;
+        b = m->kv_layer_bytes * m->s.layers;
+    } else if (n == "tokens") {
+        *ptr = m->tokens;
+        b = sizeof(int32_t) * m->s.max_seq;
+    } else {
+        MUYO_REQUIRE(false, "buffer: unknown buffer %s", name);
+    }
+    if (bytes)
+        *bytes = b;
+    return MUYO_OK;
+}
+
+extern "C" int muyo_model_destroy(MuyoModel* m)
+{
+    clear_error();
+    if (m) {
+        cudaSetDevice(m->device);
+        cudaDeviceSynchronize();
+        free_model(m);
+    }
+    return MUYO_OK;
+}

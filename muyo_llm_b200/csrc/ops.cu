@@ -1,0 +1,897 @@
+// Op-level kernels behind the reference's per-op node contracts (src/LlamaContracts.h), one
+// extern "C" entry point each. These back the reference's op checks (src/MatVec.cpp,
+// src/RmsNorm.cpp, src/Rope.cpp, ...) and its node-per-op graph; the fused decode path lives in
+// decode.cu.
+#include <climits>
+#include <cmath>
+
+#include "common.cuh"
+#include "gemv.cuh"
+
+namespace muyo {
+
+constexpr int kThreads = 256;
+constexpr int kMaxStagedK = 56 * 1024;  // floats of x staged in shared memory (224 KB)
+
+// ---- GEMV ------------------------------------------------------------------------------------------
+
+struct MatVecDev {
+    int ncols, rows, stride_a, stride_b, stride_d;
+    long long batch_stride_a, batch_stride_b, batch_stride_d;
+    int ne02, ne12, bc2, bc3;
+    int k8;  // vector chunks of 8 (F16) or 4 (F32) columns; 0 selects the scalar path
+    unsigned flags;
+};
+
+__device__ __forceinline__ long long batch_a_index(const MatVecDev& p, int b)
+{
+    const int i13 = b / p.ne12, i12 = b % p.ne12;
+    return (long long)(i13 / p.bc3) * p.ne02 + i12 / p.bc2;
+}
+
+__device__ __forceinline__ float fuse_bias(const MatVecDev& p, float v, const float* f0, const float* f1, long long di)
+{
+    if (p.flags & MUYO_MATVEC_BIAS0)
+        v += f0[di];
+    if (p.flags & MUYO_MATVEC_BIAS1)
+        v += f1[di];
+    return v;
+}
+
+template <int ROWS, int U>
+__global__ void __launch_bounds__(kThreads) k_mat_vec_f16(MatVecDev p, const __half* __restrict__ A,
+                                                          const float* __restrict__ B, float* __restrict__ D,
+                                                          const float* __restrict__ f0, const float* __restrict__ f1)
+{
+    extern __shared__ float xs[];
+    const int b = blockIdx.y;
+    const __half* Ab = A + batch_a_index(p, b) * p.batch_stride_a;
+    const float* Bb = B + (long long)b * p.batch_stride_b;
+    for (int k = threadIdx.x; k < p.ncols; k += blockDim.x)
+        xs[xs_index(k, p.k8)] = Bb[k];
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    GemvArgs<ROWS, U, 1> ga{{Ab}, (size_t)p.stride_a};
+    for (int row0 = (blockIdx.x * nw + warp) * ROWS; row0 < p.rows; row0 += gridDim.x * nw * ROWS) {
+        const int nvalid = min(ROWS, p.rows - row0);
+        float acc[1][ROWS];
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r)
+            acc[0][r] = 0.0f;
+        warp_gemv_f16<ROWS, U, 1>(ga, row0, nvalid, xs, p.k8, lane, acc);
+        warp_gemv_f16_tail<ROWS, 1>(ga.w, ga.ldw, row0, nvalid, xs, p.k8, p.ncols, lane, acc);
+        warp_reduce_acc<ROWS, 1>(acc);
+        if (lane == 0) {
+#pragma unroll
+            for (int r = 0; r < ROWS; ++r)
+                if (r < nvalid) {
+                    const long long di = (long long)b * p.batch_stride_d + row0 + r;
+                    D[di] = fuse_bias(p, acc[0][r], f0, f1, di);
+                }
+        }
+    }
+}
+
+// F32 weights: lane l takes the 4-column chunks l, l+32, ... (16-byte loads); x staged plainly.
+template <int ROWS, int U>
+__global__ void __launch_bounds__(kThreads) k_mat_vec_f32(MatVecDev p, const float* __restrict__ A,
+                                                          const float* __restrict__ B, float* __restrict__ D,
+                                                          const float* __restrict__ f0, const float* __restrict__ f1)
+{
+    extern __shared__ float xs[];
+    const int b = blockIdx.y;
+    const float* Ab = A + batch_a_index(p, b) * p.batch_stride_a;
+    const float* Bb = B + (long long)b * p.batch_stride_b;
+    for (int k = threadIdx.x; k < p.ncols; k += blockDim.x)
+        xs[k] = Bb[k];
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int K4 = p.k8;
+    for (int row0 = (blockIdx.x * nw + warp) * ROWS; row0 < p.rows; row0 += gridDim.x * nw * ROWS) {
+        const int nvalid = min(ROWS, p.rows - row0);
+        float acc[ROWS];
+        const float* rowp[ROWS];
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) {
+            acc[r] = 0.0f;
+            rowp[r] = Ab + (size_t)(row0 + (r < nvalid ? r : 0)) * p.stride_a;
+        }
+        for (int base = 0; base < K4; base += WARP * U) {
+            float4 wv[ROWS][U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int c = base + lane + WARP * u;
+#pragma unroll
+                for (int r = 0; r < ROWS; ++r)
+                    wv[r][u] = c < K4 ? ld_stream16f(rowp[r] + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int c = base + lane + WARP * u;
+                if (c < K4) {
+                    const float4 x = reinterpret_cast<const float4*>(xs)[c];
+#pragma unroll
+                    for (int r = 0; r < ROWS; ++r) {
+                        acc[r] = fmaf(wv[r][u].x, x.x, acc[r]);
+                        acc[r] = fmaf(wv[r][u].y, x.y, acc[r]);
+                        acc[r] = fmaf(wv[r][u].z, x.z, acc[r]);
+                        acc[r] = fmaf(wv[r][u].w, x.w, acc[r]);
+                    }
+                }
+            }
+        }
+        for (int k = 4 * K4 + lane; k < p.ncols; k += WARP) {
+#pragma unroll
+            for (int r = 0; r < ROWS; ++r)
+                acc[r] = fmaf(rowp[r][k], xs[k], acc[r]);
+        }
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r)
+            acc[r] = warp_sum(acc[r]);
+        if (lane == 0) {
+#pragma unroll
+            for (int r = 0; r < ROWS; ++r)
+                if (r < nvalid) {
+                    const long long di = (long long)b * p.batch_stride_d + row0 + r;
+                    D[di] = fuse_bias(p, acc[r], f0, f1, di);
+                }
+        }
+    }
+}
+
+template <typename Kernel>
+static cudaError_t set_smem(Kernel k, size_t bytes)
+{
+    if (bytes <= 48 * 1024)
+        return cudaSuccess;
+    return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+static int mat_vec_prepare(const MuyoMatVecParams* p, const void* a, const float* b, float* d, const float* f0,
+                           const float* f1, size_t esize, MatVecDev& q)
+{
+    MUYO_REQUIRE(p && a && b && d, "mat_vec: null parameter block or buffer");
+    MUYO_REQUIRE(p->ncols > 0 && p->rows > 0, "mat_vec: ncols and rows must be positive");
+    if (p->fusion_flags & (MUYO_MATVEC_SCALE0 | MUYO_MATVEC_SCALE1)) {
+        set_error("mat_vec: SCALE0/SCALE1 fusion is not implemented");
+        return MUYO_EUNSUPPORTED;
+    }
+    MUYO_REQUIRE((p->fusion_flags & ~0xFu) == 0, "mat_vec: unknown fusion flag bits 0x%x", p->fusion_flags);
+    MUYO_REQUIRE(!(p->fusion_flags & MUYO_MATVEC_BIAS0) || f0, "mat_vec: BIAS0 set but fuse0 is null");
+    MUYO_REQUIRE(!(p->fusion_flags & MUYO_MATVEC_BIAS1) || f1, "mat_vec: BIAS1 set but fuse1 is null");
+    MUYO_REQUIRE(p->ncols <= (uint32_t)kMaxStagedK, "mat_vec: ncols %u exceeds %d", p->ncols, kMaxStagedK);
+    q.ncols = (int)p->ncols;
+    q.rows = (int)p->rows;
+    q.stride_a = (int)(p->stride_a ? p->stride_a : p->ncols);
+    q.stride_b = (int)(p->stride_b ? p->stride_b : p->ncols);
+    q.stride_d = (int)(p->stride_d ? p->stride_d : p->rows);
+    MUYO_REQUIRE((uint32_t)q.stride_a >= p->ncols, "mat_vec: stride_a %d < ncols %u", q.stride_a, p->ncols);
+    MUYO_REQUIRE(p->rows <= (uint32_t)q.stride_d, "mat_vec: rows %u exceed stride_d %d", p->rows, q.stride_d);
+    q.batch_stride_a = p->batch_stride_a;
+    q.batch_stride_b = p->batch_stride_b;
+    q.batch_stride_d = p->batch_stride_d;
+    q.ne02 = p->ne02 ? (int)p->ne02 : 1;
+    q.ne12 = p->ne12 ? (int)p->ne12 : 1;
+    q.bc2 = p->broadcast2 ? (int)p->broadcast2 : 1;
+    q.bc3 = p->broadcast3 ? (int)p->broadcast3 : 1;
+    q.flags = p->fusion_flags;
+    const uint32_t batches = p->batches ? p->batches : 1;
+    MUYO_REQUIRE(batches <= 65535u, "mat_vec: batches %u exceed 65535", batches);
+    MUYO_REQUIRE(batches == 1 || p->batch_stride_d >= p->rows, "mat_vec: batch_stride_d < rows would overlap batches");
+    (void)f0;
+    (void)f1;
+    const int per = esize == 2 ? 8 : 4;  // elements per 16-byte chunk
+    const bool vec = aligned16(a) && (q.stride_a % per) == 0 && (q.batch_stride_a % per) == 0;
+    q.k8 = vec ? q.ncols / per : 0;
+    return MUYO_OK;
+}
+
+template <int ROWS>
+static int launch_mat_vec(bool f16, const MatVecDev& q, int batches, const void* a, const float* b, float* d,
+                          const float* f0, const float* f1, cudaStream_t s)
+{
+    const int tiles = (q.rows + 8 * ROWS - 1) / (8 * ROWS);
+    int gx = tiles < sm_count() * 8 ? tiles : sm_count() * 8;
+    if (batches > 1 && gx * batches > sm_count() * 16)
+        gx = (sm_count() * 16 + batches - 1) / batches > 0 ? ((sm_count() * 16 + batches - 1) / batches) : 1;
+    if (gx > tiles)
+        gx = tiles;
+    if (gx < 1)
+        gx = 1;
+    const size_t smem = (size_t)q.ncols * sizeof(float);
+    dim3 grid(gx, batches);
+    if (f16) {
+        auto k = k_mat_vec_f16<ROWS, 4>;
+        MUYO_CUDA_TRY(set_smem(k, smem));
+        k<<<grid, kThreads, smem, s>>>(q, static_cast<const __half*>(a), b, d, f0, f1);
+    } else {
+        auto k = k_mat_vec_f32<ROWS, 4>;
+        MUYO_CUDA_TRY(set_smem(k, smem));
+        k<<<grid, kThreads, smem, s>>>(q, static_cast<const float*>(a), b, d, f0, f1);
+    }
+    MUYO_LAUNCH_CHECK();
+    return MUYO_OK;
+}
+
+static int mat_vec_any(bool f16, const MuyoMatVecParams* p, const void* a, const float* b, float* d, const float* f0,
+                       const float* f1, void* stream)
+{
+    MatVecDev q{};
+    int rc = mat_vec_prepare(p, a, b, d, f0, f1, f16 ? 2 : 4, q);
+    if (rc != MUYO_OK)
+        return rc;
+    const int batches = p->batches ? (int)p->batches : 1;
+    const bool two_rows = (q.rows + 15) / 16 >= 2 * sm_count();
+    return two_rows ? launch_mat_vec<2>(f16, q, batches, a, b, d, f0, f1, as_stream(stream))
+                    : launch_mat_vec<1>(f16, q, batches, a, b, d, f0, f1, as_stream(stream));
+}
+
+// ---- binary head ops -----------------------------------------------------------------------------
+
+struct Dims4 {
+    int ne[4];
+    long long nb[4];
+};
+
+static Dims4 dims(uint32_t n0, uint32_t n1, uint32_t n2, uint32_t n3, uint32_t s0, uint32_t s1, uint32_t s2,
+                  uint32_t s3)
+{
+    Dims4 d;
+    d.ne[0] = n0 ? (int)n0 : 1;
+    d.ne[1] = n1 ? (int)n1 : 1;
+    d.ne[2] = n2 ? (int)n2 : 1;
+    d.ne[3] = n3 ? (int)n3 : 1;
+    d.nb[0] = s0;
+    d.nb[1] = s1;
+    d.nb[2] = s2;
+    d.nb[3] = s3;
+    return d;
+}
+
+__global__ void k_add_contig(const float4* __restrict__ a, const float4* __restrict__ b, float4* __restrict__ d,
+                             long long n4)
+{
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+        const float4 x = a[i], y = b[i];
+        d[i] = make_float4(x.x + y.x, x.y + y.y, x.z + y.z, x.w + y.w);
+    }
+}
+
+__global__ void k_add_general(Dims4 A, Dims4 B, Dims4 D, const float* __restrict__ a, const float* __restrict__ b,
+                              float* __restrict__ d, long long n)
+{
+    for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < n;
+         idx += (long long)gridDim.x * blockDim.x) {
+        long long t = idx;
+        int i[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            i[k] = (int)(t % D.ne[k]);
+            t /= D.ne[k];
+        }
+        long long ai = 0, bi = 0, di = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            ai += i[k] * A.nb[k];
+            bi += (i[k] % B.ne[k]) * B.nb[k];
+            di += i[k] * D.nb[k];
+        }
+        d[di] = a[ai] + b[bi];
+    }
+}
+
+static bool contiguous(const Dims4& x)
+{
+    return x.nb[0] == 1 && x.nb[1] == x.ne[0] && x.nb[2] == (long long)x.ne[0] * x.ne[1] &&
+           x.nb[3] == (long long)x.ne[0] * x.ne[1] * x.ne[2];
+}
+
+static long long count(const Dims4& x) { return (long long)x.ne[0] * x.ne[1] * x.ne[2] * x.ne[3]; }
+
+static int grid_for(long long n, int per_thread = 1)
+{
+    long long blocks = (n / per_thread + kThreads - 1) / kThreads;
+    const long long cap = (long long)sm_count() * 16;
+    if (blocks > cap)
+        blocks = cap;
+    return blocks < 1 ? 1 : (int)blocks;
+}
+
+// One CTA per row: sum of squares in F32 (per-thread partials, then a shuffle tree), scale =
+// 1/sqrt(mean + eps) in IEEE arithmetic, D = A * scale * W[col % ne10] (rms_norm.comp:87-122,
+// src/RmsNorm.cpp:194-205).
+__global__ void __launch_bounds__(kThreads) k_rms_norm(Dims4 A, Dims4 W, Dims4 D, const float* __restrict__ a,
+                                                       const float* __restrict__ w, float* __restrict__ d, float eps)
+{
+    __shared__ float red[32];
+    const int row = blockIdx.x;
+    const int i1 = row % A.ne[1], i2 = (row / A.ne[1]) % A.ne[2], i3 = row / (A.ne[1] * A.ne[2]);
+    const float* ar = a + i1 * A.nb[1] + i2 * A.nb[2] + i3 * A.nb[3];
+    float* dr = d + i1 * D.nb[1] + i2 * D.nb[2] + i3 * D.nb[3];
+    const int n = A.ne[0];
+    float ss = 0.0f;
+    for (int c = threadIdx.x; c < n; c += blockDim.x) {
+        const float v = ar[c * A.nb[0]];
+        ss = fmaf(v, v, ss);
+    }
+    ss = block_sum(ss, red);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(ss, (float)n) + eps));
+    for (int c = threadIdx.x; c < n; c += blockDim.x)
+        dr[c * D.nb[0]] = ar[c * A.nb[0]] * scale * w[(c % W.ne[0]) * W.nb[0]];
+}
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<float>(float v)
+{
+    return v;
+}
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half v)
+{
+    return __half2float(v);
+}
+
+// get_rows.comp:8-42: D[i10, i11, i12][i00] = A[idx, i11, i12][i00]. An id outside [0, ne01)
+// writes zeros (the reference would read out of bounds).
+template <typename T>
+__global__ void k_get_rows(Dims4 A, Dims4 B, Dims4 D, const T* __restrict__ a, const int32_t* __restrict__ b,
+                           float* __restrict__ d)
+{
+    const int i10 = blockIdx.y;
+    const int z = blockIdx.z, i11 = z % B.ne[1], i12 = z / B.ne[1];
+    const int idx = b[i10 * B.nb[0] + i11 * B.nb[1] + i12 * B.nb[2]];
+    const bool ok = idx >= 0 && idx < A.ne[1];
+    const T* ar = a + (long long)idx * A.nb[1] + i11 * A.nb[2] + i12 * A.nb[3];
+    float* dr = d + i10 * D.nb[1] + i11 * D.nb[2] + i12 * D.nb[3];
+    for (int i00 = blockIdx.x * blockDim.x + threadIdx.x; i00 < A.ne[0]; i00 += gridDim.x * blockDim.x)
+        dr[i00 * D.nb[0]] = ok ? to_f32(ar[i00 * A.nb[0]]) : 0.0f;
+}
+
+// ---- swiglu ----------------------------------------------------------------------------------------
+
+struct GluDev {
+    long long N;
+    int ne00, ne20, ne21, ne22, mode;
+    long long nb0[4], nb1[4], nb2[4];
+};
+
+__global__ void k_swiglu(GluDev p, const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ d)
+{
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < p.N; i += (long long)gridDim.x * blockDim.x) {
+        const long long per3 = (long long)p.ne22 * p.ne21 * p.ne20, per2 = (long long)p.ne21 * p.ne20;
+        const long long i23 = i / per3;
+        const long long r3 = i - i23 * per3;
+        const long long i22 = r3 / per2;
+        const long long r2 = r3 - i22 * per2;
+        const long long i21 = r2 / p.ne20;
+        const long long i20 = r2 - i21 * p.ne20;
+        const long long sa = i23 * p.nb0[3] + i22 * p.nb0[2] + i21 * p.nb0[1] + i20 * p.nb0[0];
+        const long long sb = i23 * p.nb1[3] + i22 * p.nb1[2] + i21 * p.nb1[1] + i20 * p.nb1[0];
+        const long long sd = i23 * p.nb2[3] + i22 * p.nb2[2] + i21 * p.nb2[1] + i20 * p.nb2[0];
+        float g, u;
+        if (p.mode == MUYO_GLU_SPLIT) {
+            g = a[sa];
+            u = b[sb];
+        } else {
+            const long long off = (long long)(p.ne00 / 2) * p.nb0[0];
+            g = p.mode == MUYO_GLU_HALVES ? a[sa] : a[sa + off];
+            u = p.mode == MUYO_GLU_HALVES ? a[sa + off] : a[sa];
+        }
+        d[sd] = silu_mul(g, u);
+    }
+}
+
+// ---- RoPE ------------------------------------------------------------------------------------------
+
+struct RopeDev {
+    int mode, nrows, n_dims, n_offs, has_ff, is_back;
+    float freq_scale, ext_factor, attn_factor, corr0, corr1, theta_scale;
+    int ne00, ne01, ne02;
+    long long nb01, nb02, nb03, nb11, nb12, nb13, a_offset, d_offset;
+};
+
+// rope_funcs.glsl:14-45 (rope_yarn with its ramp), in F32 with accurate cosf/sinf/powf.
+__device__ __forceinline__ void rope_yarn(const RopeDev& p, float theta_extrap, int i0, float& c, float& s)
+{
+    float mscale = p.attn_factor;
+    const float theta_interp = p.freq_scale * theta_extrap;
+    float theta = theta_interp;
+    if (p.ext_factor != 0.0f) {
+        const float y = ((float)(i0 / 2) - p.corr0) / fmaxf(0.001f, p.corr1 - p.corr0);
+        const float ramp = 1.0f - fminf(1.0f, fmaxf(0.0f, y));
+        const float mix = ramp * p.ext_factor;
+        theta = theta_interp * (1.0f - mix) + theta_extrap * mix;
+        mscale *= 1.0f + 0.1f * logf(1.0f / p.freq_scale);
+    }
+    if (p.is_back)
+        theta = -theta;
+    c = cosf(theta) * mscale;
+    s = sinf(theta) * mscale;
+}
+
+__global__ void k_rope(RopeDev p, const float* __restrict__ x, const int32_t* __restrict__ pos,
+                       const float* __restrict__ ff, float* __restrict__ d)
+{
+    const int pairs = p.ne00 / 2;
+    const long long total = (long long)p.nrows * pairs;
+    for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < total;
+         t += (long long)gridDim.x * blockDim.x) {
+        const int row = (int)(t / pairs);
+        const int i0 = 2 * (int)(t - (long long)row * pairs);
+        const int i3 = row / (p.ne01 * p.ne02);
+        const int i2 = (row - i3 * p.ne01 * p.ne02) / p.ne01;
+        const int i1 = row - i3 * p.ne01 * p.ne02 - i2 * p.ne01;
+        const long long xs = p.a_offset + i3 * p.nb03 + i2 * p.nb02 + i1 * p.nb01;
+        const long long ds = p.d_offset + i3 * p.nb13 + i2 * p.nb12 + i1 * p.nb11;
+        if (i0 < p.n_offs || i0 >= p.n_offs + p.n_dims) {
+            d[ds + i0] = x[xs + i0];
+            d[ds + i0 + 1] = x[xs + i0 + 1];
+            continue;
+        }
+        const int iw = i0 - p.n_offs;
+        const float theta_base = (float)pos[i2] * powf(p.theta_scale, (float)(iw / 2));
+        const float freq = p.has_ff ? ff[iw / 2] : 1.0f;
+        float c, s;
+        rope_yarn(p, theta_base / freq, iw, c, s);
+        long long j0, j1;
+        if (p.mode == MUYO_ROPE_NEOX) {
+            j0 = p.n_offs + iw / 2;
+            j1 = j0 + p.n_dims / 2;
+        } else {
+            j0 = i0;
+            j1 = i0 + 1;
+        }
+        const float x0 = x[xs + j0], x1 = x[xs + j1];
+        d[ds + j0] = x0 * c - x1 * s;
+        d[ds + j1] = x0 * s + x1 * c;
+    }
+}
+
+// ---- soft_max --------------------------------------------------------------------------------------
+
+struct SoftMaxDev {
+    int KX, KY, ne01, ne02, ne12, ne13;
+    long long nb11, nb12, nb13;
+    float scale, max_bias, m0, m1;
+    int n_head_log2, nrows_x, has_sinks;
+};
+
+// One CTA per row (soft_max.comp:58-169): v = x*scale + slope*mask, max (seeded with the sink),
+// sum of exp(v - max) (+ exp(sink - max)), D = exp(v - max) * (1 / sum).
+__global__ void __launch_bounds__(kThreads) k_soft_max(SoftMaxDev p, const float* __restrict__ x,
+                                                       const float* __restrict__ mask,
+                                                       const float* __restrict__ sinks, float* __restrict__ d)
+{
+    __shared__ float red[32];
+    const int rowx = blockIdx.x;
+    const int i03 = rowx / (p.ne01 * p.ne02);
+    const int i02 = (rowx - i03 * p.ne01 * p.ne02) / p.ne01;
+    const int i01 = rowx % p.ne01;
+    long long rowy = 0;
+    if (p.KY > 0)
+        rowy = i01 * p.nb11 + (i02 % p.ne12) * p.nb12 + (i03 % p.ne13) * p.nb13;
+    float slope = 1.0f;
+    if (p.max_bias > 0.0f) {
+        const int h = (rowx / p.ne01) % p.ne02;
+        const float base = h < p.n_head_log2 ? p.m0 : p.m1;
+        const int e = h < p.n_head_log2 ? h + 1 : 2 * (h - p.n_head_log2) + 1;
+        slope = powf(base, (float)e);
+    }
+    const float* xr = x + (long long)rowx * p.KX;
+    float* dr = d + (long long)rowx * p.KX;
+    float m = p.has_sinks ? sinks[i02] : -INFINITY;
+    for (int c = threadIdx.x; c < p.KX; c += blockDim.x) {
+        const float v = xr[c] * p.scale + (p.KY > 0 ? slope * mask[rowy + c] : 0.0f);
+        dr[c] = v;
+        m = fmaxf(m, v);
+    }
+    m = block_max(m, red);
+    float sum = 0.0f;
+    for (int c = threadIdx.x; c < p.KX; c += blockDim.x) {
+        const float e = expf(dr[c] - m);
+        dr[c] = e;
+        sum += e;
+    }
+    sum = block_sum(sum, red);
+    if (p.has_sinks)
+        sum += expf(sinks[i02] - m);
+    const float rcp = __fdiv_rn(1.0f, sum);
+    for (int c = threadIdx.x; c < p.KX; c += blockDim.x)
+        dr[c] = dr[c] * rcp;
+}
+
+// ---- argmax ----------------------------------------------------------------------------------------
+
+constexpr int kArgmaxChunk = 8192;  // logits per CTA
+struct ArgPair {
+    float v;
+    int i;
+};
+
+// Stage 1: each CTA scans kArgmaxChunk logits of a row (increasing index per thread, strict >),
+// then reduces with the first-index tie rule. Stage 2 reduces a row's CTA pairs the same way.
+__device__ __forceinline__ ArgPair block_argmax(float v, int i)
+{
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    warp_argmax(v, i);
+    __syncthreads();
+    if (lane == 0) {
+        sv[warp] = v;
+        si[warp] = i;
+    }
+    __syncthreads();
+    v = lane < nw ? sv[lane] : -INFINITY;
+    i = lane < nw ? si[lane] : INT_MAX;
+    warp_argmax(v, i);
+    return ArgPair{v, i};
+}
+
+__global__ void __launch_bounds__(kThreads) k_argmax_partial(const float* __restrict__ a, int KX, int per_row,
+                                                             int index_base, ArgPair* __restrict__ part)
+{
+    const int row = blockIdx.y, blk = blockIdx.x;
+    const float* ar = a + (long long)row * KX;
+    const int c0 = blk * kArgmaxChunk, c1 = min(KX, c0 + kArgmaxChunk);
+    float bv = -INFINITY;
+    int bi = INT_MAX;
+    for (int c = c0 + threadIdx.x; c < c1; c += blockDim.x) {
+        const float v = ar[c];
+        if (pair_better(v, c, bv, bi))
+            bv = v, bi = c;
+    }
+    ArgPair r = block_argmax(bv, bi);
+    if (threadIdx.x == 0) {
+        if (r.i != INT_MAX)
+            r.i += index_base;
+        part[(long long)row * per_row + blk] = r;
+    }
+}
+
+// Reduces n pairs per row; writes the index (0 when no value compares, e.g. all NaN, as the
+// host's scan that starts from index 0 would return).
+__global__ void __launch_bounds__(kThreads) k_argmax_final(const ArgPair* __restrict__ part, int n,
+                                                           int32_t* __restrict__ d)
+{
+    const int row = blockIdx.x;
+    float bv = -INFINITY;
+    int bi = INT_MAX;
+    for (int k = threadIdx.x; k < n; k += blockDim.x) {
+        const ArgPair q = part[(long long)row * n + k];
+        if (pair_better(q.v, q.i, bv, bi))
+            bv = q.v, bi = q.i;
+    }
+    ArgPair r = block_argmax(bv, bi);
+    if (threadIdx.x == 0)
+        d[row] = r.i == INT_MAX ? 0 : r.i;
+}
+
+// ---- copy ------------------------------------------------------------------------------------------
+
+__global__ void k_copy(Dims4 S, Dims4 T, long long a_off, long long d_off, const float* __restrict__ a,
+                       float* __restrict__ d, long long n)
+{
+    for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < n;
+         idx += (long long)gridDim.x * blockDim.x) {
+        long long t = idx, u = idx, si = a_off, di = d_off;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            si += (t % S.ne[k]) * S.nb[k];
+            t /= S.ne[k];
+            di += (u % T.ne[k]) * T.nb[k];
+            u /= T.ne[k];
+        }
+        d[di] = a[si];
+    }
+}
+
+// Reduces n partial pairs into one pair (the shard result of mat_vec_f16_argmax).
+__global__ void __launch_bounds__(kThreads) k_pairs_to_pair(const ArgPair* __restrict__ part, int n, ArgPair* __restrict__ out)
+{
+    float bv = -INFINITY;
+    int bi = INT_MAX;
+    for (int k = threadIdx.x; k < n; k += blockDim.x) {
+        const ArgPair q = part[k];
+        if (pair_better(q.v, q.i, bv, bi))
+            bv = q.v, bi = q.i;
+    }
+    const ArgPair r = block_argmax(bv, bi);
+    if (threadIdx.x == 0)
+        *out = r;
+}
+
+}  // namespace muyo
+
+using namespace muyo;
+
+// ---- extern "C" entry points ---------------------------------------------------------------------
+
+extern "C" int muyo_cuda_mat_vec_f16(const MuyoMatVecParams* p, const void* a, const float* b, float* d,
+                                     const float* fuse0, const float* fuse1, void* stream)
+{
+    clear_error();
+    return mat_vec_any(true, p, a, b, d, fuse0, fuse1, stream);
+}
+
+extern "C" int muyo_cuda_mat_vec_f32(const MuyoMatVecParams* p, const float* a, const float* b, float* d,
+                                     const float* fuse0, const float* fuse1, void* stream)
+{
+    clear_error();
+    return mat_vec_any(false, p, a, b, d, fuse0, fuse1, stream);
+}
+
+extern "C" int muyo_cuda_add(const MuyoBinaryParams* p, const float* a, const float* b, float* d, void* stream)
+{
+    clear_error();
+    MUYO_REQUIRE(p && a && b && d, "add: null parameter block or buffer");
+    const Dims4 A = dims(p->ne00, p->ne01, p->ne02, p->ne03, p->nb00, p->nb01, p->nb02, p->nb03);
+    const Dims4 B = dims(p->ne10, p->ne11, p->ne12, p->ne13, p->nb10, p->nb11, p->nb12, p->nb13);
+    const Dims4 D = dims(p->ne20, p->ne21, p->ne22, p->ne23, p->nb20, p->nb21, p->nb22, p->nb23);
+    const long long n = count(D);
+    MUYO_REQUIRE(n > 0, "add: empty output");
+    MUYO_REQUIRE(count(A) == n, "add: A and D element counts differ");
+    for (int k = 0; k < 4; ++k)
+        MUYO_REQUIRE(A.ne[k] == D.ne[k] && D.ne[k] % B.ne[k] == 0, "add: dimension %d does not broadcast", k);
+    const cudaStream_t s = as_stream(stream);
+    if (contiguous(A) && contiguous(B) && contiguous(D) && count(B) == n && n % 4 == 0 && aligned16(a) &&
+        aligned16(b) && aligned16(d)) {
+        k_add_contig<<<grid_for(n / 4), kThreads, 0, s>>>(reinterpret_cast<const float4*>(a),
+                                                          reinterpret_cast<const float4*>(b),
+                                                          reinterpret_cast<float4*>(d), n / 4);
+    } else {
+        k_add_general<<<grid_for(n), kThreads, 0, s>>>(A, B, D, a, b, d, n);
+    }
+    MUYO_LAUNCH_CHECK();
+    return MUYO_OK;
+}
+
+extern "C" int muyo_cuda_rms_norm(const MuyoBinaryParams* p, const float* a, const float* w, float* d, void* stream)
+{
+    clear_error();
+    MUYO_REQUIRE(p && a && w && d, "rms_norm: null parameter block or buffer");
+    const Dims4 A = dims(p->ne00, p->ne01, p->ne02, p->ne03, p->nb00 ? p->nb00 : 1, p->nb01, p->nb02, p->nb03);
+    const Dims4 W = dims(p->ne10, 1, 1, 1, p->nb10 ? p->nb10 : 1, 0, 0, 0);
+    const Dims4 D = dims(p->ne20, p->ne21, p->ne22, p->ne23, p->nb20 ? p->nb20 : 1, p->nb21, p->nb22, p->nb23);
+    MUYO_REQUIRE(p->ne00 > 0 && p->ne10 > 0, "rms_norm: empty row or weight");
+    MUYO_REQUIRE(D.ne[0] == A.ne[0] && D.ne[1] == A.ne[1] && D.ne[2] == A.ne[2] && D.ne[3] == A.ne[3],
+                 "rms_norm: D shape differs from A");
+    MUYO_REQUIRE(p->param1 >= 0.0f, "rms_norm: eps must be >= 0");
+    const long long rows = (long long)A.ne[1] * A.ne[2] * A.ne[3];
+    MUYO_REQUIRE(rows <= INT_MAX, "rms_norm: too many rows");
+    k_rms_norm<<<(unsigned)rows, kThreads, 0, as_stream(stream)>>>(A, W, D, a, w, d, p->param1);
+    MUYO_LAUNCH_CHECK();
+    return MUYO_OK;
+}
+
+static int get_rows_any(bool f16, const MuyoBinaryParams* p, const void* a, const int32_t* b, float* d, void* stream)
+{
+    MUYO_REQUIRE(p && a && b && d, "get_rows: null parameter block or buffer");
+    const Dims4 A = dims(p->ne00, p->ne01, p->ne02, p->ne03, p->nb00 ? p->nb00 : 1, p->nb01, p->nb02, p->nb03);
+    const Dims4 B = dims(p->ne10, p->ne11, p->ne12, p->ne13, p->nb10 ? p->nb10 : 1, p->nb11, p->nb12, p->nb13);
+    const Dims4 D = dims(p->ne20, p->ne21, p->ne22, p->ne23, p->nb20 ? p->nb20 : 1, p->nb21, p->nb22, p->nb23);
+    MUYO_REQUIRE(p->ne00 > 0 && p->ne01 > 0, "get_rows: empty table");
+    MUYO_REQUIRE(D.ne[0] == A.ne[0], "get_rows: output row length %d != table row length %d", D.ne[0], A.ne[0]);
+    MUYO_REQUIRE(B.ne[0] <= 65535 && (long long)B.ne[1] * B.ne[2] <= 65535, "get_rows: too many ids");
+    dim3 grid((A.ne[0] + kThreads - 1) / kThreads, B.ne[0], B.ne[1] * B.ne[2]);
+    if (f16)
+        k_get_rows<__half><<<grid, kThreads, 0, as_stream(stream)>>>(A, B, D, static_cast<const __half*>(a), b, d);
+    else
+        k_get_rows<float><<<grid, kThreads, 0, as_stream(stream)>>>(A, B, D, static_cast<const float*>(a), b, d);
+    MUYO_LAUNCH_CHECK();
+    return MUYO_OK;
+}
+
+extern "C" int muyo_cuda_get_rows_f16(const MuyoBinaryParams* p, const void* a, const int32_t* b, float* d,
+                                      void* stream)
+{
+    clear_error();
+    return get_rows_any(true, p, a, b, d, stream);
+}
+
+extern "C" int muyo_cuda_get_rows_f32(const MuyoBinaryParams* p, const float* a, const int32_t* b, float* d,
+                                      void* stream)
+{
+    clear_error();
+    return get_rows_any(false, p, a, b, d, stream);
+}
+
+extern "C" int muyo_cuda_swiglu(const MuyoGluParams* p, const float* a, const float* b, float* d, void* stream)
+{
+    clear_error();
+    MUYO_REQUIRE(p && a && d, "swiglu: null parameter block or buffer");
+    MUYO_REQUIRE(p->mode <= MUYO_GLU_SPLIT, "swiglu: unknown mode %u", p->mode);
+    MUYO_REQUIRE(p->mode != MUYO_GLU_SPLIT || b, "swiglu: split mode needs B");
+    MUYO_REQUIRE(p->N > 0 && p->ne20 > 0, "swiglu: empty output");
+    MUYO_REQUIRE(p->mode == MUYO_GLU_SPLIT || p->ne00 >= 2 * p->ne20, "swiglu: A row too short for [gate|up]");
+    GluDev g{};
+    g.N = p->N;
+    g.ne00 = (int)p->ne00;
+    g.ne20 = (int)p->ne20;
+    g.ne21 = p->ne21 ? (int)p->ne21 : 1;
+    g.ne22 = p->ne22 ? (int)p->ne22 : 1;
+    g.mode = (int)p->mode;
+    const uint32_t nb0[4] = {p->nb00, p->nb01, p->nb02, p->nb03}, nb1[4] = {p->nb10, p->nb11, p->nb12, p->nb13},
+                   nb2[4] = {p->nb20, p->nb21, p->nb22, p->nb23};
+    for (int k = 0; k < 4; ++k) {
+        g.nb0[k] = nb0[k];
+        g.nb1[k] = nb1[k];
+        g.nb2[k] = nb2[k];
+    }
+    if (!g.nb0[0])
+        g.nb0[0] = 1;
+    if (!g.nb1[0])
+        g.nb1[0] = 1;
+    if (!g.nb2[0])
+        g.nb2[0] = 1;
+    k_swiglu<<<grid_for(g.N), kThreads, 0, as_stream(stream)>>>(g, a, b, d);
+    MUYO_LAUNCH_CHECK();
+    return MUYO_OK;
+}
+
+extern "C" int muyo_cuda_rope(const MuyoRopeParams* p, const float* x, const int32_t* pos, const float* freq_factors,
+                              float* d, void* stream)
+{
+    clear_error();
+    MUYO_REQUIRE(p && x && pos && d, "rope: null parameter block or buffer");
+    MUYO_REQUIRE(p->rope_mode == MUYO_ROPE_NEOX || p->rope_mode == MUYO_ROPE_NORMAL,
+                 "rope: mode %u not implemented (NORMAL=0, NEOX=2)", p->rope_mode);
+    MUYO_REQUIRE(p->ne00 > 0 && p->ne00 % 2 == 0, "rope: ne00 must be positive and even");
+    MUYO_REQUIRE(p->n_dims % 2 == 0 && p->n_offs % 2 == 0 && p->n_offs + p->n_dims <= p->ne00,
+                 "rope: rotated channels [n_offs, n_offs + n_dims) must be even and within ne00");
+    MUYO_REQUIRE(!p->has_ff || freq_factors, "rope: has_ff set but freq_factors is null");
+    MUYO_REQUIRE(p->nrows > 0, "rope: no rows");
+    RopeDev r{};
+    r.mode = (int)p->rope_mode;
+    r.nrows = (int)p->nrows;
+    r.n_dims = (int)p->n_dims;
+    r.n_offs = (int)p->n_offs;
+    r.has_ff = (int)p->has_ff;
+    r.is_back = (int)p->is_back;
+    r.freq_scale = p->freq_scale;
+    r.ext_factor = p->ext_factor;
+    r.attn_factor = p->attn_factor;
+    r.corr0 = p->corr_dims[0];
+    r.corr1 = p->corr_dims[1];
+    r.theta_scale = p->theta_scale;
+    r.ne00 = (int)p->ne00;
+    r.ne01 = p->ne01 ? (int)p->ne01 : 1;
+    r.ne02 = p->ne02 ? (int)p->ne02 : 1;
+    r.nb01 = p->nb01;
+    r.nb02 = p->nb02;
+    r.nb03 = p->nb03;
+    r.nb11 = p->nb11;
+    r.nb12 = p->nb12;
+    r.nb13 = p->nb13;
+    r.a_offset = p->a_offset;
+    r.d_offset = p->d_offset;
+    const long long total = (long long)p->nrows * (p->ne00 / 2);
+    k_rope<<<grid_for(total), kThreads, 0, as_stream(stream)>>>(r, x, pos, freq_factors, d);
+    MUYO_LAUNCH_CHECK();
+    return MUYO_OK;
+}
+
+extern "C" int muyo_cuda_soft_max(const MuyoSoftMaxParams* p, const float* x, const float* mask, const float* sinks,
+                                  float* d, void* stream)
+{
+    clear_error();
+    MUYO_REQUIRE(p && x && d, "soft_max: null parameter block or buffer");
+    MUYO_REQUIRE(p->KX > 0 && p->nrows_x > 0, "soft_max: empty rows");
+    MUYO_REQUIRE(p->KY == 0 || mask, "soft_max: KY > 0 needs a mask");
+    MUYO_REQUIRE(!p->has_sinks || sinks, "soft_max: has_sinks needs sinks");
+    MUYO_REQUIRE(x != d, "soft_max: in-place (x == d) is not supported");
+    SoftMaxDev s{};
+    s.KX = (int)p->KX;
+    s.KY = (int)p->KY;
+    s.ne01 = p->ne01 ? (int)p->ne01 : 1;
+    s.ne02 = p->ne02 ? (int)p->ne02 : 1;
+    s.ne12 = p->ne12 ? (int)p->ne12 : 1;
+    s.ne13 = p->ne13 ? (int)p->ne13 : 1;
+    s.nb11 = p->nb11;
+    s.nb12 = p->nb12;
+    s.nb13 = p->nb13;
+    s.scale = p->scale;
+    s.max_bias = p->max_bias;
+    s.m0 = p->m0;
+    s.m1 = p->m1;
+    s.n_head_log2 = (int)p->n_head_log2;
+    s.nrows_x = (int)p->nrows_x;
+    s.has_sinks = (int)p->has_sinks;
+    k_soft_max<<<p->nrows_x, kThreads, 0, as_stream(stream)>>>(s, x, mask, sinks, d);
+    MUYO_LAUNCH_CHECK();
+    return MUYO_OK;
+}
+
+static int argmax_blocks(uint32_t KX) { return (int)((KX + kArgmaxChunk - 1) / kArgmaxChunk); }
+
+extern "C" size_t muyo_cuda_argmax_workspace_size(const MuyoGenericParams* p)
+{
+    if (!p || p->KX == 0)
+        return 0;
+    const size_t ky = p->KY ? p->KY : 1;
+    return ky * (size_t)argmax_blocks(p->KX) * sizeof(ArgPair);
+}
+
+static int argmax_launch(const float* a, uint32_t KX, uint32_t KY, int index_base, ArgPair* part, int32_t* d,
+                         cudaStream_t s)
+{
+    const int per_row = argmax_blocks(KX);
+    k_argmax_partial<<<dim3(per_row, KY), kThreads, 0, s>>>(a, (int)KX, per_row, index_base, part);
+    MUYO_LAUNCH_CHECK();
+    if (d) {
+        k_argmax_final<<<KY, kThreads, 0, s>>>(part, per_row, d);
+        MUYO_LAUNCH_CHECK();
+    }
+    return MUYO_OK;
+}
+
+extern "C" int muyo_cuda_argmax(const MuyoGenericParams* p, const float* a, int32_t* d, void* workspace,
+                                size_t workspace_bytes, void* stream)
+{
+    clear_error();
+    MUYO_REQUIRE(p && a && d, "argmax: null parameter block or buffer");
+    MUYO_REQUIRE(p->KX > 0 && p->KX <= (uint32_t)INT_MAX, "argmax: KX must be in [1, INT_MAX]");
+    const uint32_t KY = p->KY ? p->KY : 1;
+    MUYO_REQUIRE(KY <= 65535u, "argmax: KY %u exceeds 65535", KY);
+    const size_t need = muyo_cuda_argmax_workspace_size(p);
+    MUYO_REQUIRE(workspace && workspace_bytes >= need, "argmax: workspace of %zu bytes needed, %zu given", need,
+                 workspace_bytes);
+    MUYO_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 7u) == 0, "argmax: workspace must be 8-byte aligned");
+    return argmax_launch(a, p->KX, KY, 0, static_cast<ArgPair*>(workspace), d, as_stream(stream));
+}
+
+extern "C" int muyo_cuda_copy_f32(const MuyoUnaryParams* p, const float* a, float* d, void* stream)
+{
+    clear_error();
+    MUYO_REQUIRE(p && a && d, "copy: null parameter block or buffer");
+    const Dims4 S = dims(p->ne00, p->ne01, p->ne02, p->ne03, p->nb00, p->nb01, p->nb02, p->nb03);
+    const Dims4 T = dims(p->ne10, p->ne11, p->ne12, p->ne13, p->nb10, p->nb11, p->nb12, p->nb13);
+    MUYO_REQUIRE(p->ne > 0, "copy: ne must be positive");
+    MUYO_REQUIRE((long long)p->ne <= count(S) && (long long)p->ne <= count(T),
+                 "copy: ne exceeds the source or destination shape");
+    k_copy<<<grid_for(p->ne), kThreads, 0, as_stream(stream)>>>(S, T, p->a_offset, p->d_offset, a, d, p->ne);
+    MUYO_LAUNCH_CHECK();
+    return MUYO_OK;
+}
+
+extern "C" int muyo_cuda_mat_vec_f16_argmax(const MuyoMatVecParams* p, const void* a, const float* b, float* d,
+                                            uint32_t row_begin, void* pair_out, void* workspace,
+                                            size_t workspace_bytes, void* stream)
+{
+    clear_error();
+    MUYO_REQUIRE(p && pair_out, "mat_vec_argmax: null parameter block or pair output");
+    MUYO_REQUIRE(p->batches <= 1, "mat_vec_argmax: one batch only");
+    MUYO_REQUIRE(p->fusion_flags == 0, "mat_vec_argmax: no fusion flags");
+    MUYO_REQUIRE((uint64_t)row_begin + p->rows <= (uint64_t)INT_MAX, "mat_vec_argmax: global row index overflows");
+    MuyoGenericParams g{p->rows, 1, 0, 0, 0, 0};
+    const size_t need = muyo_cuda_argmax_workspace_size(&g);
+    MUYO_REQUIRE(workspace && workspace_bytes >= need, "mat_vec_argmax: workspace of %zu bytes needed, %zu given",
+                 need, workspace_bytes);
+    MUYO_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 7u) == 0 &&
+                     (reinterpret_cast<uintptr_t>(pair_out) & 7u) == 0,
+                 "mat_vec_argmax: workspace and pair_out must be 8-byte aligned");
+    int rc = mat_vec_any(true, p, a, b, d, nullptr, nullptr, stream);
+    if (rc != MUYO_OK)
+        return rc;
+    const cudaStream_t s = as_stream(stream);
+    ArgPair* part = static_cast<ArgPair*>(workspace);
+    rc = argmax_launch(d, p->rows, 1, (int)row_begin, part, nullptr, s);
+    if (rc != MUYO_OK)
+        return rc;
+    // One shard pair: reduce the partials into pair_out.
+    k_pairs_to_pair<<<1, kThreads, 0, s>>>(part, argmax_blocks(p->rows), static_cast<ArgPair*>(pair_out));
+    MUYO_LAUNCH_CHECK();
+    return MUYO_OK;
+}
+
+extern "C" int muyo_cuda_argmax_pairs(const void* pairs, uint32_t n_pairs, int32_t* d, void* stream)
+{
+    clear_error();
+    MUYO_REQUIRE(pairs && d && n_pairs > 0, "argmax_pairs: null buffer or no pairs");
+    MUYO_REQUIRE((reinterpret_cast<uintptr_t>(pairs) & 7u) == 0, "argmax_pairs: pairs must be 8-byte aligned");
+    k_argmax_final<<<1, kThreads, 0, as_stream(stream)>>>(static_cast<const ArgPair*>(pairs), (int)n_pairs, d);
+    MUYO_LAUNCH_CHECK();
+    return MUYO_OK;
+}

@@ -1,0 +1,238 @@
+"""TEST INFRASTRUCTURE: ctypes wrapper of the C oracle (oracle.c).
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline legs import this module, as
+the checker or as the timed CPU baseline. The product path never does.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
+
+
+def build() -> str:
+    """Compile liboracle.so with oracle/Makefile (idempotent)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < os.path.getmtime(os.path.join(HERE, "oracle.c")):
+            build()
+        L = C.CDLL(LIB_PATH)
+        L.oracle_mat_vec_f16.argtypes = [_u16p, C.c_int64, _f32p, _f32p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+        L.oracle_mat_vec_f32.argtypes = [_f32p, _f32p, _f32p] + [C.c_int] * 11 + [C.c_void_p]
+        L.oracle_rms_norm.argtypes = [_f32p, _f32p, _f32p, C.c_int, C.c_int, C.c_float]
+        L.oracle_add.argtypes = [_f32p, _f32p, _f32p, C.c_int64]
+        L.oracle_swiglu.argtypes = [_f32p, _f32p, _f32p, C.c_int64]
+        L.oracle_rope_neox.argtypes = [_f32p, _f32p] + [C.c_int] * 6 + [C.c_float]
+        L.oracle_soft_max.argtypes = [_f32p, _f32p, C.c_int, C.c_int, C.c_float]
+        L.oracle_argmax.argtypes = [_f32p, C.c_int64]
+        L.oracle_argmax.restype = C.c_int
+        L.oracle_get_rows_f16.argtypes = [_u16p, C.c_int, C.c_int, _f32p]
+        L.oracle_attention.argtypes = [_f32p, _f32p, _f32p, _f32p] + [C.c_int] * 5 + [C.c_float]
+        L.oracle_f2h_array.argtypes = [_f32p, _u16p, C.c_int64]
+        L.oracle_h2f.argtypes = [C.c_uint16]
+        L.oracle_h2f.restype = C.c_float
+        L.oracle_qwen2_layer.argtypes = [C.c_void_p, C.c_int, _f32p, C.c_void_p, C.c_void_p, C.c_int, C.c_int]
+        L.oracle_qwen2_step.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
+                                        _f32p, C.c_void_p]
+        L.oracle_qwen2_step.restype = C.c_int
+        L.oracle_set_num_threads.argtypes = [C.c_int]
+        L.oracle_num_threads.restype = C.c_int
+        _lib = L
+    return _lib
+
+
+def set_threads(n: int) -> None:
+    lib().oracle_set_num_threads(int(n))
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _ptr(a) -> int | None:
+    return None if a is None else a.ctypes.data
+
+
+def f16_bits(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.float16)).view(np.uint16)
+
+
+def mat_vec_f16(w16: np.ndarray, x, bias0=None, bias1=None) -> np.ndarray:
+    rows, cols = w16.shape
+    y = np.empty(rows, np.float32)
+    b0 = None if bias0 is None else _f32(bias0)
+    b1 = None if bias1 is None else _f32(bias1)
+    lib().oracle_mat_vec_f16(f16_bits(w16), cols, _f32(x), y, rows, cols, _ptr(b0), _ptr(b1))
+    return y
+
+
+def mat_vec_f32(a, b, *, ncols, rows, batches, stride_a, batch_stride_a, batch_stride_b, batch_stride_d,
+                ne02=1, ne12=1, broadcast2=1, broadcast3=1, bias0=None, d_size=None) -> np.ndarray:
+    d = np.zeros(d_size if d_size is not None else batches * batch_stride_d if batches > 1 else rows, np.float32)
+    b0 = None if bias0 is None else _f32(bias0)
+    lib().oracle_mat_vec_f32(_f32(a), _f32(b), d, ncols, rows, batches, stride_a, batch_stride_a,
+                             batch_stride_b, batch_stride_d, ne02, ne12, broadcast2, broadcast3, _ptr(b0))
+    return d
+
+
+def rms_norm(x, w, eps: float) -> np.ndarray:
+    x = _f32(x)
+    x2 = x.reshape(-1, x.shape[-1])
+    y = np.empty_like(x2)
+    lib().oracle_rms_norm(x2, _f32(w), y, x2.shape[0], x2.shape[1], eps)
+    return y.reshape(x.shape)
+
+
+def add(a, b) -> np.ndarray:
+    a, b = _f32(a), _f32(b)
+    d = np.empty_like(a)
+    lib().oracle_add(a, b, d, a.size)
+    return d
+
+
+def swiglu(g, u) -> np.ndarray:
+    g, u = _f32(g), _f32(u)
+    d = np.empty_like(g)
+    lib().oracle_swiglu(g, u, d, g.size)
+    return d
+
+
+def rope_neox(x, pos: int, theta_scale: float, n_dims: int | None = None) -> np.ndarray:
+    x = _f32(x)
+    x2 = x.reshape(-1, x.shape[-1])
+    rows, ne00 = x2.shape
+    y = np.empty_like(x2)
+    lib().oracle_rope_neox(x2, y, rows, ne00, n_dims or ne00, ne00, ne00, pos, theta_scale)
+    return y.reshape(x.shape)
+
+
+def soft_max(x, scale: float) -> np.ndarray:
+    x = _f32(x)
+    x2 = x.reshape(-1, x.shape[-1])
+    y = np.empty_like(x2)
+    lib().oracle_soft_max(x2, y, x2.shape[0], x2.shape[1], scale)
+    return y.reshape(x.shape)
+
+
+def argmax(x) -> int:
+    x = _f32(x)
+    return int(lib().oracle_argmax(x, x.size))
+
+
+def get_rows_f16(table16: np.ndarray, token: int) -> np.ndarray:
+    out = np.empty(table16.shape[1], np.float32)
+    lib().oracle_get_rows_f16(f16_bits(table16), table16.shape[1], int(token), out)
+    return out
+
+
+def attention(q, keys, values, heads: int, kv_heads: int, scale: float) -> np.ndarray:
+    """q [heads, hd]; keys/values [kv_heads, n, hd] -> [heads, hd]."""
+    q, keys, values = _f32(q), _f32(keys), _f32(values)
+    kvh, n, hd = keys.shape
+    out = np.empty((heads, hd), np.float32)
+    lib().oracle_attention(q, keys, values, out, heads, kv_heads, n, hd, n * hd, scale)
+    return out
+
+
+def f2h(x) -> np.ndarray:
+    x = _f32(x)
+    y = np.empty(x.shape, np.uint16)
+    lib().oracle_f2h_array(x.reshape(-1), y.reshape(-1), x.size)
+    return y
+
+
+# ---- Qwen2 model ----------------------------------------------------------------------------------
+
+class _Layer(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("attn_norm", "wq", "bq", "wk", "bk", "wv", "bv", "wo", "ffn_norm",
+                                           "wgate", "wup", "wdown")]
+
+
+class _Model(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("layers", "hidden", "ffn", "heads", "kv_heads", "vocab", "max_seq")] + \
+               [("eps", C.c_float), ("rope_base", C.c_float), ("token_embd", C.c_void_p), ("output", C.c_void_p),
+                ("output_norm", C.c_void_p), ("layer", C.POINTER(_Layer))]
+
+
+_LAYER_TENSORS = [("attn_norm", "attn_norm.weight"), ("wq", "attn_q.weight"), ("bq", "attn_q.bias"),
+                  ("wk", "attn_k.weight"), ("bk", "attn_k.bias"), ("wv", "attn_v.weight"), ("bv", "attn_v.bias"),
+                  ("wo", "attn_output.weight"), ("ffn_norm", "ffn_norm.weight"), ("wgate", "ffn_gate.weight"),
+                  ("wup", "ffn_up.weight"), ("wdown", "ffn_down.weight")]
+
+
+class Qwen2:
+    """The oracle's view of a synthetic model (``muyo_llm_b200.synth.make_model``), with its caches."""
+
+    def __init__(self, cfg, tensors: dict[str, np.ndarray], kv_f16: bool = False):
+        self.cfg = cfg
+        self.kv_f16 = kv_f16
+        keep = {}
+        for k, v in tensors.items():
+            keep[k] = np.ascontiguousarray(v.view(np.uint16) if v.dtype == np.float16 else v.astype(np.float32))
+        self._keep = keep
+        self._layers = (_Layer * cfg.layers)()
+        for l in range(cfg.layers):
+            for field, suffix in _LAYER_TENSORS:
+                setattr(self._layers[l], field, keep[f"blk.{l}.{suffix}"].ctypes.data)
+        self._m = _Model(cfg.layers, cfg.hidden, cfg.ffn, cfg.heads, cfg.kv_heads, cfg.vocab, cfg.max_seq,
+                         cfg.rms_eps, cfg.rope_base, keep["token_embd.weight"].ctypes.data,
+                         keep["output.weight"].ctypes.data, keep["output_norm.weight"].ctypes.data, self._layers)
+        n = cfg.layers * cfg.kv_heads * cfg.max_seq * cfg.head_dim
+        dt = np.uint16 if kv_f16 else np.float32
+        self.kcache = np.zeros(n, dt)
+        self.vcache = np.zeros(n, dt)
+
+    def reset(self) -> None:
+        self.kcache[:] = 0
+        self.vcache[:] = 0
+
+    def step(self, token: int, pos: int, want_hidden: bool = False):
+        logits = np.empty(self.cfg.vocab, np.float32)
+        hidden = np.empty(self.cfg.hidden, np.float32) if want_hidden else None
+        arg = lib().oracle_qwen2_step(C.byref(self._m), self.kcache.ctypes.data, self.vcache.ctypes.data,
+                                      int(self.kv_f16), int(token), int(pos), logits, _ptr(hidden))
+        return (arg, logits, hidden) if want_hidden else (arg, logits)
+
+    def layer(self, l: int, h: np.ndarray, pos: int) -> np.ndarray:
+        h = _f32(h).copy()
+        cfg = self.cfg
+        per = cfg.kv_heads * cfg.max_seq * cfg.head_dim
+        lib().oracle_qwen2_layer(C.byref(self._m), l, h, self.kcache[l * per:].ctypes.data,
+                                 self.vcache[l * per:].ctypes.data, int(self.kv_f16), int(pos))
+        return h
+
+
+def top2_margin(logits: np.ndarray) -> float:
+    top = np.partition(logits, -2)[-2:]
+    return float(top[1] - top[0])
+
+
+def qwen2_greedy(cfg, tensors, forced: list[int], n_total: int, kv_f16: bool = False, threads: int | None = None):
+    """Teacher-force ``forced`` then decode greedily up to ``n_total`` ids; returns (ids, margins)
+    where margins[i] is the top-1 minus top-2 logit after step i."""
+    set_threads(threads or os.cpu_count() or 1)
+    m = Qwen2(cfg, tensors, kv_f16=kv_f16)
+    seq = list(forced)
+    margins = []
+    for step in range(n_total - 1):
+        arg, logits = m.step(seq[step], step)
+        margins.append(top2_margin(logits))
+        if step + 1 >= len(seq):
+            seq.append(arg)
+    return seq, margins
