@@ -131,6 +131,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnDev p, const flo
 
     const int kvh = blockIdx.x, chunk = blockIdx.y;
     const int pos = pos_ptr ? *pos_ptr : p.n_keys_fixed - 1;
+    if (pos < 0 || pos >= p.max_seq)
+        return;  // a device position outside the cache: nothing is read or written
     const int n = pos + 1;
     const int nchunks = (n + kAttnKeys - 1) / kAttnKeys;
     if (chunk >= nchunks)
@@ -179,6 +181,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnDev p, const flo
         for (int e = threadIdx.x; e < G * HD; e += blockDim.x)
             Qs[e] = q_in[(size_t)kvh * G * HD + e];
     }
+    __syncthreads();  // Kn / Vn are read by other threads below
 
     // Stage the K and V tiles (keys that earlier steps wrote; the new key comes from Kn/Vn).
     for (int e = threadIdx.x; e < kAttnKeys * HD; e += blockDim.x) {
@@ -281,6 +284,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention_combine(AttnDev p, c
 {
     const int kvh = blockIdx.x;
     const int pos = pos_ptr ? *pos_ptr : p.n_keys_fixed - 1;
+    if (pos < 0 || pos >= p.max_seq)
+        return;
     const int nchunks = (pos + 1 + kAttnKeys - 1) / kAttnKeys;
     if (nchunks <= 1)
         return;  // the single chunk wrote its output directly

@@ -50,6 +50,7 @@ struct GemvFused {
     const __half* embd;    // EMBED_NORM table [vocab][K]
     const int32_t* tokens;
     const Control* ctrl_ro;
+    int vocab, max_seq;    // EMBED_NORM bounds
     float* x_copy;         // EMBED_NORM: CTA 0 stores the embedded row (the residual stream)
     int K;
     // matrices
@@ -83,7 +84,12 @@ __device__ __forceinline__ void stage_input(const GemvFused& a, float* xs, float
     const float* src = a.x;
     const __half* erow = nullptr;
     if (PRO == PRO_EMBED_NORM) {
-        const int token = a.tokens[a.ctrl_ro->step];
+        // Ids and positions are bounded on the host; an out-of-range value read here gathers row 0
+        // rather than reading outside the table.
+        const int step = a.ctrl_ro->step;
+        int token = step >= 0 && step < a.max_seq ? a.tokens[step] : 0;
+        if (token < 0 || token >= a.vocab)
+            token = 0;
         erow = a.embd + (size_t)token * K;
     }
     float ss = 0.0f;
@@ -220,9 +226,10 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvFused a)
             const int greedy = i == INT_MAX ? 0 : i;
             Control* c = a.ctrl;
             const int s = c->step;
-            const int next = s + 1 < c->prompt_end ? a.tokens_rw[s + 1] : greedy;
-            if (s + 1 < c->total)
+            if (s + 1 < c->total && s + 1 < a.max_seq) {
+                const int next = s + 1 < c->prompt_end ? a.tokens_rw[s + 1] : greedy;
                 a.tokens_rw[s + 1] = next;
+            }
             c->greedy = greedy;
             c->step = s + 1;
             *a.counter = 0;
@@ -395,6 +402,8 @@ static int layer_forward(const Shape& s, const LayerPtrs& w, void* kc, void* vc,
         a.embd = embd;
         a.tokens = tokens;
         a.ctrl_ro = ctrl;
+        a.vocab = s.vocab;
+        a.max_seq = s.max_seq;
         a.x_copy = embed_out;
         rc = launch_gemv<1, 4, 1, 1, PRO_EMBED_NORM, EPI_BIAS>(a, sms * 8, st);
     } else {
@@ -541,6 +550,7 @@ static int record_step(MuyoModel* m, cudaStream_t st)
     a.counter = m->lm_counter;
     a.ctrl = m->ctrl;
     a.tokens_rw = m->tokens;
+    a.max_seq = s.max_seq;
     return launch_gemv<2, 4, 1, 1, PRO_NORM, EPI_LOGITS>(a, m->lm_grid, st);
 }
 
@@ -556,6 +566,8 @@ __global__ void k_kv_append(int kv_heads, int max_seq, double base, const float*
                             const int32_t* __restrict__ pos_ptr)
 {
     const int pos = *pos_ptr;
+    if (pos < 0 || pos >= max_seq)
+        return;  // a device position outside the cache: nothing is written
     const int h = blockIdx.x;
     const size_t row = ((size_t)h * max_seq + pos) * HD;
     for (int j = threadIdx.x; j < HD / 2; j += blockDim.x) {

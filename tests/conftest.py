@@ -59,3 +59,22 @@ def assert_rel_close(actual, expected, tol: float, what: str = "") -> None:
         i = bad[0]
         raise AssertionError(f"{what}: {bad.size} of {a.size} outside {tol}*(1+|e|); first at {i}: {a[i]} vs {e[i]}"
                              f" (max err {np.max(np.abs(a - e) / (1 + np.abs(e))):.3g})")
+
+
+def assert_gemv_accurate(actual, w, x, bias=None, what: str = "") -> None:
+    """A rigorous accuracy bound for an FP32-accumulated dot product of K terms: |y - exact| <=
+    gamma_K * sum_k |w_k x_k| with gamma_K = K * 2^-24 / (1 - K * 2^-24) (recursive summation, any
+    order), plus one rounding of the bias add. The exact value is computed in float64."""
+    w64 = np.asarray(w, np.float64)
+    x64 = np.asarray(x, np.float64)
+    exact = w64 @ x64
+    mag = np.abs(w64) @ np.abs(x64)
+    K = w64.shape[1]
+    u = 2.0 ** -24
+    bound = (K * u / (1 - K * u)) * mag
+    if bias is not None:
+        exact = exact + np.asarray(bias, np.float64)
+        bound = bound + 2 * u * (np.abs(exact) + mag)
+    err = np.abs(np.asarray(actual, np.float64) - exact)
+    bad = np.flatnonzero(err > bound + 1e-30)
+    assert bad.size == 0, f"{what}: {bad.size} rows exceed the FP32 summation bound; first {bad[0]}: err {err[bad[0]]} > {bound[bad[0]]}"
