@@ -119,6 +119,7 @@ SIGNATURES = {
     "muyo_model_position": (C.c_int, [VP, P(C.c_int32)]),
     "muyo_model_buffer": (C.c_int, [VP, C.c_char_p, P(VP), P(C.c_size_t)]),
     "muyo_model_destroy": (C.c_int, [VP]),
+    "muyo_model_set_option": (C.c_int, [VP, C.c_char_p, C.c_int]),
     "muyo_cuda_mat_vec_f16_argmax": (C.c_int, [P(MatVecParams), VP, VP, VP, U32, VP, VP, C.c_size_t, VP]),
     "muyo_cuda_argmax_pairs": (C.c_int, [VP, U32, VP, VP]),
 }

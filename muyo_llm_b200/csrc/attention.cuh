@@ -1,26 +1,29 @@
 // Split-K GQA decode attention over the persistent KV cache (flash-decoding style).
 //
-// Grid (kv_heads, chunks): one CTA per (KV head, 64-key chunk). The CTA stages its K and V tiles
-// in shared memory once (F16 or F32 cache, converted to F32) and serves all `gqa` query heads of
-// the group from them, which is the GQA broadcast of tools/reference_qwen2.py:133 and
-// shaders/llama/mul_mat_vec_base.glsl:55-64 without re-reading K/V per query head. Each CTA writes
-// (max, sum, unnormalised output) per query head; the chunks are merged either by the last CTA of
-// the KV head to finish (a self-resetting arrival counter, used by the fused decode step) or by a
-// separate combine kernel (the op-level entry point, whose workspace may hold anything).
+// Work item (kv head, 64-key chunk): the item stages its K and V tiles in shared memory once (F16 or
+// F32 cache, converted to F32) and serves all `gqa` query heads of the group from them, which is the
+// GQA broadcast of tools/reference_qwen2.py:133 and shaders/llama/mul_mat_vec_base.glsl:55-64
+// without re-reading K/V per query head. Each item writes (max, sum, unnormalised output) per query
+// head; the chunks are merged by the last CTA of the KV head to finish (a self-resetting arrival
+// counter, the fused layer step), by a separate combine kernel (the op-level entry point, whose
+// workspace may hold anything), or by the consumer of the output (the persistent decode kernel).
 //
-// With FUSED the CTA also performs the step's KV append: it rotates the raw key with NeoX RoPE in
+// With FUSED the item also performs the step's KV append: it rotates the raw key with NeoX RoPE in
 // double precision (theta = pos * base^(-2j/hd), the rotation of tools/reference_qwen2.py:84-93,
 // evaluated in float64 as there and rounded once), rounds key and value to the cache type, and the
-// CTA holding the last chunk stores them at row `pos`; that CTA also uses the stored values for
-// key `pos` itself, so every CTA reads only rows the previous steps finished writing.
+// item holding the last chunk stores them at row `pos`; that item also uses the stored values for
+// key `pos` itself, so every item reads only rows that earlier steps finished writing.
+//
+// All loads of data written on the device go through L2 (ld.global.cg): in the persistent kernel the
+// producer of a row can be another SM within the same launch.
 #pragma once
 
 #include "common.cuh"
 
 namespace muyo {
 
-constexpr int kAttnKeys = 64;      // keys per CTA
-constexpr int kAttnThreads = 128;  // 4 warps
+constexpr int kAttnKeys = 64;      // keys per work item
+constexpr int kAttnThreads = 128;  // threads of the standalone attention CTA
 constexpr int kAttnMaxGroup = 16;  // query heads per KV head
 
 struct AttnDev {
@@ -28,6 +31,7 @@ struct AttnDev {
     float scale;
     double rope_base;
     int max_chunks;
+    const double* rope_cs;  // optional [max_seq][hd]: cos theta_j at [pos*hd + j], sin at [pos*hd + hd/2 + j]
 };
 
 template <typename KV>
@@ -35,12 +39,12 @@ __device__ __forceinline__ float kv_load(const KV* p);
 template <>
 __device__ __forceinline__ float kv_load<float>(const float* p)
 {
-    return *p;
+    return __ldcg(p);
 }
 template <>
 __device__ __forceinline__ float kv_load<__half>(const __half* p)
 {
-    return __half2float(*p);
+    return __half2float(__ldcg(p));
 }
 
 template <typename KV>
@@ -54,6 +58,19 @@ template <>
 __device__ __forceinline__ __half kv_round<__half>(float v)
 {
     return __float2half_rn(v);
+}
+
+template <typename KV>
+__device__ __forceinline__ float kv_value(KV v);
+template <>
+__device__ __forceinline__ float kv_value<float>(float v)
+{
+    return v;
+}
+template <>
+__device__ __forceinline__ float kv_value<__half>(__half v)
+{
+    return __half2float(v);
 }
 
 // Rotated pair, as numpy computes x[:half]*c - x[half:]*s and x[:half]*s + x[half:]*c in float64
@@ -72,7 +89,7 @@ __device__ __forceinline__ void rope_cs_f64(int pos, int j, int hd, double base,
     s = sin(theta);
 }
 
-// Shared-memory footprint of the attention CTA (floats).
+// Shared-memory footprint of one work item (floats), excluding the double cos/sin table (hd doubles).
 __host__ __device__ constexpr int attn_smem_floats(int hd, int g)
 {
     return 2 * kAttnKeys * (hd + 1) /* K, V tiles */ + g * hd /* q */ + g * kAttnKeys /* p */ + 2 * g /* m, l */ +
@@ -86,105 +103,115 @@ __device__ __forceinline__ float* part_ptr(float* part, const AttnDev& p, int kv
     return part + ((size_t)(kvh * p.max_chunks + chunk) * p.gqa + g) * (HD + 2);
 }
 
+// Merge of one output element (query head h = kvh*gqa + g, channel d) over nchunks partials.
 template <int HD>
-__device__ void attn_merge(const AttnDev& p, const float* part, int kvh, int nchunks, float* out)
+__device__ __forceinline__ float attn_merge_one(const AttnDev& p, const float* part, int kvh, int g, int d,
+                                                int nchunks)
 {
-    for (int e = threadIdx.x; e < p.gqa * HD; e += blockDim.x) {
-        const int g = e / HD, d = e % HD;
-        float M = -INFINITY;
-        for (int c = 0; c < nchunks; ++c)
-            M = fmaxf(M, part_ptr<HD>(const_cast<float*>(part), p, kvh, c, g)[0]);
-        float L = 0.0f, O = 0.0f;
-        for (int c = 0; c < nchunks; ++c) {
-            const float* q = part_ptr<HD>(const_cast<float*>(part), p, kvh, c, g);
-            if (q[1] > 0.0f) {
-                const float w = expf(q[0] - M);
-                L = fmaf(q[1], w, L);
-                O = fmaf(q[2 + d], w, O);
-            }
+    float M = -INFINITY;
+    for (int c = 0; c < nchunks; ++c)
+        M = fmaxf(M, __ldcg(part_ptr<HD>(const_cast<float*>(part), p, kvh, c, g)));
+    float L = 0.0f, O = 0.0f;
+    for (int c = 0; c < nchunks; ++c) {
+        const float* q = part_ptr<HD>(const_cast<float*>(part), p, kvh, c, g);
+        const float l = __ldcg(q + 1);
+        if (l > 0.0f) {
+            const float w = expf(__ldcg(q) - M);
+            L = fmaf(l, w, L);
+            O = fmaf(__ldcg(q + 2 + d), w, O);
         }
-        out[(size_t)(kvh * p.gqa + g) * HD + d] = __fdiv_rn(O, L);
+    }
+    return __fdiv_rn(O, L);
+}
+
+template <int HD>
+__device__ void attn_merge(const AttnDev& p, const float* part, int kvh, int nchunks, float* out, int tid,
+                           int nthreads)
+{
+    for (int e = tid; e < p.gqa * HD; e += nthreads) {
+        const int g = e / HD, d = e % HD;
+        out[(size_t)(kvh * p.gqa + g) * HD + d] = attn_merge_one<HD>(p, part, kvh, g, d, nchunks);
     }
 }
 
-// q_in: FUSED -> raw projections [heads*hd | kv_heads*hd (k) | kv_heads*hd (v)]; else rotated q.
-template <typename KV, int HD, bool FUSED, bool INLINE_MERGE>
-__global__ void __launch_bounds__(kAttnThreads) k_attention(AttnDev p, const float* __restrict__ q_in,
-                                                             KV* __restrict__ kc, KV* __restrict__ vc,
-                                                             const int32_t* __restrict__ pos_ptr,
-                                                             float* __restrict__ out, float* __restrict__ part,
-                                                             int32_t* __restrict__ counters)
+struct BlockSync {
+    __device__ __forceinline__ void operator()() const { __syncthreads(); }
+};
+
+// One work item (kvh, chunk) of the attention at position `pos`, run by threads tid in [0, nthreads)
+// of a CTA (nthreads a multiple of 32, at least 64). `sm` holds attn_smem_floats(HD, gqa) floats, `cs`
+// HD doubles. When `out` is non-null and the item is the only chunk, the normalised output is written
+// there; otherwise the partial (m, l, o) goes to `part`.
+template <typename KV, int HD, bool FUSED, typename Sync>
+__device__ void attention_item(const AttnDev& p, const float* q_in, KV* kc, KV* vc, int pos, int kvh, int chunk,
+                               float* out, float* part, float* sm, double* cs, int tid, int nthreads, Sync sync)
 {
-    extern __shared__ float sm[];
     constexpr int LD = HD + 1;
     const int G = p.gqa;
-    float* Ks = sm;                          // [kAttnKeys][LD]
-    float* Vs = Ks + kAttnKeys * LD;         // [kAttnKeys][LD]
-    float* Qs = Vs + kAttnKeys * LD;         // [G][HD]
-    float* Ps = Qs + G * HD;                 // [G][kAttnKeys]
-    float* Ms = Ps + G * kAttnKeys;          // [G]
-    float* Ls = Ms + G;                      // [G]
-    float* Kn = Ls + G;                      // [HD] new key (rounded)
-    float* Vn = Kn + HD;                     // [HD] new value (rounded)
-    __shared__ double cs[HD];                // cos at [j], sin at [HD/2 + j]
-    __shared__ int last_flag;
+    float* Ks = sm;                   // [kAttnKeys][LD]
+    float* Vs = Ks + kAttnKeys * LD;  // [kAttnKeys][LD]
+    float* Qs = Vs + kAttnKeys * LD;  // [G][HD]
+    float* Ps = Qs + G * HD;          // [G][kAttnKeys]
+    float* Ms = Ps + G * kAttnKeys;   // [G]
+    float* Ls = Ms + G;               // [G]
+    float* Kn = Ls + G;               // [HD] new key (rounded)
+    float* Vn = Kn + HD;              // [HD] new value (rounded)
 
-    const int kvh = blockIdx.x, chunk = blockIdx.y;
-    const int pos = pos_ptr ? *pos_ptr : p.n_keys_fixed - 1;
-    if (pos < 0 || pos >= p.max_seq)
-        return;  // a device position outside the cache: nothing is read or written
     const int n = pos + 1;
     const int nchunks = (n + kAttnKeys - 1) / kAttnKeys;
-    if (chunk >= nchunks)
-        return;
     const int key0 = chunk * kAttnKeys;
     const int nk = min(kAttnKeys, n - key0);
     const size_t head_base = (size_t)kvh * p.max_seq * HD;
     const bool holds_new = FUSED && (chunk == nchunks - 1);
 
     if (FUSED) {
-        if (threadIdx.x < HD / 2) {
+        for (int j = tid; j < HD / 2; j += nthreads) {
             double c, s;
-            rope_cs_f64(pos, threadIdx.x, HD, p.rope_base, c, s);
-            cs[threadIdx.x] = c;
-            cs[HD / 2 + threadIdx.x] = s;
+            if (p.rope_cs) {
+                c = __ldg(p.rope_cs + (size_t)pos * HD + j);
+                s = __ldg(p.rope_cs + (size_t)pos * HD + HD / 2 + j);
+            } else {
+                rope_cs_f64(pos, j, HD, p.rope_base, c, s);
+            }
+            cs[j] = c;
+            cs[HD / 2 + j] = s;
         }
-        __syncthreads();
+        sync();
         const int qd = p.heads * HD, kvd = p.kv_heads * HD;
-        for (int e = threadIdx.x; e < G * (HD / 2); e += blockDim.x) {
+        for (int e = tid; e < G * (HD / 2); e += nthreads) {
             const int g = e / (HD / 2), j = e % (HD / 2);
             const float* qh = q_in + (size_t)(kvh * G + g) * HD;
             float y0, y1;
-            rope_pair_f64(qh[j], qh[j + HD / 2], cs[j], cs[HD / 2 + j], y0, y1);
+            rope_pair_f64(__ldcg(qh + j), __ldcg(qh + j + HD / 2), cs[j], cs[HD / 2 + j], y0, y1);
             Qs[g * HD + j] = y0;
             Qs[g * HD + j + HD / 2] = y1;
         }
         if (holds_new) {
             const float* kr = q_in + qd + (size_t)kvh * HD;
             const float* vr = q_in + qd + kvd + (size_t)kvh * HD;
-            for (int j = threadIdx.x; j < HD / 2; j += blockDim.x) {
+            for (int j = tid; j < HD / 2; j += nthreads) {
                 float y0, y1;
-                rope_pair_f64(kr[j], kr[j + HD / 2], cs[j], cs[HD / 2 + j], y0, y1);
+                rope_pair_f64(__ldcg(kr + j), __ldcg(kr + j + HD / 2), cs[j], cs[HD / 2 + j], y0, y1);
                 const KV k0 = kv_round<KV>(y0), k1 = kv_round<KV>(y1);
                 kc[head_base + (size_t)pos * HD + j] = k0;
                 kc[head_base + (size_t)pos * HD + j + HD / 2] = k1;
-                Kn[j] = kv_load<KV>(&k0);
-                Kn[j + HD / 2] = kv_load<KV>(&k1);
+                Kn[j] = kv_value<KV>(k0);
+                Kn[j + HD / 2] = kv_value<KV>(k1);
             }
-            for (int d = threadIdx.x; d < HD; d += blockDim.x) {
-                const KV v0 = kv_round<KV>(vr[d]);
+            for (int d = tid; d < HD; d += nthreads) {
+                const KV v0 = kv_round<KV>(__ldcg(vr + d));
                 vc[head_base + (size_t)pos * HD + d] = v0;
-                Vn[d] = kv_load<KV>(&v0);
+                Vn[d] = kv_value<KV>(v0);
             }
         }
     } else {
-        for (int e = threadIdx.x; e < G * HD; e += blockDim.x)
-            Qs[e] = q_in[(size_t)kvh * G * HD + e];
+        for (int e = tid; e < G * HD; e += nthreads)
+            Qs[e] = __ldcg(q_in + (size_t)kvh * G * HD + e);
     }
-    __syncthreads();  // Kn / Vn are read by other threads below
+    sync();  // Kn / Vn / Qs are read by other threads below
 
     // Stage the K and V tiles (keys that earlier steps wrote; the new key comes from Kn/Vn).
-    for (int e = threadIdx.x; e < kAttnKeys * HD; e += blockDim.x) {
+    for (int e = tid; e < kAttnKeys * HD; e += nthreads) {
         const int t = e / HD, d = e % HD;
         const int j = key0 + t;
         float kv = 0.0f, vv = 0.0f;
@@ -200,27 +227,29 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnDev p, const flo
         Ks[t * LD + d] = kv;
         Vs[t * LD + d] = vv;
     }
-    __syncthreads();
+    sync();
 
-    // Scores: thread (t, half) computes keys t for group members g = half, half + 2, ...
+    // Scores: thread (t, h0) computes key t for group members g = h0, h0 + hs, ...
     {
-        const int t = threadIdx.x % kAttnKeys, h0 = threadIdx.x / kAttnKeys, hs = kAttnThreads / kAttnKeys;
-        for (int g = h0; g < G; g += hs) {
-            float s = -INFINITY;
-            if (t < nk) {
-                float dot = 0.0f;
+        const int t = tid % kAttnKeys, h0 = tid / kAttnKeys, hs = nthreads / kAttnKeys;
+        if (h0 < hs) {
+            for (int g = h0; g < G; g += hs) {
+                float s = -INFINITY;
+                if (t < nk) {
+                    float dot = 0.0f;
 #pragma unroll 16
-                for (int d = 0; d < HD; ++d)
-                    dot = fmaf(Qs[g * HD + d], Ks[t * LD + d], dot);
-                s = dot * p.scale;
+                    for (int d = 0; d < HD; ++d)
+                        dot = fmaf(Qs[g * HD + d], Ks[t * LD + d], dot);
+                    s = dot * p.scale;
+                }
+                Ps[g * kAttnKeys + t] = s;
             }
-            Ps[g * kAttnKeys + t] = s;
         }
     }
-    __syncthreads();
+    sync();
     // Softmax statistics per group member: one warp per member.
     {
-        const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = kAttnThreads / 32;
+        const int lane = tid & 31, warp = tid >> 5, nw = nthreads / 32;
         for (int g = warp; g < G; g += nw) {
             float m = -INFINITY;
             for (int t = lane; t < kAttnKeys; t += 32)
@@ -240,10 +269,10 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnDev p, const flo
             }
         }
     }
-    __syncthreads();
+    sync();
     // Unnormalised P.V for this chunk.
-    const bool single = nchunks == 1;
-    for (int e = threadIdx.x; e < G * HD; e += blockDim.x) {
+    const bool single = out != nullptr && nchunks == 1;
+    for (int e = tid; e < G * HD; e += nthreads) {
         const int g = e / HD, d = e % HD;
         float o = 0.0f;
         for (int t = 0; t < nk; ++t)
@@ -259,7 +288,29 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnDev p, const flo
             }
         }
     }
-    if (single || !INLINE_MERGE)
+}
+
+// Standalone attention: grid (kv_heads, max_chunks), CTAs past the current chunk count exit.
+template <typename KV, int HD, bool FUSED, bool INLINE_MERGE>
+__global__ void __launch_bounds__(kAttnThreads) k_attention(AttnDev p, const float* __restrict__ q_in,
+                                                             KV* __restrict__ kc, KV* __restrict__ vc,
+                                                             const int32_t* __restrict__ pos_ptr,
+                                                             float* __restrict__ out, float* __restrict__ part,
+                                                             int32_t* __restrict__ counters)
+{
+    extern __shared__ float sm[];
+    __shared__ double cs[HD];
+    __shared__ int last_flag;
+    const int kvh = blockIdx.x, chunk = blockIdx.y;
+    const int pos = pos_ptr ? __ldcg(pos_ptr) : p.n_keys_fixed - 1;
+    if (pos < 0 || pos >= p.max_seq)
+        return;  // a device position outside the cache: nothing is read or written
+    const int nchunks = (pos + 1 + kAttnKeys - 1) / kAttnKeys;
+    if (chunk >= nchunks)
+        return;
+    attention_item<KV, HD, FUSED>(p, q_in, kc, vc, pos, kvh, chunk, out, part, sm, cs, threadIdx.x, blockDim.x,
+                                  BlockSync{});
+    if (nchunks == 1 || !INLINE_MERGE)
         return;
     // Last CTA of this KV head merges the chunks, then re-arms the counter for the next launch.
     __threadfence();
@@ -272,7 +323,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnDev p, const flo
     if (!last_flag)
         return;
     __threadfence();
-    attn_merge<HD>(p, part, kvh, nchunks, out);
+    attn_merge<HD>(p, part, kvh, nchunks, out, threadIdx.x, blockDim.x);
     if (threadIdx.x == 0)
         counters[kvh] = 0;
 }
@@ -283,13 +334,13 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention_combine(AttnDev p, c
                                                                      float* __restrict__ out)
 {
     const int kvh = blockIdx.x;
-    const int pos = pos_ptr ? *pos_ptr : p.n_keys_fixed - 1;
+    const int pos = pos_ptr ? __ldcg(pos_ptr) : p.n_keys_fixed - 1;
     if (pos < 0 || pos >= p.max_seq)
         return;
     const int nchunks = (pos + 1 + kAttnKeys - 1) / kAttnKeys;
     if (nchunks <= 1)
         return;  // the single chunk wrote its output directly
-    attn_merge<HD>(p, part, kvh, nchunks, out);
+    attn_merge<HD>(p, part, kvh, nchunks, out, threadIdx.x, blockDim.x);
 }
 
 }  // namespace muyo

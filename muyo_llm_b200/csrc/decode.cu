@@ -8,6 +8,7 @@
 //   k_gemv<NORM, SWIGLU>           rms_norm -> gate and up GEMVs (one pass, two matrices) -> SwiGLU
 //   k_gemv<PLAIN, RESIDUAL>        down_proj GEMV (K split across warps) + residual add
 //   k_gemv<NORM, LOGITS>           final rms_norm -> LM head GEMV -> logits, argmax, next token
+#include <algorithm>
 #include <climits>
 #include <cmath>
 #include <cstring>
@@ -21,13 +22,6 @@
 #include "gemv.cuh"
 
 namespace muyo {
-
-constexpr int kGemvThreads = 256;  // 8 warps
-constexpr int kGemvWarps = kGemvThreads / 32;
-
-enum Prologue { PRO_PLAIN = 0, PRO_NORM = 1, PRO_EMBED_NORM = 2 };
-enum Epilogue { EPI_BIAS = 1, EPI_RESIDUAL = 2, EPI_SWIGLU = 3, EPI_LOGITS = 4 };
-
 struct Pair {
     float v;
     int i;
@@ -41,6 +35,17 @@ struct Control {
     int32_t total;       // tokens[] is written for positions < total
     int32_t greedy;      // the last step's raw argmax
 };
+}  // namespace muyo
+
+#include "decode_persistent.cuh"
+
+namespace muyo {
+
+constexpr int kGemvThreads = 256;  // 8 warps
+constexpr int kGemvWarps = kGemvThreads / 32;
+
+enum Prologue { PRO_PLAIN = 0, PRO_NORM = 1, PRO_EMBED_NORM = 2 };
+enum Epilogue { EPI_BIAS = 1, EPI_RESIDUAL = 2, EPI_SWIGLU = 3, EPI_LOGITS = 4 };
 
 struct GemvFused {
     // prologue
@@ -259,6 +264,7 @@ struct Shape {
     float eps, rope_base;
     bool kv_f16;
     int max_chunks;
+    const double* rope_cs;  // optional device (cos, sin) table [max_seq][head_dim] (the model's)
 };
 
 static int make_shape(const MuyoQwen2Config* c, Shape& s, bool need_vocab)
@@ -350,7 +356,7 @@ static int launch_attention_fused(const Shape& s, const float* qkv, void* kc, vo
                                   float* out, float* part, int32_t* counters, cudaStream_t st)
 {
     AttnDev p{s.heads, s.kv_heads, s.gqa, s.max_seq, 0, 1.0f / sqrtf((float)s.head_dim), (double)s.rope_base,
-              s.max_chunks};
+              s.max_chunks, s.rope_cs};
     const size_t smem = (size_t)attn_smem_floats(HD, s.gqa) * sizeof(float);
     auto k = k_attention<KV, HD, true, true>;
     if (smem > 48 * 1024)
@@ -487,10 +493,16 @@ struct MuyoModel {
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     cudaStream_t cap_stream = nullptr;
-    int32_t* pinned = nullptr;  // host staging for control/prompt/output
+    int32_t* pinned = nullptr;  // host staging for prompt/output (generate/step synchronise before reuse)
     size_t pinned_ints = 0;
     int32_t host_pos = 0;
     bool finalized = false;
+    int engine = 0;                 // 0: persistent kernel, 1: CUDA graph of per-phase kernels
+    double* rope_cs = nullptr;      // [max_seq][head_dim] cos/sin table (float64)
+    muyo::PLayer* d_layers = nullptr;
+    unsigned* bar = nullptr;        // persistent kernel grid-barrier counter
+    int* err = nullptr;             // persistent kernel error word
+    int p_slots = 0, p_slot_bytes = 0, p_region_b = 0, p_smem = 0, p_grid = 0;
 };
 
 namespace muyo {
@@ -554,6 +566,117 @@ static int record_step(MuyoModel* m, cudaStream_t st)
     return launch_gemv<2, 4, 1, 1, PRO_NORM, EPI_LOGITS>(a, m->lm_grid, st);
 }
 
+// ---- persistent engine ----------------------------------------------------------------------------
+
+constexpr int kSmemLimit = 227 * 1024;
+
+static size_t round16(size_t n) { return (n + 15) / 16 * 16; }
+
+// Shared-memory plan of the persistent kernel: a ring of weight slots, region B (the staged input
+// vector, or one attention work item), the cos/sin row, reduction scratch and the mbarriers.
+static int persistent_plan(MuyoModel* m)
+{
+    const Shape& s = m->s;
+    const size_t x_bytes = sizeof(float) * (size_t)std::max(std::max(s.hidden, s.q_dim), s.ffn);
+    const size_t attn_bytes = sizeof(float) * (size_t)attn_smem_floats(s.head_dim, s.gqa);
+    const size_t region_b = round16(std::max(x_bytes, attn_bytes));
+    const size_t min_slot = std::max(std::max((size_t)4 * s.hidden, (size_t)2 * s.q_dim), (size_t)2 * s.ffn);
+    const size_t slot = round16(std::max(min_slot, std::max((size_t)6 * s.ffn, (size_t)32 * s.hidden)));
+    const size_t misc = sizeof(double) * s.head_dim + 32 * sizeof(float) + 32 * sizeof(Pair) +
+                        2 * kMaxSlots * sizeof(uint64_t) + 128;
+    if (region_b + misc + 2 * slot > (size_t)kSmemLimit) {
+        set_error("persistent engine: shapes need %zu bytes of shared memory for two slots", region_b + misc + 2 * slot);
+        return MUYO_EUNSUPPORTED;
+    }
+    const int slots = (int)std::min<size_t>(kMaxSlots, ((size_t)kSmemLimit - region_b - misc) / slot);
+    m->p_slots = slots;
+    m->p_slot_bytes = (int)slot;
+    m->p_region_b = (int)region_b;
+    m->p_smem = (int)((size_t)slots * slot + region_b + misc);
+    return MUYO_OK;
+}
+
+template <typename KV, int HD>
+static int launch_persistent_t(MuyoModel* m, int n_steps, cudaStream_t st)
+{
+    const Shape& s = m->s;
+    auto k = k_decode_persistent<KV, HD>;
+    if (m->p_grid == 0) {
+        MUYO_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, m->p_smem));
+        int per_sm = 0;
+        MUYO_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kPThreads, m->p_smem));
+        if (per_sm < 1) {
+            set_error("persistent engine: the kernel does not fit on an SM (%d bytes of shared memory)", m->p_smem);
+            return MUYO_EUNSUPPORTED;
+        }
+        m->p_grid = sm_count();
+    }
+    PArgs a{};
+    a.layers = m->d_layers;
+    a.L = s.layers;
+    a.embd = W(m, "token_embd.weight");
+    a.lm = W(m, m->tied_output ? "token_embd.weight" : "output.weight");
+    a.final_norm = F(m, "output_norm.weight");
+    a.H = s.hidden;
+    a.F = s.ffn;
+    a.V = s.vocab;
+    a.QKV = s.qkv_rows;
+    a.QD = s.q_dim;
+    a.KVD = s.kv_dim;
+    a.heads = s.heads;
+    a.kv_heads = s.kv_heads;
+    a.gqa = s.gqa;
+    a.hd = s.head_dim;
+    a.max_seq = s.max_seq;
+    a.eps = s.eps;
+    a.attn = AttnDev{s.heads, s.kv_heads, s.gqa, s.max_seq, 0, 1.0f / sqrtf((float)s.head_dim), (double)s.rope_base,
+                     s.max_chunks, m->rope_cs};
+    a.kc = m->kc;
+    a.vc = m->vc;
+    a.kv_layer_elems = (long long)(m->kv_layer_bytes / (s.kv_f16 ? 2 : 4));
+    a.h = m->h;
+    a.h1 = m->ls.h1;
+    a.qkv = m->ls.qkv;
+    a.act = m->ls.act;
+    a.logits = m->logits;
+    a.attn_part = m->ls.part;
+    a.lm_part = m->lm_part;
+    a.ctrl = m->ctrl;
+    a.tokens = m->tokens;
+    a.bar = m->bar;
+    a.err = m->err;
+    a.n_steps = n_steps;
+    a.slots = m->p_slots;
+    a.slot_bytes = m->p_slot_bytes;
+    a.region_b_bytes = m->p_region_b;
+    MUYO_CUDA_TRY(cudaMemsetAsync(m->bar, 0, sizeof(unsigned), st));
+    void* args[] = {&a};
+    MUYO_CUDA_TRY(cudaLaunchCooperativeKernel((const void*)k, dim3(m->p_grid), dim3(kPThreads), args, (size_t)m->p_smem,
+                                              st));
+    return MUYO_OK;
+}
+
+static int launch_persistent(MuyoModel* m, int n_steps, cudaStream_t st)
+{
+    const Shape& s = m->s;
+    if (s.kv_f16) {
+        switch (s.head_dim) {
+            case 16: return launch_persistent_t<__half, 16>(m, n_steps, st);
+            case 32: return launch_persistent_t<__half, 32>(m, n_steps, st);
+            case 64: return launch_persistent_t<__half, 64>(m, n_steps, st);
+            default: return launch_persistent_t<__half, 128>(m, n_steps, st);
+        }
+    }
+    switch (s.head_dim) {
+        case 16: return launch_persistent_t<float, 16>(m, n_steps, st);
+        case 32: return launch_persistent_t<float, 32>(m, n_steps, st);
+        case 64: return launch_persistent_t<float, 64>(m, n_steps, st);
+        default: return launch_persistent_t<float, 128>(m, n_steps, st);
+    }
+}
+
+__global__ void k_set_control(Control* c, Control v) { *c = v; }
+
 }  // namespace muyo
 
 using namespace muyo;
@@ -611,7 +734,7 @@ static int launch_attention_op(const MuyoAttentionParams* q, const float* qv, co
                                const int32_t* pos, float* out, float* part, cudaStream_t st)
 {
     AttnDev p{(int)q->heads, (int)q->kv_heads, (int)(q->heads / q->kv_heads), (int)q->max_seq, (int)q->n_keys,
-              q->scale, 0.0, (int)((q->max_seq + kAttnKeys - 1) / kAttnKeys)};
+              q->scale, 0.0, (int)((q->max_seq + kAttnKeys - 1) / kAttnKeys), nullptr};
     const size_t smem = (size_t)attn_smem_floats(HD, p.gqa) * sizeof(float);
     auto k = k_attention<KV, HD, false, false>;
     if (smem > 48 * 1024)
@@ -741,6 +864,8 @@ static void free_model(MuyoModel* m)
         cudaGraphDestroy(m->graph);
     if (m->cap_stream)
         cudaStreamDestroy(m->cap_stream);
+    cudaFree(m->rope_cs);
+    cudaFree(m->d_layers);
     cudaFree(m->arena);
     cudaFree(m->kc);
     cudaFree(m->vc);
@@ -800,7 +925,8 @@ extern "C" int muyo_model_create(const MuyoQwen2Config* c, int device, MuyoModel
     m->lm_grid = sm_count() * 8;
     const size_t scratch_bytes = layer_scratch_bytes(s) + align256(sizeof(float) * H) + align256(sizeof(float) * V) +
                                  align256(sizeof(Pair) * m->lm_grid) + align256(sizeof(int32_t)) +
-                                 align256(sizeof(Control)) + align256(sizeof(int32_t) * s.max_seq);
+                                 align256(sizeof(Control)) + align256(sizeof(int32_t) * s.max_seq) +
+                                 align256(sizeof(unsigned)) + align256(sizeof(int));
     if (e == cudaSuccess)
         e = cudaMalloc(&m->scratch, scratch_bytes);
     if (e == cudaSuccess)
@@ -833,6 +959,10 @@ extern "C" int muyo_model_create(const MuyoQwen2Config* c, int device, MuyoModel
     m->ctrl = reinterpret_cast<Control*>(p);
     p += align256(sizeof(Control));
     m->tokens = reinterpret_cast<int32_t*>(p);
+    p += align256(sizeof(int32_t) * s.max_seq);
+    m->bar = reinterpret_cast<unsigned*>(p);
+    p += align256(sizeof(unsigned));
+    m->err = reinterpret_cast<int*>(p);
     *out = m;
     return MUYO_OK;
 }
@@ -920,6 +1050,34 @@ extern "C" int muyo_model_finalize(MuyoModel* m, void* stream)
         MUYO_REQUIRE(kv.second.set, "finalize: tensor %s was never set", n.c_str());
     }
     (void)stream;
+    const Shape& s = m->s;
+    // (cos, sin) of theta = pos * base^(-2j/hd) in float64 (tools/reference_qwen2.py:88-89), per position.
+    if (!m->rope_cs) {
+        std::vector<double> cs((size_t)s.max_seq * s.head_dim);
+        for (int pos = 0; pos < s.max_seq; ++pos)
+            for (int j = 0; j < s.head_dim / 2; ++j) {
+                const double theta = (double)pos * std::pow((double)s.rope_base, -2.0 * j / s.head_dim);
+                cs[(size_t)pos * s.head_dim + j] = std::cos(theta);
+                cs[(size_t)pos * s.head_dim + s.head_dim / 2 + j] = std::sin(theta);
+            }
+        MUYO_CUDA_TRY(cudaMalloc(&m->rope_cs, cs.size() * sizeof(double)));
+        MUYO_CUDA_TRY(cudaMemcpy(m->rope_cs, cs.data(), cs.size() * sizeof(double), cudaMemcpyHostToDevice));
+        m->s.rope_cs = m->rope_cs;
+    }
+    std::vector<PLayer> pl(s.layers);
+    for (int l = 0; l < s.layers; ++l) {
+        const LayerPtrs w = layer_ptrs(m, l);
+        pl[l] = PLayer{w.wqkv, w.bqkv, w.attn_norm, w.wo, w.ffn_norm, w.wgate, w.wup, w.wdown};
+    }
+    if (!m->d_layers)
+        MUYO_CUDA_TRY(cudaMalloc(&m->d_layers, sizeof(PLayer) * s.layers));
+    MUYO_CUDA_TRY(cudaMemcpy(m->d_layers, pl.data(), sizeof(PLayer) * s.layers, cudaMemcpyHostToDevice));
+    {
+        const int rc = persistent_plan(m);
+        if (rc)
+            return rc;
+        m->p_grid = 0;
+    }
     if (m->exec) {
         cudaGraphExecDestroy(m->exec);
         m->exec = nullptr;
@@ -962,13 +1120,33 @@ extern "C" int muyo_model_reset(MuyoModel* m, void* stream)
 // forced up to `prompt_end`, and replays the step graph n_steps times.
 static int run_steps(MuyoModel* m, int prompt_end, int total, int n_steps, cudaStream_t st)
 {
-    Control c{m->host_pos, prompt_end, total, 0};
-    int32_t* staging = m->pinned + m->pinned_ints - 8;
-    std::memcpy(staging, &c, sizeof(c));
-    MUYO_CUDA_TRY(cudaMemcpyAsync(m->ctrl, staging, sizeof(Control), cudaMemcpyHostToDevice, st));
-    for (int i = 0; i < n_steps; ++i)
-        MUYO_CUDA_TRY(cudaGraphLaunch(m->exec, st));
+    k_set_control<<<1, 1, 0, st>>>(m->ctrl, Control{m->host_pos, prompt_end, total, 0});
+    MUYO_LAUNCH_CHECK();
+    if (m->engine == 0) {
+        const int rc = launch_persistent(m, n_steps, st);
+        if (rc)
+            return rc;
+    } else {
+        for (int i = 0; i < n_steps; ++i)
+            MUYO_CUDA_TRY(cudaGraphLaunch(m->exec, st));
+    }
     m->host_pos += n_steps;
+    return MUYO_OK;
+}
+
+// Error word of the persistent kernel (read after a synchronisation); clears it.
+static int check_device_error(MuyoModel* m, cudaStream_t st)
+{
+    if (m->engine != 0)
+        return MUYO_OK;
+    int e = 0;
+    MUYO_CUDA_TRY(cudaMemcpyAsync(&e, m->err, sizeof(int), cudaMemcpyDeviceToHost, st));
+    MUYO_CUDA_TRY(cudaStreamSynchronize(st));
+    if (e != 0) {
+        MUYO_CUDA_TRY(cudaMemsetAsync(m->err, 0, sizeof(int), st));
+        set_error("decode: a bounded device wait expired in the persistent kernel (error word %d)", e);
+        return MUYO_ETIMEOUT;
+    }
     return MUYO_OK;
 }
 
@@ -1034,7 +1212,7 @@ extern "C" int muyo_model_generate(MuyoModel* m, const int32_t* prompt, int n_pr
     MUYO_CUDA_TRY(cudaStreamSynchronize(st));
     if (n_predict > 0)
         std::memcpy(out_tokens, m->pinned, sizeof(int32_t) * n_predict);
-    return MUYO_OK;
+    return check_device_error(m, st);
 }
 
 extern "C" int muyo_model_step(MuyoModel* m, int32_t token, float* logits, int32_t* next_token, void* stream)
@@ -1058,7 +1236,7 @@ extern "C" int muyo_model_step(MuyoModel* m, int32_t token, float* logits, int32
     MUYO_CUDA_TRY(cudaStreamSynchronize(st));
     if (next_token)
         *next_token = m->pinned[1];
-    return MUYO_OK;
+    return check_device_error(m, st);
 }
 
 extern "C" int muyo_model_position(const MuyoModel* m, int32_t* pos)
@@ -1107,4 +1285,18 @@ extern "C" int muyo_model_destroy(MuyoModel* m)
         free_model(m);
     }
     return MUYO_OK;
+}
+
+extern "C" int muyo_model_set_option(MuyoModel* m, const char* key, int value)
+{
+    clear_error();
+    MUYO_REQUIRE(m && key, "set_option: null argument");
+    const std::string k(key);
+    if (k == "engine") {
+        MUYO_REQUIRE(value == 0 || value == 1, "set_option: engine must be 0 (persistent) or 1 (graph)");
+        m->engine = value;
+        return MUYO_OK;
+    }
+    MUYO_REQUIRE(false, "set_option: unknown option %s", key);
+    return MUYO_EINVAL;
 }

@@ -23,8 +23,10 @@ def config_struct(cfg: Qwen2Config, kv_dtype: int) -> _abi.Qwen2Config:
 class Qwen2Model:
     """A device-resident Qwen2 model with its KV cache (``kv_dtype``: ``_abi.KV_F16`` or ``KV_F32``)."""
 
+    ENGINE_PERSISTENT, ENGINE_GRAPH = 0, 1
+
     def __init__(self, cfg: Qwen2Config, tensors: dict | None = None, gguf_path: str | None = None,
-                 kv_dtype: int = _abi.KV_F16, device: int = 0):
+                 kv_dtype: int = _abi.KV_F16, device: int = 0, engine: int = 0):
         self.cfg = cfg
         self.kv_dtype = kv_dtype
         self._cfg = config_struct(cfg, kv_dtype)
@@ -40,6 +42,7 @@ class Qwen2Model:
                         continue  # tied LM head: the model reads token_embd.weight
                     a = np.ascontiguousarray(arr)
                     _abi.call("muyo_model_set_tensor", self._m, name.encode(), a.ctypes.data, a.nbytes)
+            _abi.call("muyo_model_set_option", self._m, b"engine", engine)
             _abi.call("muyo_model_finalize", self._m, None)
         except Exception:
             self.close()

@@ -150,18 +150,40 @@ def make_full(ref: str) -> None:
     print("[golden] wrote qwen2_05b_greedy.json", file=sys.stderr)
 
 
+def make_full_f16() -> None:
+    """Adds the oracle's greedy ids with the F16 KV cache BASELINE names (keys after RoPE and values
+    rounded to F16 at append) to the 0.5B fixture. The reference forward keeps an F32 cache
+    (tools/reference_qwen2.py:127-130), so this sequence is the oracle's, pinned by the F32 run above."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+
+    path = os.path.join(HERE, "qwen2_05b_greedy.json")
+    doc = json.load(open(path))
+    cfg = synth.QWEN2_05B
+    model = synth.make_model(cfg, doc["seed"])
+    seq, margins = oracle.qwen2_greedy(cfg, model, doc["prompt"], doc["n_prompt"] + doc["n_predict"], kv_f16=True)
+    doc["oracle_kv_f16_generated"] = [int(i) for i in seq[doc["n_prompt"]:]]
+    doc["oracle_kv_f16_top2_margin"] = [float(m) for m in margins]
+    with open(path, "w") as f:
+        json.dump(doc, f, indent=1)
+    print("[golden] added the F16-cache oracle ids to qwen2_05b_greedy.json", file=sys.stderr)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference/tools/reference_qwen2.py")
     ap.add_argument("--tiny", action="store_true")
     ap.add_argument("--full", action="store_true")
+    ap.add_argument("--full-f16", action="store_true")
     a = ap.parse_args()
-    if not (a.tiny or a.full):
-        a.tiny = a.full = True
+    if not (a.tiny or a.full or a.full_f16):
+        a.tiny = a.full = a.full_f16 = True
     if a.tiny:
         make_tiny(a.ref)
     if a.full:
         make_full(a.ref)
+    if a.full_f16:
+        make_full_f16()
 
 
 if __name__ == "__main__":

@@ -30,9 +30,13 @@ def tiny():
     return g, synth.make_model(synth.QWEN2_TINY, int(g["seed"]))
 
 
-def test_tiny_matches_reference_forward(cuda, tiny):
+ENGINES = [engine.Qwen2Model.ENGINE_PERSISTENT, engine.Qwen2Model.ENGINE_GRAPH]
+
+
+@pytest.mark.parametrize("eng", ENGINES)
+def test_tiny_matches_reference_forward(cuda, tiny, eng):
     g, t = tiny
-    m = engine.Qwen2Model(synth.QWEN2_TINY, t, kv_dtype=_abi.KV_F32)
+    m = engine.Qwen2Model(synth.QWEN2_TINY, t, kv_dtype=_abi.KV_F32, engine=eng)
     for step, tok in enumerate(g["ids"]):
         arg, logits = m.step(int(tok))
         assert arg == g["argmax"][step], f"step {step}"
@@ -43,10 +47,11 @@ def test_tiny_matches_reference_forward(cuda, tiny):
     m.close()
 
 
+@pytest.mark.parametrize("eng", ENGINES)
 @pytest.mark.parametrize("kv_dtype", [_abi.KV_F32, _abi.KV_F16])
-def test_generate_equals_stepwise(cuda, tiny, kv_dtype):
+def test_generate_equals_stepwise(cuda, tiny, kv_dtype, eng):
     g, t = tiny
-    m = engine.Qwen2Model(synth.QWEN2_TINY, t, kv_dtype=kv_dtype)
+    m = engine.Qwen2Model(synth.QWEN2_TINY, t, kv_dtype=kv_dtype, engine=eng)
     prompt = [int(i) for i in g["ids"][:5]]
     gen = m.generate(prompt, 20)
     m.reset()
@@ -111,9 +116,10 @@ def full():
 
 
 @pytest.mark.skipif(not os.path.exists(FULL), reason="0.5B golden fixture not generated")
-def test_05b_greedy_bit_identical_to_reference(cuda, full):
+@pytest.mark.parametrize("eng", ENGINES)
+def test_05b_greedy_bit_identical_to_reference(cuda, full, eng):
     doc, t = full
-    m = engine.Qwen2Model(synth.QWEN2_05B, t, kv_dtype=_abi.KV_F32)
+    m = engine.Qwen2Model(synth.QWEN2_05B, t, kv_dtype=_abi.KV_F32, engine=eng)
     gen = m.generate(doc["prompt"], doc["n_predict"])
     mism = [i for i, (a, b) in enumerate(zip(gen, doc["generated"])) if a != b]
     assert not mism, f"first mismatch at generated[{mism[0]}]: {gen[mism[0]]} vs {doc['generated'][mism[0]]}"
@@ -121,9 +127,10 @@ def test_05b_greedy_bit_identical_to_reference(cuda, full):
 
 
 @pytest.mark.skipif(not os.path.exists(FULL), reason="0.5B golden fixture not generated")
-def test_05b_f16_cache(cuda, full, oracle_mod):
+@pytest.mark.parametrize("eng", ENGINES)
+def test_05b_f16_cache(cuda, full, oracle_mod, eng):
     doc, t = full
-    m = engine.Qwen2Model(synth.QWEN2_05B, t, kv_dtype=_abi.KV_F16)
+    m = engine.Qwen2Model(synth.QWEN2_05B, t, kv_dtype=_abi.KV_F16, engine=eng)
     if "oracle_kv_f16_generated" in doc:
         gen = m.generate(doc["prompt"], doc["n_predict"])
         assert list(gen) == doc["oracle_kv_f16_generated"]
@@ -137,3 +144,22 @@ def test_05b_f16_cache(cuda, full, oracle_mod):
         assert arg == oarg
         assert_rel_close(logits, ologits, 1e-3, f"step {step} logits")
     m.close()
+
+
+@pytest.mark.parametrize("kv_dtype", [_abi.KV_F32, _abi.KV_F16])
+def test_engines_agree_on_05b_arch(cuda, kv_dtype):
+    """Persistent and graph engines: identical greedy ids and near-identical logits on the 0.5B
+    architecture (independent of the golden fixture)."""
+    cfg = synth.QWEN2_05B
+    t = synth.make_model(cfg, 99)
+    prompt = [int(i) for i in synth.prompt_ids(99, 12, cfg.vocab)]
+    outs = []
+    for eng in ENGINES:
+        m = engine.Qwen2Model(cfg, t, kv_dtype=kv_dtype, engine=eng)
+        gen = m.generate(prompt, 40)
+        m.reset()
+        _, logits = m.step(prompt[0])
+        outs.append((list(gen), logits))
+        m.close()
+    assert outs[0][0] == outs[1][0]
+    assert_rel_close(outs[0][1], outs[1][1], 1e-4, "step-0 logits, persistent vs graph")
