@@ -287,10 +287,11 @@ int muyo_model_position(const MuyoModel* m, int32_t* pos);
 /* Device pointers of the model's buffers, for tests: "logits", "hidden", "k_cache", "v_cache". */
 int muyo_model_buffer(MuyoModel* m, const char* name, void** ptr, size_t* bytes);
 int muyo_model_destroy(MuyoModel* m);
-/* Engine options: "engine" = 0 runs every decode step of a generate call in one persistent
- * cooperative kernel (weights streamed into shared memory ahead of the activation dependencies;
- * the default), 1 replays the per-phase kernels of muyo_cuda_layer_step as a CUDA graph per step.
- * Both compute the same arithmetic in the same order. */
+/* Engine options: "engine" = 1 (the default) replays the per-phase kernels of muyo_cuda_layer_step
+ * as a CUDA graph per decode step; 0 runs every decode step of a generate call in one persistent
+ * cooperative kernel (a producer warp streams weight tiles into shared memory ahead of the
+ * activation dependencies, consumer warps meet at bounded grid barriers). Both compute the same
+ * arithmetic; they differ only in F32 reduction order (last-bit differences). */
 int muyo_model_set_option(MuyoModel* m, const char* key, int value);
 
 /* ---- row-sharded GEMV + cross-GPU greedy (multi-GPU LM head) --------------------------------------

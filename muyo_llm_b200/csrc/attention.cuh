@@ -134,6 +134,60 @@ __device__ void attn_merge(const AttnDev& p, const float* part, int kvh, int nch
     }
 }
 
+// Merge of every query head's partials into a vector (e.g. the staged input of the O projection):
+// out_at(e) receives element e = head * HD + d. Two batched passes over the partials: the
+// statistics (m, l) of every (head, chunk) into shared scratch and from them per-chunk weights
+// w_c = exp(m_c - M) / L; then o = sum_c o_c[d] w_c. `scratch` holds 2 * heads * nchunks floats.
+template <int HD, typename Sync, typename Out>
+__device__ void attn_merge_all(const AttnDev& p, const float* part, int nchunks, float* scratch, int tid, int nthreads,
+                               Sync sync, Out out_at)
+{
+    const int heads = p.kv_heads * p.gqa;
+    float* mw = scratch;                     // [heads][nchunks]: m, then the weight
+    float* lw = scratch + heads * nchunks;   // [heads][nchunks]: l
+    for (int i = tid; i < heads * nchunks; i += nthreads) {
+        const int h = i / nchunks, c = i % nchunks;
+        const float* q = part_ptr<HD>(const_cast<float*>(part), p, h / p.gqa, c, h % p.gqa);
+        mw[i] = __ldcg(q);
+        lw[i] = __ldcg(q + 1);
+    }
+    sync();
+    for (int h = tid; h < heads; h += nthreads) {
+        float M = -INFINITY;
+        for (int c = 0; c < nchunks; ++c)
+            M = fmaxf(M, mw[h * nchunks + c]);
+        float L = 0.0f;
+        for (int c = 0; c < nchunks; ++c) {
+            const float l = lw[h * nchunks + c];
+            const float w = l > 0.0f ? expf(mw[h * nchunks + c] - M) : 0.0f;
+            mw[h * nchunks + c] = w;
+            L = fmaf(l, w, L);
+        }
+        const float inv = __fdiv_rn(1.0f, L);
+        for (int c = 0; c < nchunks; ++c)
+            mw[h * nchunks + c] *= inv;
+    }
+    sync();
+    for (int e = tid; e < heads * HD; e += nthreads) {
+        const int h = e / HD, d = e % HD;
+        const float* w = mw + h * nchunks;
+        float o = 0.0f;
+        int c = 0;
+        for (; c + 4 <= nchunks; c += 4) {
+            float v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                v[u] = __ldcg(part_ptr<HD>(const_cast<float*>(part), p, h / p.gqa, c + u, h % p.gqa) + 2 + d);
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                o = fmaf(v[u], w[c + u], o);
+        }
+        for (; c < nchunks; ++c)
+            o = fmaf(__ldcg(part_ptr<HD>(const_cast<float*>(part), p, h / p.gqa, c, h % p.gqa) + 2 + d), w[c], o);
+        out_at(e, o);
+    }
+}
+
 struct BlockSync {
     __device__ __forceinline__ void operator()() const { __syncthreads(); }
 };
@@ -143,7 +197,7 @@ struct BlockSync {
 // HD doubles. When `out` is non-null and the item is the only chunk, the normalised output is written
 // there; otherwise the partial (m, l, o) goes to `part`.
 template <typename KV, int HD, bool FUSED, typename Sync>
-__device__ void attention_item(const AttnDev& p, const float* q_in, KV* kc, KV* vc, int pos, int kvh, int chunk,
+__device__ __forceinline__ void attention_item(const AttnDev& p, const float* q_in, KV* kc, KV* vc, int pos, int kvh, int chunk,
                                float* out, float* part, float* sm, double* cs, int tid, int nthreads, Sync sync)
 {
     constexpr int LD = HD + 1;
@@ -154,8 +208,6 @@ __device__ void attention_item(const AttnDev& p, const float* q_in, KV* kc, KV* 
     float* Ps = Qs + G * HD;          // [G][kAttnKeys]
     float* Ms = Ps + G * kAttnKeys;   // [G]
     float* Ls = Ms + G;               // [G]
-    float* Kn = Ls + G;               // [HD] new key (rounded)
-    float* Vn = Kn + HD;              // [HD] new value (rounded)
 
     const int n = pos + 1;
     const int nchunks = (n + kAttnKeys - 1) / kAttnKeys;
@@ -163,6 +215,43 @@ __device__ void attention_item(const AttnDev& p, const float* q_in, KV* kc, KV* 
     const int nk = min(kAttnKeys, n - key0);
     const size_t head_base = (size_t)kvh * p.max_seq * HD;
     const bool holds_new = FUSED && (chunk == nchunks - 1);
+    const int t_new = holds_new ? pos - key0 : -1;  // tile row of the key appended by this step
+
+    // K/V tile rows written by earlier steps, as 16-byte vectors: the first batch is issued before
+    // the RoPE work below so that both sets of loads are in flight together.
+    constexpr int VEC = 16 / (int)sizeof(KV);
+    constexpr int VPR = HD / VEC;
+    constexpr int BATCH = 4;
+    const int nvec = nk * VPR;
+    uint4 kreg[BATCH], vreg[BATCH];
+#define MUYO_KV_LOAD_BATCH(BASE)                                                                      \
+    _Pragma("unroll") for (int u = 0; u < BATCH; ++u)                                                 \
+    {                                                                                                 \
+        const int v = (BASE) + u * nthreads + tid;                                                    \
+        const int t = v / VPR;                                                                        \
+        if (v < nvec && t != t_new) {                                                                 \
+            const size_t off = head_base + (size_t)(key0 + t) * HD + (size_t)(v % VPR) * VEC;         \
+            kreg[u] = __ldcg(reinterpret_cast<const uint4*>(kc + off));                              \
+            vreg[u] = __ldcg(reinterpret_cast<const uint4*>(vc + off));                              \
+        }                                                                                             \
+    }
+#define MUYO_KV_STORE_BATCH(BASE)                                                                     \
+    _Pragma("unroll") for (int u = 0; u < BATCH; ++u)                                                 \
+    {                                                                                                 \
+        const int v = (BASE) + u * nthreads + tid;                                                    \
+        const int t = v / VPR;                                                                        \
+        if (v < nvec && t != t_new) {                                                                 \
+            const int c0 = (v % VPR) * VEC;                                                           \
+            const KV* kk = reinterpret_cast<const KV*>(&kreg[u]);                                     \
+            const KV* vv = reinterpret_cast<const KV*>(&vreg[u]);                                     \
+            _Pragma("unroll") for (int i = 0; i < VEC; ++i)                                           \
+            {                                                                                         \
+                Ks[t * LD + c0 + i] = kv_value<KV>(kk[i]);                                            \
+                Vs[t * LD + c0 + i] = kv_value<KV>(vv[i]);                                            \
+            }                                                                                         \
+        }                                                                                             \
+    }
+    MUYO_KV_LOAD_BATCH(0)
 
     if (FUSED) {
         for (int j = tid; j < HD / 2; j += nthreads) {
@@ -195,38 +284,26 @@ __device__ void attention_item(const AttnDev& p, const float* q_in, KV* kc, KV* 
                 const KV k0 = kv_round<KV>(y0), k1 = kv_round<KV>(y1);
                 kc[head_base + (size_t)pos * HD + j] = k0;
                 kc[head_base + (size_t)pos * HD + j + HD / 2] = k1;
-                Kn[j] = kv_value<KV>(k0);
-                Kn[j + HD / 2] = kv_value<KV>(k1);
+                Ks[t_new * LD + j] = kv_value<KV>(k0);
+                Ks[t_new * LD + j + HD / 2] = kv_value<KV>(k1);
             }
             for (int d = tid; d < HD; d += nthreads) {
                 const KV v0 = kv_round<KV>(__ldcg(vr + d));
                 vc[head_base + (size_t)pos * HD + d] = v0;
-                Vn[d] = kv_value<KV>(v0);
+                Vs[t_new * LD + d] = kv_value<KV>(v0);
             }
         }
     } else {
         for (int e = tid; e < G * HD; e += nthreads)
             Qs[e] = __ldcg(q_in + (size_t)kvh * G * HD + e);
     }
-    sync();  // Kn / Vn / Qs are read by other threads below
-
-    // Stage the K and V tiles (keys that earlier steps wrote; the new key comes from Kn/Vn).
-    for (int e = tid; e < kAttnKeys * HD; e += nthreads) {
-        const int t = e / HD, d = e % HD;
-        const int j = key0 + t;
-        float kv = 0.0f, vv = 0.0f;
-        if (t < nk) {
-            if (holds_new && j == pos) {
-                kv = Kn[d];
-                vv = Vn[d];
-            } else {
-                kv = kv_load<KV>(kc + head_base + (size_t)j * HD + d);
-                vv = kv_load<KV>(vc + head_base + (size_t)j * HD + d);
-            }
-        }
-        Ks[t * LD + d] = kv;
-        Vs[t * LD + d] = vv;
+    MUYO_KV_STORE_BATCH(0)
+    for (int base = BATCH * nthreads; base < nvec; base += BATCH * nthreads) {
+        MUYO_KV_LOAD_BATCH(base)
+        MUYO_KV_STORE_BATCH(base)
     }
+#undef MUYO_KV_LOAD_BATCH
+#undef MUYO_KV_STORE_BATCH
     sync();
 
     // Scores: thread (t, h0) computes key t for group members g = h0, h0 + hs, ...

@@ -33,7 +33,7 @@
 
 namespace muyo {
 
-constexpr int kPWarps = 12;
+constexpr int kPWarps = 8;
 constexpr int kPThreads = kPWarps * 32;
 constexpr int kCWarps = kPWarps - 1;
 constexpr int kCThreads = kCWarps * 32;
@@ -177,15 +177,16 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p)
 }
 
 // Grid barrier among the consumer warps of all CTAs (the producer never joins). `k` counts the
-// barriers of this launch; the counter was zeroed before the launch.
+// barriers of this launch; the counter was zeroed before the launch. The named barrier orders the
+// CTA's writes before thread 0's acq_rel fence and relaxed arrival (the release pattern of a GPU-scope
+// barrier); the acquire poll orders the reads that follow.
 __device__ __forceinline__ bool grid_sync(const PArgs& a, unsigned& k, int ctid, volatile int* abort_sm)
 {
     ++k;
     consumer_sync();
     if (ctid == 0 && !*abort_sm) {
         const unsigned target = k * gridDim.x;
-        __threadfence();
-        atomicAdd(a.bar, 1u);
+        asm volatile("fence.acq_rel.gpu;\n\tred.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
         if (ld_acquire_u32(a.bar) < target) {
             const unsigned long long t0 = now_ns();
             while (ld_acquire_u32(a.bar) < target) {
@@ -195,7 +196,6 @@ __device__ __forceinline__ bool grid_sync(const PArgs& a, unsigned& k, int ctid,
                 }
             }
         }
-        __threadfence();
     }
     consumer_sync();
     return !*abort_sm;
@@ -213,6 +213,22 @@ __device__ __forceinline__ int tile_rows(const PArgs& a, const TileGeom& g)
     return a.slot_bytes / (g.K * 2 * g.nmat);
 }
 
+// Tiles of one phase for this CTA: its rows [rb, re) split evenly into ceil(rows / R) tiles
+// (R rows fit a slot), so no tile is a small remainder.
+__device__ __forceinline__ void tile_span(int rb, int re, int R, int t, int& r0, int& n, int& ntiles)
+{
+    const int rows = re - rb;
+    ntiles = rows > 0 ? (rows + R - 1) / R : 0;
+    if (ntiles == 0) {
+        r0 = rb;
+        n = 0;
+        return;
+    }
+    const int a = rows * t / ntiles, b = rows * (t + 1) / ntiles;  // rows per CTA stay far below 2^31 / ntiles
+    r0 = rb + a;
+    n = b - a;
+}
+
 // ---- producer ---------------------------------------------------------------------------------------
 
 __device__ void producer_loop(const PArgs& a, char* ring, uint64_t* full, uint64_t* empty, volatile int* abort_sm)
@@ -227,8 +243,12 @@ __device__ void producer_loop(const PArgs& a, char* ring, uint64_t* full, uint64
                 int rb, re;
                 cta_rows(g.rows, rb, re);
                 const int R = tile_rows(a, g);
-                for (int r0 = rb; r0 < re; r0 += R, ++i) {
-                    const int n = min(R, re - r0);
+                int ntiles = 1;
+                for (int t = 0; t < ntiles; ++t, ++i) {
+                    int r0, n;
+                    tile_span(rb, re, R, t, r0, n, ntiles);
+                    if (ntiles == 0)
+                        break;
                     const int s = (int)(i % a.slots);
                     if (i >= (unsigned long long)a.slots &&
                         !mbar_wait(&empty[s], (unsigned)(((i / a.slots) - 1) & 1), abort_sm))
@@ -256,22 +276,62 @@ __device__ void producer_loop(const PArgs& a, char* ring, uint64_t* full, uint64
 
 // ---- consumers -----------------------------------------------------------------------------------------
 
-// Stage a K-vector into xs (split layout). NORM applies x / sqrt(mean(x^2) + eps) * w
-// (tools/reference_qwen2.py:81-82). EMBED reads row `token` of the F16 table; CTA 0 then also
-// stores it to `copy` (the residual stream).
+// Stage a K-vector into xs (split layout of gemv.cuh). NORM applies x / sqrt(mean(x^2) + eps) * w
+// (tools/reference_qwen2.py:81-82). EMBED reads row `token` of the F16 table, and CTA 0 also stores
+// it to `copy` (the residual stream). All loads (x and w) are issued before any is used: one L2 round
+// trip per phase. K must be a multiple of 8.
 template <bool NORM, bool EMBED>
-__device__ __forceinline__ void stage_x(const float* src, const __half* erow, const float* w, float eps, int K,
+__device__ __noinline__ void stage_x(const float* src, const __half* erow, const float* w, float eps, int K,
                                         float* xs, float* red, float* copy, int ctid)
 {
+    constexpr int NB = 2;  // 8-element chunks per thread per pass
     const int K8 = K / 8;
     float ss = 0.0f;
-    for (int k = ctid; k < K; k += kCThreads) {
-        const float v = EMBED ? __half2float(erow[k]) : __ldcg(src + k);
-        if (NORM)
-            ss = fmaf(v, v, ss);
-        xs[xs_index(k, K8)] = v;
-        if (EMBED && blockIdx.x == 0)
-            copy[k] = v;
+    for (int base = 0; base < K8; base += NB * kCThreads) {
+        float4 lo[NB], hi[NB], wl[NB], wh[NB];
+#pragma unroll
+        for (int u = 0; u < NB; ++u) {
+            const int c = base + u * kCThreads + ctid;
+            if (c < K8) {
+                if (EMBED) {
+                    const uint4 hv = __ldg(reinterpret_cast<const uint4*>(erow) + c);
+                    const float2 a0 = h2_to_f2(hv.x), a1 = h2_to_f2(hv.y), a2 = h2_to_f2(hv.z), a3 = h2_to_f2(hv.w);
+                    lo[u] = make_float4(a0.x, a0.y, a1.x, a1.y);
+                    hi[u] = make_float4(a2.x, a2.y, a3.x, a3.y);
+                } else {
+                    lo[u] = __ldcg(reinterpret_cast<const float4*>(src) + 2 * c);
+                    hi[u] = __ldcg(reinterpret_cast<const float4*>(src) + 2 * c + 1);
+                }
+                if (NORM) {
+                    wl[u] = __ldg(reinterpret_cast<const float4*>(w) + 2 * c);
+                    wh[u] = __ldg(reinterpret_cast<const float4*>(w) + 2 * c + 1);
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < NB; ++u) {
+            const int c = base + u * kCThreads + ctid;
+            if (c < K8) {
+                if (NORM) {
+                    ss = fmaf(lo[u].x, lo[u].x, ss); ss = fmaf(lo[u].y, lo[u].y, ss);
+                    ss = fmaf(lo[u].z, lo[u].z, ss); ss = fmaf(lo[u].w, lo[u].w, ss);
+                    ss = fmaf(hi[u].x, hi[u].x, ss); ss = fmaf(hi[u].y, hi[u].y, ss);
+                    ss = fmaf(hi[u].z, hi[u].z, ss); ss = fmaf(hi[u].w, hi[u].w, ss);
+                    // keep raw x and w side by side until the scale is known
+                    reinterpret_cast<float4*>(xs)[c] = lo[u];
+                    reinterpret_cast<float4*>(xs + 4 * K8)[c] = hi[u];
+                    reinterpret_cast<float4*>(xs + 8 * K8)[c] = wl[u];
+                    reinterpret_cast<float4*>(xs + 12 * K8)[c] = wh[u];
+                } else {
+                    reinterpret_cast<float4*>(xs)[c] = lo[u];
+                    reinterpret_cast<float4*>(xs + 4 * K8)[c] = hi[u];
+                }
+                if (EMBED && blockIdx.x == 0) {
+                    reinterpret_cast<float4*>(copy)[2 * c] = lo[u];
+                    reinterpret_cast<float4*>(copy)[2 * c + 1] = hi[u];
+                }
+            }
+        }
     }
     if (!NORM) {
         consumer_sync();
@@ -285,10 +345,9 @@ __device__ __forceinline__ void stage_x(const float* src, const __half* erow, co
     float t = lane < kCWarps ? red[lane] : 0.0f;
     t = warp_sum(t);
     const float s = __fsqrt_rn(__fdiv_rn(t, (float)K) + eps);
-    for (int k = ctid; k < K; k += kCThreads) {
-        const int i = xs_index(k, K8);
-        xs[i] = __fdiv_rn(xs[i], s) * __ldg(w + k);
-    }
+#pragma unroll 1
+    for (int i = ctid; i < 8 * K8; i += kCThreads)
+        xs[i] = __fdiv_rn(xs[i], s) * xs[8 * K8 + i];
     consumer_sync();
 }
 
@@ -297,74 +356,155 @@ struct HeadBest {
     int i;
 };
 
+__device__ __forceinline__ uint4 lds_u4(unsigned addr)
+{
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ float4 lds_f4(unsigned addr)
+{
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+    return v;
+}
+
+// Dot products of NR rows (of NMAT matrices; NR * NMAT = 2 dot products) of a tile with x, for one
+// lane: the lane takes the 16-byte chunks c = lane + 32 j; four chunks are loaded before any is used
+// and accumulate into four independent chains per dot product (instruction-level parallelism over
+// the shared-memory latency). All operands are read with ld.shared from 32-bit shared addresses
+// (the tile at `base`, the split-layout x at `xs`), which stays explicit across the out-of-line
+// phase functions.
+template <int NMAT, int NR>
+__device__ __forceinline__ void dot_rows(unsigned base, unsigned rowb, unsigned matb, int ra, int rb_, int K8,
+                                         unsigned xs, int lane, float (&out)[NMAT][2])
+{
+    static_assert(NMAT * NR == 2, "two dot products per pass");
+    float acc[NMAT][NR][4];
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+        for (int j = 0; j < NR; ++j)
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                acc[m][j][q] = 0.0f;
+    unsigned w[NMAT][NR];
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m) {
+        w[m][0] = base + m * matb + ra * rowb;
+        if (NR > 1)
+            w[m][NR - 1] = base + m * matb + rb_ * rowb;
+    }
+    const unsigned xhi = xs + 16u * K8;
+    for (int c0 = lane; c0 < K8; c0 += 128) {
+        uint4 wv[NMAT][NR][4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int c = c0 + 32 * q;
+            if (c < K8) {
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+                    for (int j = 0; j < NR; ++j)
+                        wv[m][j][q] = lds_u4(w[m][j] + 16u * c);
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int c = c0 + 32 * q;
+            if (c < K8) {
+                const float4 xa = lds_f4(xs + 16u * c), xb = lds_f4(xhi + 16u * c);
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+                    for (int j = 0; j < NR; ++j) {
+                        const uint4 v = wv[m][j][q];
+                        float s = acc[m][j][q];
+                        float2 f = h2_to_f2(v.x);
+                        s = fmaf(f.x, xa.x, s);
+                        s = fmaf(f.y, xa.y, s);
+                        f = h2_to_f2(v.y);
+                        s = fmaf(f.x, xa.z, s);
+                        s = fmaf(f.y, xa.w, s);
+                        f = h2_to_f2(v.z);
+                        s = fmaf(f.x, xb.x, s);
+                        s = fmaf(f.y, xb.y, s);
+                        f = h2_to_f2(v.w);
+                        s = fmaf(f.x, xb.z, s);
+                        s = fmaf(f.y, xb.w, s);
+                        acc[m][j][q] = s;
+                    }
+            }
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+            out[m][j] = j < NR ? warp_sum((acc[m][j < NR ? j : 0][0] + acc[m][j < NR ? j : 0][1]) +
+                                          (acc[m][j < NR ? j : 0][2] + acc[m][j < NR ? j : 0][3]))
+                               : 0.0f;
+}
+
 // Consume this CTA's tiles of one phase: two rows per warp pass, lanes over 16-byte chunks.
 template <int EPI>
-__device__ __forceinline__ void consume_phase(const PArgs& a, const TileGeom& g, const float* xs, char* ring,
+__device__ __noinline__ void consume_phase(const PArgs& a, const TileGeom& g, const float* xs, char* ring,
                                               uint64_t* full, uint64_t* empty, unsigned long long& ti, int layer,
                                               int cwarp, int lane, volatile int* abort_sm, HeadBest& best)
 {
+    constexpr int NMAT = EPI == PH_GATEUP ? 2 : 1;
     int rb, re;
     cta_rows(g.rows, rb, re);
     const int R = tile_rows(a, g);
     const int K8 = g.K / 8;
-    const float4* xlo = reinterpret_cast<const float4*>(xs);
-    const float4* xhi = reinterpret_cast<const float4*>(xs + 4 * K8);
+    const unsigned xs_s = smem_u32(xs), ring_s = smem_u32(ring);
     const PLayer* L = layer < a.L ? &a.layers[layer] : nullptr;
-    for (int r0 = rb; r0 < re; r0 += R, ++ti) {
-        const int n = min(R, re - r0);
+    int ntiles = 1;
+    for (int t = 0; t < ntiles; ++t, ++ti) {
+        int r0, n;
+        tile_span(rb, re, R, t, r0, n, ntiles);
+        if (ntiles == 0)
+            break;
         const int s = (int)(ti % a.slots);
         if (!mbar_wait(&full[s], (unsigned)((ti / a.slots) & 1), abort_sm))
             continue;  // aborted: skip this warp's work (no barrier is skipped)
-        const char* base = ring + (size_t)s * a.slot_bytes;
-        const size_t rowb = (size_t)g.K * 2, matb = (size_t)n * rowb;
-        for (int r = cwarp; r < n; r += 2 * kCWarps) {
-            const int r2 = r + kCWarps;
-            const bool two = r2 < n;
-            float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-            const uint4* w00 = reinterpret_cast<const uint4*>(base + r * rowb);
-            const uint4* w01 = reinterpret_cast<const uint4*>(base + (two ? r2 : r) * rowb);
-            const uint4* w10 = reinterpret_cast<const uint4*>(base + matb + r * rowb);
-            const uint4* w11 = reinterpret_cast<const uint4*>(base + matb + (two ? r2 : r) * rowb);
-            for (int c = lane; c < K8; c += 32) {
-                const float4 xa = xlo[c], xb = xhi[c];
-                const uint4 wa = w00[c];
-                const uint4 wb = w01[c];
-                float2 f;
-#define MUYO_DOT8(W, S)                                                                  \
-    f = h2_to_f2(W.x); S = fmaf(f.x, xa.x, S); S = fmaf(f.y, xa.y, S);                   \
-    f = h2_to_f2(W.y); S = fmaf(f.x, xa.z, S); S = fmaf(f.y, xa.w, S);                   \
-    f = h2_to_f2(W.z); S = fmaf(f.x, xb.x, S); S = fmaf(f.y, xb.y, S);                   \
-    f = h2_to_f2(W.w); S = fmaf(f.x, xb.z, S); S = fmaf(f.y, xb.w, S);
-                MUYO_DOT8(wa, acc[0][0]);
-                MUYO_DOT8(wb, acc[0][1]);
-                if (g.nmat == 2) {
-                    const uint4 wc = w10[c];
-                    const uint4 wd = w11[c];
-                    MUYO_DOT8(wc, acc[1][0]);
-                    MUYO_DOT8(wd, acc[1][1]);
+        const unsigned base = ring_s + (unsigned)s * a.slot_bytes;
+        const unsigned rowb = (unsigned)g.K * 2, matb = (unsigned)n * rowb;
+        constexpr int NR = 2 / NMAT;  // rows per warp pass
+        for (int r = NR * cwarp; r < n; r += NR * kCWarps) {
+            const bool two = NR == 2 && r + 1 < n;
+            // epilogue operands, loaded before the dot products so their latency overlaps them
+            float pre[2] = {0.f, 0.f};
+            if (lane == 0) {
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const int row = r0 + (j == 1 && two ? r + 1 : r);
+                    if (EPI == PH_QKV)
+                        pre[j] = __ldg(L->bqkv + row);
+                    else if (EPI == PH_O)
+                        pre[j] = __ldcg(a.h + row);
+                    else if (EPI == PH_DOWN)
+                        pre[j] = __ldcg(a.h1 + row);
                 }
-#undef MUYO_DOT8
             }
-#pragma unroll
-            for (int m = 0; m < 2; ++m)
-#pragma unroll
-                for (int j = 0; j < 2; ++j)
-                    acc[m][j] = warp_sum(acc[m][j]);
+            float acc[NMAT][2];
+            dot_rows<NMAT, NR>(base, rowb, matb, r, two ? r + 1 : r, K8, xs_s, lane, acc);
             if (lane == 0) {
 #pragma unroll
                 for (int j = 0; j < 2; ++j) {
                     if (j == 1 && !two)
                         break;
-                    const int row = r0 + (j == 0 ? r : r2);
+                    const int row = r0 + r + j;
                     const float v = acc[0][j];
                     if (EPI == PH_QKV) {
-                        a.qkv[row] = v + __ldg(L->bqkv + row);
+                        a.qkv[row] = v + pre[j];
                     } else if (EPI == PH_O) {
-                        a.h1[row] = __ldcg(a.h + row) + v;
+                        a.h1[row] = pre[j] + v;
                     } else if (EPI == PH_GATEUP) {
-                        a.act[row] = silu_mul(v, acc[1][j]);
+                        a.act[row] = silu_mul(v, acc[NMAT - 1][0]);
                     } else if (EPI == PH_DOWN) {
-                        a.h[row] = __ldcg(a.h1 + row) + v;
+                        a.h[row] = pre[j] + v;
                     } else {
                         a.logits[row] = v;
                         if (pair_better(v, row, best.v, best.i))
@@ -377,6 +517,32 @@ __device__ __forceinline__ void consume_phase(const PArgs& a, const TileGeom& g,
         if (lane == 0)
             mbar_arrive(&empty[s]);
     }
+}
+
+// The attention work items of this CTA at `pos` (one layer), then the O-phase input: the merged
+// attention output staged into xs. The phases are out of line so that each gets its own register
+// allocation (the whole step inlined into one loop body exceeds 255 registers).
+template <typename KV, int HD>
+__device__ __noinline__ void attention_phase(const PArgs& a, int l, int pos, int nchunks, float* region_b, double* cs,
+                                             int ctid)
+{
+    KV* kcl = static_cast<KV*>(a.kc) + (size_t)a.kv_layer_elems * l;
+    KV* vcl = static_cast<KV*>(a.vc) + (size_t)a.kv_layer_elems * l;
+    for (int it = blockIdx.x; it < a.kv_heads * nchunks; it += gridDim.x) {
+        attention_item<KV, HD, true>(a.attn, a.qkv, kcl, vcl, pos, it % a.kv_heads, it / a.kv_heads, nullptr,
+                                     a.attn_part, region_b, cs, ctid, kCThreads, ConsumerSync{});
+        consumer_sync();
+    }
+}
+
+template <int HD>
+__device__ __noinline__ void merge_phase(const PArgs& a, int nchunks, float* region_b, int ctid)
+{
+    const int K8 = a.QD / 8;
+    float* xs = region_b;
+    attn_merge_all<HD>(a.attn, a.attn_part, nchunks, region_b + a.QD, ctid, kCThreads, ConsumerSync{},
+                       [&](int e, float v) { xs[xs_index(e, K8)] = v; });
+    consumer_sync();
 }
 
 template <typename KV, int HD>
@@ -440,24 +606,10 @@ __global__ void __launch_bounds__(kPThreads, 1) k_decode_persistent(PArgs a)
                                   abort_sm, unused);
             grid_sync(a, k, ctid, abort_sm);
             // ATTN: work items (kv head, chunk) spread over the CTAs
-            KV* kcl = static_cast<KV*>(a.kc) + (size_t)a.kv_layer_elems * l;
-            KV* vcl = static_cast<KV*>(a.vc) + (size_t)a.kv_layer_elems * l;
-            for (int it = blockIdx.x; it < a.kv_heads * nchunks; it += gridDim.x) {
-                attention_item<KV, HD, true>(a.attn, a.qkv, kcl, vcl, pos, it % a.kv_heads, it / a.kv_heads,
-                                             nullptr, a.attn_part, region_b, cs, ctid, kCThreads, ConsumerSync{});
-                consumer_sync();
-            }
+            attention_phase<KV, HD>(a, l, pos, nchunks, region_b, cs, ctid);
             grid_sync(a, k, ctid, abort_sm);
             // O: merge the attention partials straight into the staged x
-            {
-                const int K8 = a.QD / 8;
-                for (int e = ctid; e < a.QD; e += kCThreads) {
-                    const int hh = e / HD, d = e % HD;
-                    region_b[xs_index(e, K8)] =
-                        attn_merge_one<HD>(a.attn, a.attn_part, hh / a.gqa, hh % a.gqa, d, nchunks);
-                }
-                consumer_sync();
-            }
+            merge_phase<HD>(a, nchunks, region_b, ctid);
             consume_phase<PH_O>(a, phase_geom(a, l, PH_O), region_b, ring, full, empty, ti, l, cwarp, lane, abort_sm,
                                 unused);
             grid_sync(a, k, ctid, abort_sm);

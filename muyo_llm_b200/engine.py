@@ -26,7 +26,7 @@ class Qwen2Model:
     ENGINE_PERSISTENT, ENGINE_GRAPH = 0, 1
 
     def __init__(self, cfg: Qwen2Config, tensors: dict | None = None, gguf_path: str | None = None,
-                 kv_dtype: int = _abi.KV_F16, device: int = 0, engine: int = 0):
+                 kv_dtype: int = _abi.KV_F16, device: int = 0, engine: int = 1):
         self.cfg = cfg
         self.kv_dtype = kv_dtype
         self._cfg = config_struct(cfg, kv_dtype)
