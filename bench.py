@@ -8,7 +8,9 @@ cache. `value` = decode tokens (prompt + generated, one decode step each) per se
 job: with N GPUs, N independent seeded streams (one per GPU, weak scaling; the decode chain does not
 shard), summed. Timed on the device with CUDA events around K sequences, max over ranks.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--engine graph|persistent]
+  python bench.py --suite gemv [--shapes 14336x4096,...]   # F16 GEMV sweep, one JSON line per shape
+  python bench.py --suite ops                              # op latency + multi-row bandwidth sweep
 
 `--impl reference` times the reference's CPU forward on the host cores instead: the C oracle port
 (oracle/oracle.c, the reference's numpy forward restated in C, row-parallel on all host threads;
@@ -170,17 +172,17 @@ def run_b200(args, rank, world, local_rank):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local_rank))
     cfg = synth.QWEN2_05B
     tensors = synth.make_model(cfg, SEED)
-    prompt = synth.prompt_ids(SEED + rank, N_PROMPT, cfg.vocab)  # an independent stream per GPU
+    prompt = synth.prompt_ids(SEED + rank, args.n_prompt, cfg.vocab)  # an independent stream per GPU
     eng = engine.Qwen2Model.ENGINE_GRAPH if args.engine == "graph" else engine.Qwen2Model.ENGINE_PERSISTENT
     model = engine.Qwen2Model(cfg, tensors, kv_dtype=_abi.KV_F16, device=local_rank, engine=eng)
     stream = torch.cuda.current_stream()
     sptr = stream.cuda_stream
     prompt_dev = torch.from_numpy(prompt).cuda()
-    out_dev = torch.empty(N_PREDICT, dtype=torch.int32, device="cuda")
+    out_dev = torch.empty(args.n_predict, dtype=torch.int32, device="cuda")
 
     def one_sequence():
         _abi.call("muyo_model_reset", model._m, sptr)
-        model.generate_device(prompt_dev.data_ptr(), N_PROMPT, N_PREDICT, out_dev.data_ptr(), sptr)
+        model.generate_device(prompt_dev.data_ptr(), args.n_prompt, args.n_predict, out_dev.data_ptr(), sptr)
 
     def barrier():
         torch.cuda.synchronize()
@@ -206,7 +208,7 @@ def run_b200(args, rank, world, local_rank):
         ev1.record(stream)
         barrier()
     ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
-    steps_per_seq = N_PROMPT + N_PREDICT
+    steps_per_seq = args.n_prompt + args.n_predict
     value = steps_per_seq * world / (ms / 1e3)
 
     # e2e: the public host API, pinned host prompt in, generated ids out, per sequence
@@ -214,11 +216,11 @@ def run_b200(args, rank, world, local_rank):
     t0 = time.perf_counter()
     for _ in range(args.steps):
         model.reset(sptr)
-        model.generate(prompt, N_PREDICT, sptr)
+        model.generate(prompt, args.n_predict, sptr)
     barrier()
     e2e_s = max_over_ranks((time.perf_counter() - t0) / args.steps)
-    e2e = {"value": steps_per_seq * world / e2e_s, "unit": UNIT, "h2d_bytes_per_step": N_PROMPT * 4,
-           "d2h_bytes_per_step": N_PREDICT * 4}
+    e2e = {"value": steps_per_seq * world / e2e_s, "unit": UNIT, "h2d_bytes_per_step": args.n_prompt * 4,
+           "d2h_bytes_per_step": args.n_predict * 4}
 
     # roofline: one decode step (a CUDA-graph replay of 5*layers+1 kernels) against HBM bandwidth
     peak, peak_kind = measured_peaks()
@@ -242,11 +244,14 @@ def run_b200(args, rank, world, local_rank):
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f16 weights / f32 compute", "data": "synthetic (seeded random-init)",
-                "config": {"workload": "config 4: Qwen2.5-0.5B arch, 32-token prompt + 256 greedy, F16 KV, cap 2048",
+                "config": {"workload": (f"config 4: Qwen2.5-0.5B arch, {args.n_prompt}-token prompt + {args.n_predict} "
+                                        "greedy, F16 KV, cap 2048"
+                                        + ("" if (args.n_prompt, args.n_predict) == (N_PROMPT, N_PREDICT)
+                                           else " (shortened: a profiling run, not the config-4 workload)")),
                            "model": "Qwen2.5-0.5B architecture (random init)", "global_batch": world,
                            "seq_len": steps_per_seq, "parallelism": f"replicas x{world} (independent streams)",
                            "l2": "inputs larger than L2 (988 MB of weights per step)",
-                           "generated_tokens_per_s": value * N_PREDICT / steps_per_seq,
+                           "generated_tokens_per_s": value * args.n_predict / steps_per_seq,
                            "ms_per_token": ms / steps_per_seq},
                 "e2e": e2e, "roofline": roofline, "cpu_baseline": cb, "clocks": clocks.summary(),
                 "gpu_launches": launches, "engine": args.engine}
@@ -257,6 +262,27 @@ def run_b200(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
+def run_suite(args):
+    """Kernel sweeps (muyo_llm_b200/sweep.py): one JSON line per case, then a clocks line."""
+    import torch
+
+    from muyo_llm_b200 import _abi, sweep
+
+    torch.cuda.set_device(0)
+    _abi.call("muyo_cuda_init", 0)
+    peak, peak_kind = measured_peaks()
+    with ClockSampler(0) as clocks:
+        if args.suite == "gemv":
+            shapes = [tuple(int(v) for v in s.split("x")) for s in args.shapes.split(",") if s] or None
+            res = sweep.gemv(shapes, args.iters, peak)
+        else:
+            res = sweep.ops(args.iters, peak)
+    for r in res:
+        r.update({"suite": args.suite, "peak_GB_s": peak, "peak_kind": peak_kind})
+        print(json.dumps(r), flush=True)
+    print(json.dumps({"suite": args.suite, "clocks": clocks.summary()}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -265,8 +291,20 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--engine", default="graph", choices=["persistent", "graph"])
+    ap.add_argument("--suite", default="decode", choices=["decode", "gemv", "ops"],
+                    help="decode: the config-4 headline line (default); gemv / ops: kernel sweeps, one JSON line "
+                         "per case (1 GPU)")
+    ap.add_argument("--shapes", default="", help="gemv suite: comma-separated ROWSxCOLS list (default: all)")
+    ap.add_argument("--iters", type=int, default=0, help="gemv / ops suite: calls timed per case (0: automatic)")
+    ap.add_argument("--n-prompt", type=int, default=N_PROMPT,
+                    help="decode suite: prompt ids per sequence (config 4: 32; smaller only for profiling)")
+    ap.add_argument("--n-predict", type=int, default=N_PREDICT,
+                    help="decode suite: generated ids per sequence (config 4: 256; smaller only for profiling)")
     args = ap.parse_args()
     rank, world, local_rank = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
+    if args.suite != "decode":
+        run_suite(args)
+        return
     if args.impl == "reference":
         run_reference(args, rank, world)
     else:
