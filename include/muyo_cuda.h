@@ -305,6 +305,29 @@ int muyo_cuda_mat_vec_f16_argmax(const MuyoMatVecParams* p, const void* a, const
                                  void* stream);
 int muyo_cuda_argmax_pairs(const void* pairs, uint32_t n_pairs, int32_t* d, void* stream);
 
+/* ---- argmax with no workspace --------------------------------------------------------------------
+ * No counterpart in the reference: an addition of this library for callers that cannot supply
+ * device memory, either because allocating is off limits where they run (a memory budget already
+ * carved up by a pool; a latency-critical loop that cannot take cudaMalloc's implicit device
+ * synchronisation) or because they hold no device allocator (a thin FFI host that passes logits in
+ * and reads an index back). Same contract and result as muyo_cuda_argmax; the partials live in a
+ * static device array compiled into the library instead of a caller workspace, and the call
+ * allocates nothing (no cudaMalloc, cudaFree or allocating library routine).
+ *
+ * Limit: KY * ceil(KX / 8192) partials must not exceed muyo_cuda_argmax_noalloc_max_pairs() (8192,
+ * a 64 KB array per device): for example one row of up to 67,108,864 logits, or 431 rows of a
+ * 151,936-entry vocabulary. Larger calls fail with MUYO_EINVAL and a message; nothing is launched.
+ *
+ * The first call on each device looks up the array's device address (cudaGetSymbolAddress, with
+ * that device current) and caches it; make that first call before any stream capture. The cached
+ * address belongs to the device's current context: do not call after a cudaDeviceReset.
+ *
+ * All calls on one device share the one array, so two calls that can run at the same time (on
+ * different streams, or from different host threads without ordering) race on it and may return a
+ * wrong index. Calls issued in order on a single stream are safe. */
+size_t muyo_cuda_argmax_noalloc_max_pairs(void);
+int muyo_cuda_argmax_noalloc(const MuyoGenericParams* p, const float* a, int32_t* d, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

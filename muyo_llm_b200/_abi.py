@@ -122,6 +122,8 @@ SIGNATURES = {
     "muyo_model_set_option": (C.c_int, [VP, C.c_char_p, C.c_int]),
     "muyo_cuda_mat_vec_f16_argmax": (C.c_int, [P(MatVecParams), VP, VP, VP, U32, VP, VP, C.c_size_t, VP]),
     "muyo_cuda_argmax_pairs": (C.c_int, [VP, U32, VP, VP]),
+    "muyo_cuda_argmax_noalloc_max_pairs": (C.c_size_t, []),
+    "muyo_cuda_argmax_noalloc": (C.c_int, [P(GenericParams), VP, VP, VP]),
 }
 
 _lib = None

@@ -4,6 +4,7 @@
 // decode.cu.
 #include <climits>
 #include <cmath>
+#include <mutex>
 
 #include "common.cuh"
 #include "gemv.cuh"
@@ -894,4 +895,62 @@ extern "C" int muyo_cuda_argmax_pairs(const void* pairs, uint32_t n_pairs, int32
     k_argmax_final<<<1, kThreads, 0, as_stream(stream)>>>(static_cast<const ArgPair*>(pairs), (int)n_pairs, d);
     MUYO_LAUNCH_CHECK();
     return MUYO_OK;
+}
+
+// ---- argmax without a caller workspace ---------------------------------------------------------
+// For callers that cannot hand the library device memory: they run where allocating is off limits
+// (a fixed memory budget already carved up by a pool, a latency-critical loop where cudaMalloc's
+// implicit device synchronisation is unacceptable) or hold no device allocator at all (a thin FFI
+// host that only passes logits in and reads an index back). The partial pairs live in a static
+// device array compiled into this library, so the call itself allocates nothing.
+
+namespace muyo {
+constexpr int kNoAllocArgmaxPairs = 8192;  // 64 KB of (value, index) partials per device
+static __device__ __align__(256) ArgPair g_noalloc_argmax_pairs[kNoAllocArgmaxPairs];
+}  // namespace muyo
+
+namespace {
+constexpr int kMaxCachedDevices = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_ptr[kMaxCachedDevices] = {};
+
+// Device address of the static partials on the current device, resolved once per device.
+int noalloc_scratch(ArgPair** out)
+{
+    int dev = -1;
+    MUYO_CUDA_TRY(cudaGetDevice(&dev));
+    MUYO_REQUIRE(dev >= 0 && dev < kMaxCachedDevices, "argmax_noalloc: device ordinal %d is not supported", dev);
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (!g_noalloc_ptr[dev]) {
+        void* ptr = nullptr;
+        MUYO_CUDA_TRY(cudaGetSymbolAddress(&ptr, muyo::g_noalloc_argmax_pairs));
+        MUYO_REQUIRE(ptr != nullptr, "argmax_noalloc: no device address for the static scratch");
+        g_noalloc_ptr[dev] = ptr;
+    }
+    *out = static_cast<ArgPair*>(g_noalloc_ptr[dev]);
+    return MUYO_OK;
+}
+}  // namespace
+
+extern "C" size_t muyo_cuda_argmax_noalloc_max_pairs(void) { return (size_t)kNoAllocArgmaxPairs; }
+
+extern "C" int muyo_cuda_argmax_noalloc(const MuyoGenericParams* p, const float* a, int32_t* d, void* stream)
+{
+    clear_error();
+    MUYO_REQUIRE(p && a && d, "argmax_noalloc: null parameter block or buffer");
+    MUYO_REQUIRE(p->KX > 0 && p->KX <= (uint32_t)INT_MAX, "argmax_noalloc: KX must be in [1, INT_MAX]");
+    const uint32_t KY = p->KY ? p->KY : 1;
+    MUYO_REQUIRE(KY <= 65535u, "argmax_noalloc: KY %u exceeds 65535", KY);
+    const uint64_t pairs = (uint64_t)KY * (uint64_t)argmax_blocks(p->KX);
+    MUYO_REQUIRE(pairs <= (uint64_t)kNoAllocArgmaxPairs,
+                 "argmax_noalloc: KY * ceil(KX / %d) = %llu partials exceeds the static scratch of %d; "
+                 "use muyo_cuda_argmax with a workspace",
+                 kArgmaxChunk, (unsigned long long)pairs, kNoAllocArgmaxPairs);
+    ArgPair* part = nullptr;
+    const int rc = noalloc_scratch(&part);
+    if (rc != MUYO_OK)
+        return rc;
+    // Every partial is written by the first kernel before the second reads it, so no part of the
+    // scratch has to start at zero.
+    return argmax_launch(a, p->KX, KY, 0, part, d, as_stream(stream));
 }
