@@ -225,8 +225,9 @@ int muyo_cuda_kv_append(const MuyoAttentionParams* p, float rope_base, const flo
 
 /* ---- fused Qwen2 decoder layer (one token) ------------------------------------------------------
  * One decoder layer of the reference's 18-node layer graph (src/FullModel.cpp:685-953) as five
- * fused kernels: [rms_norm + QKV GEMV + bias] -> [rope + KV append + split-K GQA attention] ->
- * [o_proj GEMV + residual] -> [rms_norm + gate/up GEMV + SwiGLU] -> [down GEMV + residual].
+ * fused kernels: [rms_norm + QKV GEMV + bias] -> [rope + KV append + split-K GQA attention
+ * partials] -> [merge of the partials + o_proj GEMV + residual] -> [rms_norm + gate/up GEMV +
+ * SwiGLU] -> [down GEMV + residual].
  * Weights F16 row-major [out][in] (GGUF [ne0 = in, ne1 = out]); biases and norms F32. wqkv is the
  * q, k and v projections stacked by rows ([q_dim + 2*kv_dim][hidden]) and bqkv their biases. */
 typedef struct MuyoQwen2Config {
@@ -248,7 +249,8 @@ typedef struct MuyoLayerWeights {
 
 size_t muyo_cuda_layer_workspace_size(const MuyoQwen2Config* c);
 /* x_in -> x_out (both [hidden] F32, may not alias); k_cache/v_cache are this layer's caches;
- * pos: device int32 position of the token. */
+ * pos: device int32 position of the token. Weight matrices, norm weights, x_in and x_out must be
+ * 16-byte aligned (MUYO_EINVAL otherwise); the workspace 256-byte aligned. */
 int muyo_cuda_layer_step(const MuyoQwen2Config* c, const MuyoLayerWeights* w, void* k_cache, void* v_cache,
                          const int32_t* pos, const float* x_in, float* x_out, void* workspace, size_t workspace_bytes,
                          void* stream);
@@ -291,7 +293,12 @@ int muyo_model_destroy(MuyoModel* m);
  * as a CUDA graph per decode step; 0 runs every decode step of a generate call in one persistent
  * cooperative kernel (a producer warp streams weight tiles into shared memory ahead of the
  * activation dependencies, consumer warps meet at bounded grid barriers). Both compute the same
- * arithmetic; they differ only in F32 reduction order (last-bit differences). */
+ * arithmetic; they differ only in F32 reduction order (last-bit differences).
+ * Graph-engine options (set before muyo_model_finalize; results are bit-identical either way):
+ * "pdl" = 1 (default) launches each kernel with programmatic stream serialization, so it starts
+ * while the previous kernel drains and waits on the device for that kernel's results; "prefetch" =
+ * 1 (default) has each GEMV kernel stream the weights of the GEMV kernel two launches later into
+ * L2. */
 int muyo_model_set_option(MuyoModel* m, const char* key, int value);
 
 /* ---- row-sharded GEMV + cross-GPU greedy (multi-GPU LM head) --------------------------------------

@@ -23,7 +23,7 @@
 namespace muyo {
 
 constexpr int kAttnKeys = 64;      // keys per work item
-constexpr int kAttnThreads = 128;  // threads of the standalone attention CTA
+constexpr int kAttnThreads = 256;  // threads of the standalone attention CTA
 constexpr int kAttnMaxGroup = 16;  // query heads per KV head
 
 struct AttnDev {
@@ -138,15 +138,15 @@ __device__ void attn_merge(const AttnDev& p, const float* part, int kvh, int nch
 // out_at(e) receives element e = head * HD + d. Two batched passes over the partials: the
 // statistics (m, l) of every (head, chunk) into shared scratch and from them per-chunk weights
 // w_c = exp(m_c - M) / L; then o = sum_c o_c[d] w_c. `scratch` holds 2 * heads * nchunks floats.
+// attn_merge_heads covers the query heads h0 .. h0 + heads - 1 only (e then counts from h0 * HD).
 template <int HD, typename Sync, typename Out>
-__device__ void attn_merge_all(const AttnDev& p, const float* part, int nchunks, float* scratch, int tid, int nthreads,
-                               Sync sync, Out out_at)
+__device__ void attn_merge_heads(const AttnDev& p, const float* part, int nchunks, int h0, int heads, float* scratch,
+                                 int tid, int nthreads, Sync sync, Out out_at)
 {
-    const int heads = p.kv_heads * p.gqa;
     float* mw = scratch;                     // [heads][nchunks]: m, then the weight
     float* lw = scratch + heads * nchunks;   // [heads][nchunks]: l
     for (int i = tid; i < heads * nchunks; i += nthreads) {
-        const int h = i / nchunks, c = i % nchunks;
+        const int h = h0 + i / nchunks, c = i % nchunks;
         const float* q = part_ptr<HD>(const_cast<float*>(part), p, h / p.gqa, c, h % p.gqa);
         mw[i] = __ldcg(q);
         lw[i] = __ldcg(q + 1);
@@ -169,8 +169,8 @@ __device__ void attn_merge_all(const AttnDev& p, const float* part, int nchunks,
     }
     sync();
     for (int e = tid; e < heads * HD; e += nthreads) {
-        const int h = e / HD, d = e % HD;
-        const float* w = mw + h * nchunks;
+        const int hl = e / HD, h = h0 + hl, d = e % HD;
+        const float* w = mw + hl * nchunks;
         float o = 0.0f;
         int c = 0;
         for (; c + 4 <= nchunks; c += 4) {
@@ -188,17 +188,32 @@ __device__ void attn_merge_all(const AttnDev& p, const float* part, int nchunks,
     }
 }
 
+template <int HD, typename Sync, typename Out>
+__device__ void attn_merge_all(const AttnDev& p, const float* part, int nchunks, float* scratch, int tid, int nthreads,
+                               Sync sync, Out out_at)
+{
+    attn_merge_heads<HD>(p, part, nchunks, 0, p.kv_heads * p.gqa, scratch, tid, nthreads, sync, out_at);
+}
+
 struct BlockSync {
     __device__ __forceinline__ void operator()() const { __syncthreads(); }
 };
 
 // One work item (kvh, chunk) of the attention at position `pos`, run by threads tid in [0, nthreads)
-// of a CTA (nthreads a multiple of 32, at least 64). `sm` holds attn_smem_floats(HD, gqa) floats, `cs`
+// of a CTA (nthreads a multiple of 32, at least 128). `sm` holds attn_smem_floats(HD, gqa) floats, `cs`
 // HD doubles. When `out` is non-null and the item is the only chunk, the normalised output is written
 // there; otherwise the partial (m, l, o) goes to `part`.
-template <typename KV, int HD, bool FUSED, typename Sync>
+struct NoWait {
+    __device__ void operator()() const {}
+};
+
+// `wait` runs after the loads of cache rows written by earlier steps (and of the RoPE table) are
+// issued and before q_in is read: a kernel launched early uses it to wait for the kernel that
+// produced q_in.
+template <typename KV, int HD, bool FUSED, typename Sync, typename Wait = NoWait>
 __device__ __forceinline__ void attention_item(const AttnDev& p, const float* q_in, KV* kc, KV* vc, int pos, int kvh, int chunk,
-                               float* out, float* part, float* sm, double* cs, int tid, int nthreads, Sync sync)
+                               float* out, float* part, float* sm, double* cs, int tid, int nthreads, Sync sync,
+                               Wait wait = Wait{})
 {
     constexpr int LD = HD + 1;
     const int G = p.gqa;
@@ -252,45 +267,80 @@ __device__ __forceinline__ void attention_item(const AttnDev& p, const float* q_
         }                                                                                             \
     }
     MUYO_KV_LOAD_BATCH(0)
-
+    // cos/sin of frequency j = tid at this position (HD / 2 <= 64 < nthreads): table loads issued now.
+    double rc = 0.0, rs = 0.0;
+    if (FUSED && tid < HD / 2 && p.rope_cs) {
+        rc = __ldg(p.rope_cs + (size_t)pos * HD + tid);
+        rs = __ldg(p.rope_cs + (size_t)pos * HD + HD / 2 + tid);
+    }
+    wait();
+    // The projections of this step: rows of q, and the new key and value.
+    constexpr int QP = (kAttnMaxGroup * (HD / 2) + 127) / 128;  // q pairs per thread (nthreads >= 128)
+    constexpr int VP = (HD + 127) / 128;                        // new-value elements per thread
+    float2 qreg[QP];
+    float2 knew = make_float2(0.f, 0.f);
+    float vnew[VP];
     if (FUSED) {
-        for (int j = tid; j < HD / 2; j += nthreads) {
-            double c, s;
-            if (p.rope_cs) {
-                c = __ldg(p.rope_cs + (size_t)pos * HD + j);
-                s = __ldg(p.rope_cs + (size_t)pos * HD + HD / 2 + j);
-            } else {
-                rope_cs_f64(pos, j, HD, p.rope_base, c, s);
+#pragma unroll
+        for (int i = 0; i < QP; ++i) {
+            const int e = tid + i * nthreads;
+            if (e < G * (HD / 2)) {
+                const int g = e / (HD / 2), j = e % (HD / 2);
+                const float* qh = q_in + (size_t)(kvh * G + g) * HD;
+                qreg[i] = make_float2(__ldcg(qh + j), __ldcg(qh + j + HD / 2));
             }
-            cs[j] = c;
-            cs[HD / 2 + j] = s;
-        }
-        sync();
-        const int qd = p.heads * HD, kvd = p.kv_heads * HD;
-        for (int e = tid; e < G * (HD / 2); e += nthreads) {
-            const int g = e / (HD / 2), j = e % (HD / 2);
-            const float* qh = q_in + (size_t)(kvh * G + g) * HD;
-            float y0, y1;
-            rope_pair_f64(__ldcg(qh + j), __ldcg(qh + j + HD / 2), cs[j], cs[HD / 2 + j], y0, y1);
-            Qs[g * HD + j] = y0;
-            Qs[g * HD + j + HD / 2] = y1;
         }
         if (holds_new) {
+            const int qd = p.heads * HD, kvd = p.kv_heads * HD;
             const float* kr = q_in + qd + (size_t)kvh * HD;
             const float* vr = q_in + qd + kvd + (size_t)kvh * HD;
-            for (int j = tid; j < HD / 2; j += nthreads) {
+            if (tid < HD / 2)
+                knew = make_float2(__ldcg(kr + tid), __ldcg(kr + tid + HD / 2));
+#pragma unroll
+            for (int i = 0; i < VP; ++i)
+                if (tid + i * nthreads < HD)
+                    vnew[i] = __ldcg(vr + tid + i * nthreads);
+        }
+    }
+
+    if (FUSED) {
+        if (tid < HD / 2) {
+            if (!p.rope_cs)
+                rope_cs_f64(pos, tid, HD, p.rope_base, rc, rs);
+            cs[tid] = rc;
+            cs[HD / 2 + tid] = rs;
+        }
+        sync();
+#pragma unroll
+        for (int i = 0; i < QP; ++i) {
+            const int e = tid + i * nthreads;
+            if (e < G * (HD / 2)) {
+                const int g = e / (HD / 2), j = e % (HD / 2);
                 float y0, y1;
-                rope_pair_f64(__ldcg(kr + j), __ldcg(kr + j + HD / 2), cs[j], cs[HD / 2 + j], y0, y1);
+                rope_pair_f64(qreg[i].x, qreg[i].y, cs[j], cs[HD / 2 + j], y0, y1);
+                Qs[g * HD + j] = y0;
+                Qs[g * HD + j + HD / 2] = y1;
+            }
+        }
+        if (holds_new) {
+            if (tid < HD / 2) {
+                const int j = tid;
+                float y0, y1;
+                rope_pair_f64(knew.x, knew.y, cs[j], cs[HD / 2 + j], y0, y1);
                 const KV k0 = kv_round<KV>(y0), k1 = kv_round<KV>(y1);
                 kc[head_base + (size_t)pos * HD + j] = k0;
                 kc[head_base + (size_t)pos * HD + j + HD / 2] = k1;
                 Ks[t_new * LD + j] = kv_value<KV>(k0);
                 Ks[t_new * LD + j + HD / 2] = kv_value<KV>(k1);
             }
-            for (int d = tid; d < HD; d += nthreads) {
-                const KV v0 = kv_round<KV>(__ldcg(vr + d));
-                vc[head_base + (size_t)pos * HD + d] = v0;
-                Vs[t_new * LD + d] = kv_value<KV>(v0);
+#pragma unroll
+            for (int i = 0; i < VP; ++i) {
+                const int d = tid + i * nthreads;
+                if (d < HD) {
+                    const KV v0 = kv_round<KV>(vnew[i]);
+                    vc[head_base + (size_t)pos * HD + d] = v0;
+                    Vs[t_new * LD + d] = kv_value<KV>(v0);
+                }
             }
         }
     } else {
@@ -367,7 +417,17 @@ __device__ __forceinline__ void attention_item(const AttnDev& p, const float* q_
     }
 }
 
-// Standalone attention: grid (kv_heads, max_chunks), CTAs past the current chunk count exit.
+struct PdlWaitTrigger {
+    __device__ void operator()() const
+    {
+        pdl_wait();
+        pdl_trigger();
+    }
+};
+
+// Standalone attention: grid (kv_heads, max_chunks), CTAs past the current chunk count exit. The
+// position and the cache rows of earlier steps are read before pdl_wait (they were written two or
+// more kernels back); q_in after it.
 template <typename KV, int HD, bool FUSED, bool INLINE_MERGE>
 __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnDev p, const float* __restrict__ q_in,
                                                              KV* __restrict__ kc, KV* __restrict__ vc,
@@ -386,7 +446,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnDev p, const flo
     if (chunk >= nchunks)
         return;
     attention_item<KV, HD, FUSED>(p, q_in, kc, vc, pos, kvh, chunk, out, part, sm, cs, threadIdx.x, blockDim.x,
-                                  BlockSync{});
+                                  BlockSync{}, PdlWaitTrigger{});
     if (nchunks == 1 || !INLINE_MERGE)
         return;
     // Last CTA of this KV head merges the chunks, then re-arms the counter for the next launch.
@@ -400,7 +460,14 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnDev p, const flo
     if (!last_flag)
         return;
     __threadfence();
-    attn_merge<HD>(p, part, kvh, nchunks, out, threadIdx.x, blockDim.x);
+    if (2 * p.gqa * nchunks <= attn_smem_floats(HD, p.gqa)) {
+        // Batched merge in the (now free) item scratch: one pass of statistics, one of values.
+        float* o = out + (size_t)kvh * p.gqa * HD;
+        attn_merge_heads<HD>(p, part, nchunks, kvh * p.gqa, p.gqa, sm, threadIdx.x, blockDim.x, BlockSync{},
+                             [o](int e, float v) { o[e] = v; });
+    } else {
+        attn_merge<HD>(p, part, kvh, nchunks, out, threadIdx.x, blockDim.x);
+    }
     if (threadIdx.x == 0)
         counters[kvh] = 0;
 }

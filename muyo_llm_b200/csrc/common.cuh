@@ -41,7 +41,7 @@ void clear_error();
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
-inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+__host__ __device__ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Number of SMs of the current device (cached per device).
 int sm_count();
@@ -51,6 +51,15 @@ int sm_count();
 constexpr int WARP = 32;
 
 // 16-byte load of data read once per decode step (weights): no L1 allocation.
+// Programmatic dependent launch. pdl_wait() returns once the grids this one depends on have
+// completed and their writes are visible (at once when the kernel was launched without the
+// programmatic-serialization attribute); pdl_trigger() lets the next kernel on the stream start
+// launching. Kernels here call pdl_trigger() only after their own pdl_wait(), so a kernel's code
+// before its wait may read anything written two or more kernels back, but nothing of the kernel
+// right before it.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ uint4 ld_stream16(const void* p)
 {
     uint4 r;

@@ -3,8 +3,8 @@
 // step as one CUDA graph (src/FullModel.cpp:1096-1208 feedToken/sampleNext, without the host).
 //
 //   k_gemv<EMBED_NORM|NORM, BIAS>  rms_norm (+ embedding gather on layer 0) -> stacked QKV GEMV + bias
-//   k_attention<FUSED>             NeoX RoPE of q and k, KV append, split-K GQA attention
-//   k_gemv<PLAIN, RESIDUAL>        o_proj GEMV + residual add
+//   k_attention<FUSED>             NeoX RoPE of q and k, KV append, split-K GQA attention partials
+//   k_gemv<MERGE, RESIDUAL>        merge of the attention partials -> o_proj GEMV + residual add
 //   k_gemv<NORM, SWIGLU>           rms_norm -> gate and up GEMVs (one pass, two matrices) -> SwiGLU
 //   k_gemv<PLAIN, RESIDUAL>        down_proj GEMV (K split across warps) + residual add
 //   k_gemv<NORM, LOGITS>           final rms_norm -> LM head GEMV -> logits, argmax, next token
@@ -44,8 +44,14 @@ namespace muyo {
 constexpr int kGemvThreads = 256;  // 8 warps
 constexpr int kGemvWarps = kGemvThreads / 32;
 
-enum Prologue { PRO_PLAIN = 0, PRO_NORM = 1, PRO_EMBED_NORM = 2 };
+enum Prologue { PRO_PLAIN = 0, PRO_NORM = 1, PRO_EMBED_NORM = 2, PRO_MERGE = 3 };
 enum Epilogue { EPI_BIAS = 1, EPI_RESIDUAL = 2, EPI_SWIGLU = 3, EPI_LOGITS = 4 };
+
+// Weights of a later kernel to stream into L2 (byte ranges, 16-byte aligned, sizes multiples of 16).
+struct PfSet {
+    const void* p[2];
+    size_t bytes[2];
+};
 
 struct GemvFused {
     // prologue
@@ -57,6 +63,9 @@ struct GemvFused {
     const Control* ctrl_ro;
     int vocab, max_seq;    // EMBED_NORM bounds
     float* x_copy;         // EMBED_NORM: CTA 0 stores the embedded row (the residual stream)
+    const float* attn_part;  // MERGE: split-K attention partials [kv_heads][max_chunks][gqa][hd + 2]
+    const int32_t* pos;      // MERGE: device position (keys 0 .. pos)
+    int hd, gqa, max_chunks; // MERGE: partial layout
     int K;
     // matrices
     const __half* w0;
@@ -71,7 +80,82 @@ struct GemvFused {
     int32_t* counter;   // LOGITS: arrival counter (self-resetting)
     Control* ctrl;      // LOGITS: next-token selection and step advance
     int32_t* tokens_rw;
+    PfSet pf;           // weights of a later kernel: every CTA asks L2 for its slice of them
 };
+
+// Stage the merged attention output (the O projection's input, K = heads * hd) from the split-K
+// partials (m, l, o) of every (head, chunk): per head M = max_c m_c, w_c = exp(m_c - M) / L with
+// L = sum_c l_c exp(m_c - M), then x[h * hd + d] = sum_c o_c[d] w_c. Each pass issues its loads
+// together: the statistics of all heads and chunks, then four chunks of every element a thread
+// owns. `scratch` holds 2 * heads * max_chunks floats.
+__device__ __forceinline__ void stage_merge(const GemvFused& a, float4* xs4, float* scratch)
+{
+    float* xs = reinterpret_cast<float*>(xs4);
+    const int K = a.K, K8 = K / 8, hd = a.hd, G = a.gqa, heads = K / hd, stride = hd + 2;
+    const int tid = threadIdx.x, nt = blockDim.x;
+    const int pos = __ldcg(a.pos);
+    const int nchunks = pos >= 0 && pos < a.max_seq ? (pos + kAttnKeys) / kAttnKeys : 0;
+    auto part_at = [&](int h, int c) { return a.attn_part + ((size_t)((h / G) * a.max_chunks + c) * G + h % G) * stride; };
+    float* mw = scratch;                   // [heads][nchunks]: m, then the normalised weight
+    float* lw = scratch + heads * nchunks; // [heads][nchunks]: l
+    for (int i = tid; i < heads * nchunks; i += nt) {
+        const float* q = part_at(i / nchunks, i % nchunks);
+        mw[i] = __ldcg(q);
+        lw[i] = __ldcg(q + 1);
+    }
+    __syncthreads();
+    for (int h = tid; h < heads; h += nt) {
+        float M = -INFINITY;
+        for (int c = 0; c < nchunks; ++c)
+            M = fmaxf(M, mw[h * nchunks + c]);
+        float L = 0.0f;
+        for (int c = 0; c < nchunks; ++c) {
+            const float l = lw[h * nchunks + c];
+            const float w = l > 0.0f ? expf(mw[h * nchunks + c] - M) : 0.0f;
+            mw[h * nchunks + c] = w;
+            L = fmaf(l, w, L);
+        }
+        const float inv = __fdiv_rn(1.0f, L);
+        for (int c = 0; c < nchunks; ++c)
+            mw[h * nchunks + c] *= inv;
+    }
+    __syncthreads();
+    constexpr int E = 4;  // elements per thread per pass
+    for (int e0 = 0; e0 < K; e0 += E * nt) {
+        float o[E];
+#pragma unroll
+        for (int j = 0; j < E; ++j)
+            o[j] = 0.0f;
+        for (int c = 0; c < nchunks; c += 4) {
+            float v[E][4];
+#pragma unroll
+            for (int j = 0; j < E; ++j) {
+                const int e = e0 + tid + j * nt;
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    v[j][u] = e < K && c + u < nchunks ? __ldcg(part_at(e / hd, c + u) + 2 + e % hd) : 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < E; ++j) {
+                const int e = e0 + tid + j * nt;
+                if (e < K) {
+                    const float* w = mw + (e / hd) * nchunks;
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        if (c + u < nchunks)
+                            o[j] = fmaf(v[j][u], w[c + u], o[j]);
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < E; ++j) {
+            const int e = e0 + tid + j * nt;
+            if (e < K)
+                xs[xs_index(e, K8)] = o[j];
+        }
+    }
+    __syncthreads();
+}
 
 // Stage the GEMV input vector in shared memory (split layout of gemv.cuh). NORM and EMBED_NORM
 // apply the numpy reference's rms_norm, x / sqrt(mean(x^2) + eps) * w (tools/reference_qwen2.py:81-82),
@@ -79,14 +163,37 @@ struct GemvFused {
 template <int PRO>
 __device__ __forceinline__ void stage_input(const GemvFused& a, float* xs, float* red)
 {
-    const int K = a.K, K8 = K / 8;
+    // Every thread issues all loads of a pass (V float4s of x or of the embedding row, and of the
+    // norm weight) before its first store, so a pass costs one memory round trip; K <= 4 * V * 256
+    // takes one pass (8192 plain, 4096 normalised). K is a multiple of 8 (make_shape).
+    constexpr int V = PRO == PRO_PLAIN ? 8 : 4;
+    const int K = a.K, K8 = K / 8, Q = K / 4;
+    float4* xs4 = reinterpret_cast<float4*>(xs);
+    const int tid = threadIdx.x, nt = blockDim.x;
     if (PRO == PRO_PLAIN) {
-        for (int k = threadIdx.x; k < K; k += blockDim.x)
-            xs[xs_index(k, K8)] = a.x[k];
+        const float4* x4 = reinterpret_cast<const float4*>(a.x);
+        for (int q0 = 0; q0 < Q; q0 += V * nt) {
+            float4 v[V];
+#pragma unroll
+            for (int j = 0; j < V; ++j) {
+                const int q = q0 + tid + j * nt;
+                if (q < Q)
+                    v[j] = __ldg(x4 + q);
+            }
+#pragma unroll
+            for (int j = 0; j < V; ++j) {
+                const int q = q0 + tid + j * nt;
+                if (q < Q)
+                    xs4[xs_slot4(q, K8)] = v[j];
+            }
+        }
         __syncthreads();
         return;
     }
-    const float* src = a.x;
+    if (PRO == PRO_MERGE) {
+        stage_merge(a, xs4, xs + K);
+        return;
+    }
     const __half* erow = nullptr;
     if (PRO == PRO_EMBED_NORM) {
         // Ids and positions are bounded on the host; an out-of-range value read here gathers row 0
@@ -97,18 +204,54 @@ __device__ __forceinline__ void stage_input(const GemvFused& a, float* xs, float
             token = 0;
         erow = a.embd + (size_t)token * K;
     }
+    const float4* w4 = reinterpret_cast<const float4*>(a.norm_w);
+    float4 wv[V];  // the norm weights of the first pass, loaded with the inputs
     float ss = 0.0f;
-    for (int k = threadIdx.x; k < K; k += blockDim.x) {
-        const float v = PRO == PRO_EMBED_NORM ? __half2float(erow[k]) : src[k];
-        ss = fmaf(v, v, ss);
-        if (PRO == PRO_EMBED_NORM && blockIdx.x == 0)
-            a.x_copy[k] = v;
+    for (int q0 = 0; q0 < Q; q0 += V * nt) {
+        float4 v[V];
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+            const int q = q0 + tid + j * nt;
+            if (q < Q) {
+                if (PRO == PRO_EMBED_NORM) {
+                    const uint2 h = __ldg(reinterpret_cast<const uint2*>(erow) + q);
+                    const float2 lo = h2_to_f2(h.x), hi = h2_to_f2(h.y);
+                    v[j] = make_float4(lo.x, lo.y, hi.x, hi.y);
+                } else {
+                    v[j] = __ldg(reinterpret_cast<const float4*>(a.x) + q);
+                }
+                if (q0 == 0)
+                    wv[j] = __ldg(w4 + q);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+            const int q = q0 + tid + j * nt;
+            if (q < Q) {
+                ss = fmaf(v[j].x, v[j].x, ss);
+                ss = fmaf(v[j].y, v[j].y, ss);
+                ss = fmaf(v[j].z, v[j].z, ss);
+                ss = fmaf(v[j].w, v[j].w, ss);
+                xs4[xs_slot4(q, K8)] = v[j];
+                if (PRO == PRO_EMBED_NORM && blockIdx.x == 0)
+                    reinterpret_cast<float4*>(a.x_copy)[q] = v[j];
+            }
+        }
     }
     ss = block_sum(ss, red);
     const float s = __fsqrt_rn(__fdiv_rn(ss, (float)K) + a.eps);
-    for (int k = threadIdx.x; k < K; k += blockDim.x) {
-        const float v = PRO == PRO_EMBED_NORM ? __half2float(erow[k]) : src[k];
-        xs[xs_index(k, K8)] = __fdiv_rn(v, s) * a.norm_w[k];
+    // Each thread rescales the float4s it stored itself: x / s * w, as the numpy reference.
+    for (int q0 = 0; q0 < Q; q0 += V * nt) {
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+            const int q = q0 + tid + j * nt;
+            if (q < Q) {
+                const float4 w = q0 == 0 ? wv[j] : __ldg(w4 + q);
+                float4& x = xs4[xs_slot4(q, K8)];
+                x = make_float4(__fdiv_rn(x.x, s) * w.x, __fdiv_rn(x.y, s) * w.y, __fdiv_rn(x.z, s) * w.z,
+                                __fdiv_rn(x.w, s) * w.w);
+            }
+        }
     }
     __syncthreads();
 }
@@ -125,6 +268,34 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvFused a)
     __shared__ int last_flag;
     constexpr int RG = kGemvWarps / KSPLIT;
 
+    // The weights do not depend on the previous kernel: start streaming this CTA's first tile into
+    // L2 while the input is staged.
+    if (threadIdx.x == 0 && (int)blockIdx.x * RG * ROWS < a.rows) {
+        const int r0 = blockIdx.x * RG * ROWS, nr = min(RG * ROWS, a.rows - r0);
+        prefetch_rows_l2(a.w0, a.ldw, r0, nr);
+        if (NMAT > 1)
+            prefetch_rows_l2(a.w1, a.ldw, r0, nr);
+    }
+    if (threadIdx.x == 0) {
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const size_t n = a.pf.bytes[r];
+            const size_t per = (n / gridDim.x + 16) / 16 * 16;
+            const size_t off = (size_t)blockIdx.x * per;
+            if (n > 0 && off < n) {
+                const char* base = static_cast<const char*>(a.pf.p[r]) + off;
+                size_t left = n - off < per ? n - off : per;
+                while (left > 0) {
+                    const uint32_t c = left > 65536 ? 65536u : (uint32_t)left;
+                    prefetch_l2(base, c);
+                    base += c;
+                    left -= c;
+                }
+            }
+        }
+    }
+    pdl_wait();  // the input vector and the epilogue operands come from earlier kernels
+    pdl_trigger();
     stage_input<PRO>(a, xs, red);
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -143,6 +314,16 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvFused a)
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
         const int row0 = (tile * RG + rg) * ROWS;
         const int nvalid = min(ROWS, a.rows - row0);
+        if (threadIdx.x == 0 && tile + (int)gridDim.x < ntiles) {  // the next tile of this CTA, to L2
+            const int r1 = (tile + gridDim.x) * RG * ROWS, nr = min(RG * ROWS, a.rows - r1);
+            prefetch_rows_l2(a.w0, a.ldw, r1, nr);
+            if (NMAT > 1)
+                prefetch_rows_l2(a.w1, a.ldw, r1, nr);
+        }
+        // The epilogue operand of row row0 + lane (bias or residual), loaded before the weights.
+        float epi_op = 0.0f;
+        if ((EPI == EPI_BIAS || EPI == EPI_RESIDUAL) && ks == 0 && lane < ROWS && lane < nvalid)
+            epi_op = EPI == EPI_BIAS ? a.bias[row0 + lane] : a.res[row0 + lane];
         float acc[NMAT][ROWS];
 #pragma unroll
         for (int m = 0; m < NMAT; ++m)
@@ -176,6 +357,10 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvFused a)
             }
             __syncthreads();
         }
+        float epi[ROWS];
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r)
+            epi[r] = __shfl_sync(0xffffffffu, epi_op, r);
         if (ks == 0 && lane == 0 && nvalid > 0) {
 #pragma unroll
             for (int r = 0; r < ROWS; ++r) {
@@ -183,9 +368,9 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvFused a)
                     break;
                 const int row = row0 + r;
                 if (EPI == EPI_BIAS) {
-                    a.y[row] = acc[0][r] + a.bias[row];
+                    a.y[row] = acc[0][r] + epi[r];
                 } else if (EPI == EPI_RESIDUAL) {
-                    a.y[row] = a.res[row] + acc[0][r];
+                    a.y[row] = epi[r] + acc[0][r];
                 } else if (EPI == EPI_SWIGLU) {
                     a.y[row] = silu_mul(acc[0][r], acc[NMAT - 1][r]);
                 } else {  // EPI_LOGITS
@@ -242,17 +427,53 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvFused a)
     }
 }
 
+// Launches kernel k; with pdl the launch carries the programmatic-stream-serialization attribute,
+// so that (inside a captured graph) it may start while the kernel before it drains.
+template <typename... Params, typename... Args>
+static cudaError_t launch_kernel(void (*k)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+                                 Args... args)
+{
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
+// CTAs of kernel k (block threads, smem bytes) resident on the whole device at once.
+template <typename Kernel>
+static int resident_ctas(Kernel k, int threads, size_t smem)
+{
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, threads, smem) != cudaSuccess || per_sm < 1)
+        per_sm = 1;
+    return per_sm * sm_count();
+}
+
+// The grid is capped at the CTAs resident at once: CTAs stride over the tiles, so a tile beyond the
+// first wave reuses an already staged input instead of waiting for a second wave to start.
 template <int ROWS, int U, int NMAT, int KSPLIT, int PRO, int EPI>
-static int launch_gemv(const GemvFused& a, int max_ctas, cudaStream_t s)
+static int launch_gemv(const GemvFused& a, int max_ctas, cudaStream_t s, bool pdl)
 {
     constexpr int RG = kGemvWarps / KSPLIT;
     const int ntiles = (a.rows + RG * ROWS - 1) / (RG * ROWS);
-    const int grid = ntiles < max_ctas ? ntiles : max_ctas;
-    const size_t smem = (size_t)a.K * sizeof(float);
+    size_t smem = (size_t)a.K * sizeof(float);
+    if (PRO == PRO_MERGE)
+        smem += 2 * sizeof(float) * (size_t)(a.K / a.hd) * a.max_chunks;  // merge statistics
     auto k = k_gemv<ROWS, U, NMAT, KSPLIT, PRO, EPI>;
     if (smem > 48 * 1024)
         MUYO_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    k<<<grid, kGemvThreads, smem, s>>>(a);
+    int grid = ntiles < max_ctas ? ntiles : max_ctas;
+    const int resident = resident_ctas(k, kGemvThreads, smem);
+    if (grid > resident)
+        grid = resident;
+    MUYO_CUDA_TRY(launch_kernel(k, dim3(grid), dim3(kGemvThreads), smem, s, pdl, a));
     MUYO_LAUNCH_CHECK();
     return MUYO_OK;
 }
@@ -298,6 +519,8 @@ static int make_shape(const MuyoQwen2Config* c, Shape& s, bool need_vocab)
     MUYO_REQUIRE(!need_vocab || c->vocab > 0, "config: vocab must be positive");
     MUYO_REQUIRE(s.rope_base > 0.0f && s.eps >= 0.0f, "config: rope_base must be > 0 and rms_eps >= 0");
     s.max_chunks = (s.max_seq + kAttnKeys - 1) / kAttnKeys;
+    MUYO_REQUIRE(sizeof(float) * ((size_t)s.q_dim + 2ull * s.heads * s.max_chunks) <= 200 * 1024,
+                 "config: heads x max_seq too large for the attention merge staged in shared memory");
     return MUYO_OK;
 }
 
@@ -353,43 +576,48 @@ struct LayerPtrs {
 
 template <typename KV, int HD>
 static int launch_attention_fused(const Shape& s, const float* qkv, void* kc, void* vc, const int32_t* pos,
-                                  float* out, float* part, int32_t* counters, cudaStream_t st)
+                                  float* out, float* part, int32_t* counters, cudaStream_t st, bool pdl)
 {
     AttnDev p{s.heads, s.kv_heads, s.gqa, s.max_seq, 0, 1.0f / sqrtf((float)s.head_dim), (double)s.rope_base,
               s.max_chunks, s.rope_cs};
     const size_t smem = (size_t)attn_smem_floats(HD, s.gqa) * sizeof(float);
-    auto k = k_attention<KV, HD, true, true>;
+    // Every chunk writes its partial (no output pointer, no inline merge): the O projection merges
+    // them while staging its input.
+    auto k = k_attention<KV, HD, true, false>;
     if (smem > 48 * 1024)
         MUYO_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    k<<<dim3(s.kv_heads, s.max_chunks), kAttnThreads, smem, st>>>(p, qkv, static_cast<KV*>(kc), static_cast<KV*>(vc),
-                                                                   pos, out, part, counters);
+    (void)out;
+    MUYO_CUDA_TRY(launch_kernel(k, dim3(s.kv_heads, s.max_chunks), dim3(kAttnThreads), smem, st, pdl, p, qkv,
+                                static_cast<KV*>(kc), static_cast<KV*>(vc), pos, static_cast<float*>(nullptr), part,
+                                counters));
     MUYO_LAUNCH_CHECK();
     return MUYO_OK;
 }
 
 static int attention_fused(const Shape& s, const float* qkv, void* kc, void* vc, const int32_t* pos, float* out,
-                           float* part, int32_t* counters, cudaStream_t st)
+                           float* part, int32_t* counters, cudaStream_t st, bool pdl)
 {
     if (s.kv_f16) {
         switch (s.head_dim) {
-            case 16: return launch_attention_fused<__half, 16>(s, qkv, kc, vc, pos, out, part, counters, st);
-            case 32: return launch_attention_fused<__half, 32>(s, qkv, kc, vc, pos, out, part, counters, st);
-            case 64: return launch_attention_fused<__half, 64>(s, qkv, kc, vc, pos, out, part, counters, st);
-            default: return launch_attention_fused<__half, 128>(s, qkv, kc, vc, pos, out, part, counters, st);
+            case 16: return launch_attention_fused<__half, 16>(s, qkv, kc, vc, pos, out, part, counters, st, pdl);
+            case 32: return launch_attention_fused<__half, 32>(s, qkv, kc, vc, pos, out, part, counters, st, pdl);
+            case 64: return launch_attention_fused<__half, 64>(s, qkv, kc, vc, pos, out, part, counters, st, pdl);
+            default: return launch_attention_fused<__half, 128>(s, qkv, kc, vc, pos, out, part, counters, st, pdl);
         }
     }
     switch (s.head_dim) {
-        case 16: return launch_attention_fused<float, 16>(s, qkv, kc, vc, pos, out, part, counters, st);
-        case 32: return launch_attention_fused<float, 32>(s, qkv, kc, vc, pos, out, part, counters, st);
-        case 64: return launch_attention_fused<float, 64>(s, qkv, kc, vc, pos, out, part, counters, st);
-        default: return launch_attention_fused<float, 128>(s, qkv, kc, vc, pos, out, part, counters, st);
+        case 16: return launch_attention_fused<float, 16>(s, qkv, kc, vc, pos, out, part, counters, st, pdl);
+        case 32: return launch_attention_fused<float, 32>(s, qkv, kc, vc, pos, out, part, counters, st, pdl);
+        case 64: return launch_attention_fused<float, 64>(s, qkv, kc, vc, pos, out, part, counters, st, pdl);
+        default: return launch_attention_fused<float, 128>(s, qkv, kc, vc, pos, out, part, counters, st, pdl);
     }
 }
 
 // One decoder layer: x_in (or the embedding of tokens[ctrl->step] when embed != nullptr) -> x_out.
 static int layer_forward(const Shape& s, const LayerPtrs& w, void* kc, void* vc, const int32_t* pos,
                          const float* x_in, float* x_out, const LayerScratch& ws, const __half* embd,
-                         const int32_t* tokens, const Control* ctrl, float* embed_out, cudaStream_t st)
+                         const int32_t* tokens, const Control* ctrl, float* embed_out, cudaStream_t st, bool pdl,
+                         const PfSet* pf = nullptr)
 {
     const int sms = sm_count();
     int rc;
@@ -404,6 +632,8 @@ static int layer_forward(const Shape& s, const LayerPtrs& w, void* kc, void* vc,
     a.rows = s.qkv_rows;
     a.bias = w.bqkv;
     a.y = ws.qkv;
+    if (pf)
+        a.pf = pf[0];
     if (embd) {
         a.embd = embd;
         a.tokens = tokens;
@@ -411,27 +641,34 @@ static int layer_forward(const Shape& s, const LayerPtrs& w, void* kc, void* vc,
         a.vocab = s.vocab;
         a.max_seq = s.max_seq;
         a.x_copy = embed_out;
-        rc = launch_gemv<1, 4, 1, 1, PRO_EMBED_NORM, EPI_BIAS>(a, sms * 8, st);
+        rc = launch_gemv<1, 4, 1, 1, PRO_EMBED_NORM, EPI_BIAS>(a, sms * 8, st, pdl);
     } else {
-        rc = launch_gemv<1, 4, 1, 1, PRO_NORM, EPI_BIAS>(a, sms * 8, st);
+        rc = launch_gemv<1, 4, 1, 1, PRO_NORM, EPI_BIAS>(a, sms * 8, st, pdl);
     }
     if (rc)
         return rc;
     const float* residual = embd ? embed_out : x_in;
     // 2. rope + KV append + attention
-    rc = attention_fused(s, ws.qkv, kc, vc, pos, ws.attn, ws.part, ws.counters, st);
+    rc = attention_fused(s, ws.qkv, kc, vc, pos, ws.attn, ws.part, ws.counters, st, pdl);
     if (rc)
         return rc;
-    // 3. o_proj + residual
+    // 3. merge of the attention partials -> o_proj + residual
     GemvFused o{};
-    o.x = ws.attn;
+    o.attn_part = ws.part;
+    o.pos = pos;
+    o.hd = s.head_dim;
+    o.gqa = s.gqa;
+    o.max_chunks = s.max_chunks;
+    o.max_seq = s.max_seq;
     o.K = s.q_dim;
     o.w0 = w.wo;
     o.ldw = s.q_dim;
     o.rows = s.hidden;
     o.res = residual;
     o.y = ws.h1;
-    rc = launch_gemv<1, 4, 1, 2, PRO_PLAIN, EPI_RESIDUAL>(o, sms * 8, st);
+    if (pf)
+        o.pf = pf[1];
+    rc = launch_gemv<1, 4, 1, 2, PRO_MERGE, EPI_RESIDUAL>(o, sms * 8, st, pdl);
     if (rc)
         return rc;
     // 4. rms_norm -> gate, up -> SwiGLU
@@ -445,7 +682,9 @@ static int layer_forward(const Shape& s, const LayerPtrs& w, void* kc, void* vc,
     g.ldw = s.hidden;
     g.rows = s.ffn;
     g.y = ws.act;
-    rc = launch_gemv<1, 4, 2, 1, PRO_NORM, EPI_SWIGLU>(g, sms * 8, st);
+    if (pf)
+        g.pf = pf[2];
+    rc = launch_gemv<1, 4, 2, 1, PRO_NORM, EPI_SWIGLU>(g, sms * 8, st, pdl);
     if (rc)
         return rc;
     // 5. down_proj + residual
@@ -457,7 +696,9 @@ static int layer_forward(const Shape& s, const LayerPtrs& w, void* kc, void* vc,
     d.rows = s.hidden;
     d.res = ws.h1;
     d.y = x_out;
-    return launch_gemv<1, 4, 1, 4, PRO_PLAIN, EPI_RESIDUAL>(d, sms * 8, st);
+    if (pf)
+        d.pf = pf[3];
+    return launch_gemv<1, 4, 1, 4, PRO_PLAIN, EPI_RESIDUAL>(d, sms * 8, st, pdl);
 }
 
 // ---- model ------------------------------------------------------------------------------------------
@@ -498,6 +739,8 @@ struct MuyoModel {
     int32_t host_pos = 0;
     bool finalized = false;
     int engine = 1;                 // 0: persistent kernel, 1: CUDA graph of per-phase kernels (default)
+    bool pdl = true;                // graph engine: kernels launch early and prefetch their weights
+    bool prefetch_ahead = true;     // graph engine: each GEMV streams a later kernel's weights into L2
     double* rope_cs = nullptr;      // [max_seq][head_dim] cos/sin table (float64)
     muyo::PLayer* d_layers = nullptr;
     unsigned* bar = nullptr;        // persistent kernel grid-barrier counter
@@ -537,15 +780,37 @@ static int record_step(MuyoModel* m, cudaStream_t st)
     const Shape& s = m->s;
     const int32_t* pos = &m->ctrl->step;
     int rc;
+    // The GEMV kernels of a step in launch order (QKV, O, gate/up, down per layer, then the LM head),
+    // each with its weights. Kernel k asks L2 for the weights of kernel k + 2 (the step is replayed,
+    // so the last kernels fetch the first ones of the next step), except for the LM head's, which
+    // are larger than L2 and are streamed by the LM head itself.
+    std::vector<PfSet> mats;
+    const size_t hid = s.hidden, ffn = s.ffn;
+    for (int l = 0; l < s.layers; ++l) {
+        const LayerPtrs w = layer_ptrs(m, l);
+        mats.push_back(PfSet{{w.wqkv, nullptr}, {(size_t)s.qkv_rows * hid * 2, 0}});
+        mats.push_back(PfSet{{w.wo, nullptr}, {hid * (size_t)s.q_dim * 2, 0}});
+        mats.push_back(PfSet{{w.wgate, w.wup}, {ffn * hid * 2, ffn * hid * 2}});
+        mats.push_back(PfSet{{w.wdown, nullptr}, {hid * ffn * 2, 0}});
+    }
+    const size_t n_mats = mats.size() + 1;  // + the LM head
+    std::vector<PfSet> plan(n_mats, PfSet{{nullptr, nullptr}, {0, 0}});
+    if (m->prefetch_ahead)
+        for (size_t k = 0; k < n_mats; ++k) {
+            const size_t t = (k + 2) % n_mats;
+            if (t < mats.size())
+                plan[k] = mats[t];
+        }
     for (int l = 0; l < s.layers; ++l) {
         const LayerPtrs w = layer_ptrs(m, l);
         char* kc = static_cast<char*>(m->kc) + m->kv_layer_bytes * l;
         char* vc = static_cast<char*>(m->vc) + m->kv_layer_bytes * l;
         if (l == 0)
             rc = layer_forward(s, w, kc, vc, pos, nullptr, m->h, m->ls, W(m, "token_embd.weight"), m->tokens,
-                               m->ctrl, m->ls.h1 /*embedding row lands in h1 first*/, st);
+                               m->ctrl, m->ls.h1 /*embedding row lands in h1 first*/, st, m->pdl, &plan[4 * l]);
         else
-            rc = layer_forward(s, w, kc, vc, pos, m->h, m->h, m->ls, nullptr, nullptr, nullptr, nullptr, st);
+            rc = layer_forward(s, w, kc, vc, pos, m->h, m->h, m->ls, nullptr, nullptr, nullptr, nullptr, st, m->pdl,
+                               &plan[4 * l]);
         if (rc)
             return rc;
     }
@@ -563,7 +828,8 @@ static int record_step(MuyoModel* m, cudaStream_t st)
     a.ctrl = m->ctrl;
     a.tokens_rw = m->tokens;
     a.max_seq = s.max_seq;
-    return launch_gemv<2, 4, 1, 1, PRO_NORM, EPI_LOGITS>(a, m->lm_grid, st);
+    a.pf = plan[n_mats - 1];
+    return launch_gemv<2, 4, 1, 1, PRO_NORM, EPI_LOGITS>(a, m->lm_grid, st, m->pdl);
 }
 
 // ---- persistent engine ----------------------------------------------------------------------------
@@ -841,6 +1107,8 @@ extern "C" int muyo_cuda_layer_step(const MuyoQwen2Config* c, const MuyoLayerWei
     MUYO_REQUIRE(aligned16(w->wqkv) && aligned16(w->wo) && aligned16(w->wgate) && aligned16(w->wup) &&
                      aligned16(w->wdown),
                  "layer_step: weight matrices must be 16-byte aligned");
+    MUYO_REQUIRE(aligned16(w->attn_norm) && aligned16(w->ffn_norm) && aligned16(x_in) && aligned16(x_out),
+                 "layer_step: norm weights, x_in and x_out must be 16-byte aligned");
     const size_t need = layer_scratch_bytes(s);
     MUYO_REQUIRE(workspace && workspace_bytes >= need, "layer_step: workspace of %zu bytes needed, %zu given", need,
                  workspace_bytes);
@@ -854,7 +1122,7 @@ extern "C" int muyo_cuda_layer_step(const MuyoQwen2Config* c, const MuyoLayerWei
                  static_cast<const __half*>(w->wup),
                  static_cast<const __half*>(w->wdown)};
     return layer_forward(s, lp, k_cache, v_cache, pos, x_in, x_out, carve_layer_scratch(s, workspace), nullptr, nullptr,
-                         nullptr, nullptr, as_stream(stream));
+                         nullptr, nullptr, as_stream(stream), false);
 }
 
 // ---- extern "C": model ---------------------------------------------------------------------------------
@@ -1300,6 +1568,18 @@ extern "C" int muyo_model_set_option(MuyoModel* m, const char* key, int value)
     if (k == "engine") {
         MUYO_REQUIRE(value == 0 || value == 1, "set_option: engine must be 0 (persistent) or 1 (graph)");
         m->engine = value;
+        return MUYO_OK;
+    }
+    if (k == "prefetch") {
+        MUYO_REQUIRE(value == 0 || value == 1, "set_option: prefetch must be 0 or 1");
+        MUYO_REQUIRE(!m->exec, "set_option: prefetch must be set before muyo_model_finalize");
+        m->prefetch_ahead = value != 0;
+        return MUYO_OK;
+    }
+    if (k == "pdl") {
+        MUYO_REQUIRE(value == 0 || value == 1, "set_option: pdl must be 0 or 1");
+        MUYO_REQUIRE(!m->exec, "set_option: pdl must be set before muyo_model_finalize");
+        m->pdl = value != 0;
         return MUYO_OK;
     }
     MUYO_REQUIRE(false, "set_option: unknown option %s", key);

@@ -25,6 +25,31 @@ __device__ __forceinline__ int xs_index(int k, int K8)
     return j < 4 ? c * 4 + j : K8 * 4 + c * 4 + (j - 4);
 }
 
+// float4 q of a K-vector (elements 4q .. 4q+3) in the split layout above, as a float4 index: the
+// first half of chunk q/2 when q is even, the second half when q is odd.
+__device__ __forceinline__ int xs_slot4(int q, int K8) { return (q & 1) ? K8 + (q >> 1) : (q >> 1); }
+
+// Asks L2 to start fetching `bytes` (a multiple of 16) from the 16-byte-aligned global address p;
+// no registers or shared memory are involved and the call does not wait.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes)
+{
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Rows [row0, row0 + nrows) of a row-major F16 matrix with row stride ldw elements (ldw % 8 == 0),
+// prefetched to L2 in pieces of at most 64 KB.
+__device__ __forceinline__ void prefetch_rows_l2(const __half* w, size_t ldw, int row0, int nrows)
+{
+    const char* p = reinterpret_cast<const char*>(w + (size_t)row0 * ldw);
+    size_t left = (size_t)nrows * ldw * sizeof(__half);
+    while (left > 0) {
+        const uint32_t n = left > 65536 ? 65536u : (uint32_t)left;
+        prefetch_l2(p, n);
+        p += n;
+        left -= n;
+    }
+}
+
 template <int ROWS, int U, int NMAT>
 struct GemvArgs {
     const __half* w[NMAT];

@@ -39,6 +39,38 @@ __device__ __forceinline__ float fuse_bias(const MatVecDev& p, float v, const fl
     return v;
 }
 
+// Stages x (n floats) in the split layout of gemv.cuh. With a 16-byte-aligned x each thread issues
+// all its float4 loads of a pass before its first store, so a pass costs one memory round trip.
+__device__ __forceinline__ void stage_x_split(float* xs, const float* x, int n, int k8)
+{
+    if (k8 > 0 && aligned16(x)) {
+        constexpr int V = 4;
+        const int Q = 2 * k8;
+        const float4* x4 = reinterpret_cast<const float4*>(x);
+        float4* xs4 = reinterpret_cast<float4*>(xs);
+        for (int q0 = 0; q0 < Q; q0 += V * blockDim.x) {
+            float4 v[V];
+#pragma unroll
+            for (int j = 0; j < V; ++j) {
+                const int q = q0 + threadIdx.x + j * blockDim.x;
+                if (q < Q)
+                    v[j] = __ldg(x4 + q);
+            }
+#pragma unroll
+            for (int j = 0; j < V; ++j) {
+                const int q = q0 + threadIdx.x + j * blockDim.x;
+                if (q < Q)
+                    xs4[xs_slot4(q, k8)] = v[j];
+            }
+        }
+        for (int k = 8 * k8 + threadIdx.x; k < n; k += blockDim.x)
+            xs[k] = x[k];
+    } else {
+        for (int k = threadIdx.x; k < n; k += blockDim.x)
+            xs[xs_index(k, k8)] = x[k];
+    }
+}
+
 template <int ROWS, int U>
 __global__ void __launch_bounds__(kThreads) k_mat_vec_f16(MatVecDev p, const __half* __restrict__ A,
                                                           const float* __restrict__ B, float* __restrict__ D,
@@ -48,13 +80,21 @@ __global__ void __launch_bounds__(kThreads) k_mat_vec_f16(MatVecDev p, const __h
     const int b = blockIdx.y;
     const __half* Ab = A + batch_a_index(p, b) * p.batch_stride_a;
     const float* Bb = B + (long long)b * p.batch_stride_b;
-    for (int k = threadIdx.x; k < p.ncols; k += blockDim.x)
-        xs[xs_index(k, p.k8)] = Bb[k];
-    __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int block_rows = nw * ROWS, stride_rows = gridDim.x * block_rows;
+    // The vector path's rows are 16-byte aligned: start streaming this CTA's first row block into L2
+    // while x is staged.
+    if (p.k8 > 0 && threadIdx.x == 0 && (int)blockIdx.x * block_rows < p.rows)
+        prefetch_rows_l2(Ab, (size_t)p.stride_a, blockIdx.x * block_rows,
+                         min(block_rows, p.rows - (int)blockIdx.x * block_rows));
+    stage_x_split(xs, Bb, p.ncols, p.k8);
+    __syncthreads();
     GemvArgs<ROWS, U, 1> ga{{Ab}, (size_t)p.stride_a};
-    for (int row0 = (blockIdx.x * nw + warp) * ROWS; row0 < p.rows; row0 += gridDim.x * nw * ROWS) {
+    for (int row0 = (blockIdx.x * nw + warp) * ROWS; row0 < p.rows; row0 += stride_rows) {
         const int nvalid = min(ROWS, p.rows - row0);
+        const int next0 = row0 - warp * ROWS + stride_rows;  // the CTA's next row block
+        if (p.k8 > 0 && warp == 0 && lane == 0 && next0 < p.rows)
+            prefetch_rows_l2(Ab, (size_t)p.stride_a, next0, min(block_rows, p.rows - next0));
         float acc[1][ROWS];
 #pragma unroll
         for (int r = 0; r < ROWS; ++r)
@@ -321,6 +361,42 @@ __global__ void __launch_bounds__(kThreads) k_rms_norm(Dims4 A, Dims4 W, Dims4 D
         dr[c * D.nb[0]] = ar[c * A.nb[0]] * scale * w[(c % W.ne[0]) * W.nb[0]];
 }
 
+// Contiguous rows of n4 float4s with a weight of the same length: each thread holds its V float4s of
+// the row in registers between the sum of squares and the scaled write, so the row is read from
+// memory once. Same arithmetic as k_rms_norm.
+template <int V>
+__global__ void __launch_bounds__(kThreads) k_rms_norm_rows(const float4* __restrict__ a, const float4* __restrict__ w,
+                                                            float4* __restrict__ d, int n4, float eps)
+{
+    __shared__ float red[32];
+    const float4* ar = a + (long long)blockIdx.x * n4;
+    float4* dr = d + (long long)blockIdx.x * n4;
+    float4 v[V];
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+        const int c = threadIdx.x + j * kThreads;
+        v[j] = c < n4 ? ld_stream16f(ar + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+        ss = fmaf(v[j].x, v[j].x, ss);
+        ss = fmaf(v[j].y, v[j].y, ss);
+        ss = fmaf(v[j].z, v[j].z, ss);
+        ss = fmaf(v[j].w, v[j].w, ss);
+    }
+    ss = block_sum(ss, red);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(ss, (float)(4 * n4)) + eps));
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+        const int c = threadIdx.x + j * kThreads;
+        if (c < n4) {
+            const float4 g = __ldg(w + c);
+            dr[c] = make_float4(v[j].x * scale * g.x, v[j].y * scale * g.y, v[j].z * scale * g.z, v[j].w * scale * g.w);
+        }
+    }
+}
+
 template <typename T>
 __device__ __forceinline__ float to_f32(T v);
 template <>
@@ -381,6 +457,16 @@ __global__ void k_swiglu(GluDev p, const float* __restrict__ a, const float* __r
             u = p.mode == MUYO_GLU_HALVES ? a[sa + off] : a[sa];
         }
         d[sd] = silu_mul(g, u);
+    }
+}
+
+// Split mode with gate, up and output all dense: one flat float4 stream, no index arithmetic.
+__global__ void k_swiglu_flat(const float4* __restrict__ a, const float4* __restrict__ b, float4* __restrict__ d,
+                              long long n4)
+{
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+        const float4 g = ld_stream16f(a + i), u = ld_stream16f(b + i);
+        d[i] = make_float4(silu_mul(g.x, u.x), silu_mul(g.y, u.y), silu_mul(g.z, u.z), silu_mul(g.w, u.w));
     }
 }
 
@@ -552,6 +638,42 @@ __global__ void __launch_bounds__(kThreads) k_argmax_partial(const float* __rest
     }
 }
 
+// Stage 1 for rows whose length is a multiple of 4 and whose base is 16-byte aligned: the CTA's
+// kArgmaxChunk logits as float4 loads, all of a thread's loads issued before its compares.
+constexpr int kArgmaxVec = kArgmaxChunk / 4 / kThreads;  // float4s per thread
+__global__ void __launch_bounds__(kThreads) k_argmax_partial4(const float* __restrict__ a, int KX, int per_row,
+                                                              int index_base, ArgPair* __restrict__ part)
+{
+    const int row = blockIdx.y, blk = blockIdx.x;
+    const float4* ar = reinterpret_cast<const float4*>(a + (long long)row * KX);
+    const int q0 = blk * (kArgmaxChunk / 4), q1 = min(KX / 4, q0 + kArgmaxChunk / 4);
+    float4 v[kArgmaxVec];
+#pragma unroll
+    for (int j = 0; j < kArgmaxVec; ++j) {
+        const int q = q0 + threadIdx.x + j * kThreads;
+        v[j] = q < q1 ? ld_stream16f(ar + q) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    }
+    float bv = -INFINITY;
+    int bi = INT_MAX;
+#pragma unroll
+    for (int j = 0; j < kArgmaxVec; ++j) {
+        const int q = q0 + threadIdx.x + j * kThreads;
+        if (q < q1) {
+            const float e[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+                if (pair_better(e[t], 4 * q + t, bv, bi))
+                    bv = e[t], bi = 4 * q + t;
+        }
+    }
+    ArgPair r = block_argmax(bv, bi);
+    if (threadIdx.x == 0) {
+        if (r.i != INT_MAX)
+            r.i += index_base;
+        part[(long long)row * per_row + blk] = r;
+    }
+}
+
 // Reduces n pairs per row; writes the index (0 when no value compares, e.g. all NaN, as the
 // host's scan that starts from index 0 would return).
 __global__ void __launch_bounds__(kThreads) k_argmax_final(const ArgPair* __restrict__ part, int n,
@@ -662,7 +784,23 @@ extern "C" int muyo_cuda_rms_norm(const MuyoBinaryParams* p, const float* a, con
     MUYO_REQUIRE(p->param1 >= 0.0f, "rms_norm: eps must be >= 0");
     const long long rows = (long long)A.ne[1] * A.ne[2] * A.ne[3];
     MUYO_REQUIRE(rows <= INT_MAX, "rms_norm: too many rows");
-    k_rms_norm<<<(unsigned)rows, kThreads, 0, as_stream(stream)>>>(A, W, D, a, w, d, p->param1);
+    const int n = A.ne[0], n4 = n / 4;
+    const cudaStream_t s = as_stream(stream);
+    if (contiguous(A) && contiguous(D) && W.ne[0] == n && W.nb[0] == 1 && n % 4 == 0 && n4 <= 8 * kThreads &&
+        aligned16(a) && aligned16(w) && aligned16(d)) {
+        const float4 *a4 = reinterpret_cast<const float4*>(a), *w4 = reinterpret_cast<const float4*>(w);
+        float4* d4 = reinterpret_cast<float4*>(d);
+        if (n4 <= kThreads)
+            k_rms_norm_rows<1><<<(unsigned)rows, kThreads, 0, s>>>(a4, w4, d4, n4, p->param1);
+        else if (n4 <= 2 * kThreads)
+            k_rms_norm_rows<2><<<(unsigned)rows, kThreads, 0, s>>>(a4, w4, d4, n4, p->param1);
+        else if (n4 <= 4 * kThreads)
+            k_rms_norm_rows<4><<<(unsigned)rows, kThreads, 0, s>>>(a4, w4, d4, n4, p->param1);
+        else
+            k_rms_norm_rows<8><<<(unsigned)rows, kThreads, 0, s>>>(a4, w4, d4, n4, p->param1);
+    } else {
+        k_rms_norm<<<(unsigned)rows, kThreads, 0, s>>>(A, W, D, a, w, d, p->param1);
+    }
     MUYO_LAUNCH_CHECK();
     return MUYO_OK;
 }
@@ -727,7 +865,23 @@ extern "C" int muyo_cuda_swiglu(const MuyoGluParams* p, const float* a, const fl
         g.nb1[0] = 1;
     if (!g.nb2[0])
         g.nb2[0] = 1;
-    k_swiglu<<<grid_for(g.N), kThreads, 0, as_stream(stream)>>>(g, a, b, d);
+    // Flat when element i of D, A and B sits at offset i of each: unit element stride, and each row
+    // level that the N elements reach is packed right after the level below it.
+    const long long rows_n = (g.N + g.ne20 - 1) / g.ne20;
+    auto dense = [&](const long long* nb) {
+        return nb[0] == 1 && (g.ne21 == 1 || nb[1] == g.ne20) &&
+               (g.ne22 == 1 || nb[2] == (long long)g.ne20 * g.ne21) &&
+               (rows_n <= (long long)g.ne21 * g.ne22 || nb[3] == (long long)g.ne20 * g.ne21 * g.ne22);
+    };
+    const cudaStream_t s = as_stream(stream);
+    if (g.mode == MUYO_GLU_SPLIT && g.N % 4 == 0 && dense(g.nb0) && dense(g.nb1) && dense(g.nb2) && aligned16(a) &&
+        aligned16(b) && aligned16(d)) {
+        k_swiglu_flat<<<grid_for(g.N / 4), kThreads, 0, s>>>(reinterpret_cast<const float4*>(a),
+                                                             reinterpret_cast<const float4*>(b),
+                                                             reinterpret_cast<float4*>(d), g.N / 4);
+    } else {
+        k_swiglu<<<grid_for(g.N), kThreads, 0, s>>>(g, a, b, d);
+    }
     MUYO_LAUNCH_CHECK();
     return MUYO_OK;
 }
@@ -819,7 +973,10 @@ static int argmax_launch(const float* a, uint32_t KX, uint32_t KY, int index_bas
                          cudaStream_t s)
 {
     const int per_row = argmax_blocks(KX);
-    k_argmax_partial<<<dim3(per_row, KY), kThreads, 0, s>>>(a, (int)KX, per_row, index_base, part);
+    if (KX % 4 == 0 && aligned16(a))
+        k_argmax_partial4<<<dim3(per_row, KY), kThreads, 0, s>>>(a, (int)KX, per_row, index_base, part);
+    else
+        k_argmax_partial<<<dim3(per_row, KY), kThreads, 0, s>>>(a, (int)KX, per_row, index_base, part);
     MUYO_LAUNCH_CHECK();
     if (d) {
         k_argmax_final<<<KY, kThreads, 0, s>>>(part, per_row, d);

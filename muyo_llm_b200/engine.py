@@ -26,7 +26,8 @@ class Qwen2Model:
     ENGINE_PERSISTENT, ENGINE_GRAPH = 0, 1
 
     def __init__(self, cfg: Qwen2Config, tensors: dict | None = None, gguf_path: str | None = None,
-                 kv_dtype: int = _abi.KV_F16, device: int = 0, engine: int = 1):
+                 kv_dtype: int = _abi.KV_F16, device: int = 0, engine: int = 1, pdl: bool = True,
+                 prefetch: bool = True):
         self.cfg = cfg
         self.kv_dtype = kv_dtype
         self._cfg = config_struct(cfg, kv_dtype)
@@ -43,6 +44,8 @@ class Qwen2Model:
                     a = np.ascontiguousarray(arr)
                     _abi.call("muyo_model_set_tensor", self._m, name.encode(), a.ctypes.data, a.nbytes)
             _abi.call("muyo_model_set_option", self._m, b"engine", engine)
+            _abi.call("muyo_model_set_option", self._m, b"pdl", 1 if pdl else 0)
+            _abi.call("muyo_model_set_option", self._m, b"prefetch", 1 if prefetch else 0)
             _abi.call("muyo_model_finalize", self._m, None)
         except Exception:
             self.close()

@@ -166,3 +166,26 @@ def test_engines_agree_on_05b_arch(cuda, kv_dtype):
     # differences); with an F16 cache such a difference can flip an F16 rounding of a key or value.
     tol = 1e-4 if kv_dtype == _abi.KV_F32 else 1e-3
     assert_rel_close(outs[0][1], outs[1][1], tol, "step-0 logits, persistent vs graph")
+
+
+@pytest.mark.parametrize("kv_dtype", [_abi.KV_F32, _abi.KV_F16])
+def test_graph_engine_pdl_and_prefetch_are_bit_identical(cuda, tiny, kv_dtype):
+    """Programmatic dependent launch and the L2 prefetch of later kernels' weights change when
+    kernels start and where weights are cached, not what is computed: ids and logits of the graph
+    engine with both off and both on are bit-identical, on the tiny model and on an
+    0.5B-architecture sequence of 81 positions (two 64-key attention chunks, so the merge runs)."""
+    g, t = tiny
+    cfg = synth.QWEN2_05B
+    big = synth.make_model(cfg, 20261201)
+    for c, tensors, prompt, n in [(synth.QWEN2_TINY, t, [int(i) for i in g["ids"][:5]], 50),
+                                  (cfg, big, synth.prompt_ids(20261201, 8, cfg.vocab), 72)]:
+        runs = []
+        for pdl in (False, True):
+            m = engine.Qwen2Model(c, tensors, kv_dtype=kv_dtype, engine=engine.Qwen2Model.ENGINE_GRAPH, pdl=pdl,
+                                  prefetch=pdl)
+            ids = m.generate(prompt, n)
+            _, logits = m.step(int(ids[-1]))
+            runs.append((ids, logits))
+            m.close()
+        assert list(runs[0][0]) == list(runs[1][0])
+        assert np.array_equal(runs[0][1], runs[1][1])

@@ -145,7 +145,8 @@ def test_add_broadcast(cuda):
 
 
 @pytest.mark.parametrize("rows,cols,pattern", [(8, 512, "reference"), (1, 896, "normal"), (8, 512, "normal"),
-                                               (3, 4096, "normal"), (2, 37, "normal")])
+                                               (3, 4096, "normal"), (2, 37, "normal"), (4, 8192, "normal"),
+                                               (2, 8196, "normal"), (5, 1000, "normal")])
 def test_rms_norm(cuda, oracle_mod, rows, cols, pattern):
     if pattern == "reference":  # src/RmsNorm.cpp:60-72, tol 1e-4
         r, c = np.meshgrid(np.arange(rows), np.arange(cols), indexing="ij")
@@ -167,6 +168,34 @@ def test_swiglu(cuda, oracle_mod):
         d = torch.empty(gg.size, dtype=torch.float32, device="cuda")
         nodes.swiglu(nodes.swiglu_params(gg.size), dev(gg), dev(uu), d)
         assert_rel_close(host(d), oracle_mod.swiglu(gg, uu), 1e-5, "swiglu")
+
+
+def test_rms_norm_strided_rows(cuda, oracle_mod):
+    """Rows with a padded stride take the general kernel; the dense fast path must not be chosen."""
+    rows, cols, ld = 3, 512, 520
+    x = synth.normal_f32(SEED, "rnpad", (rows, ld))
+    w = synth.normal_f32(SEED, "rwpad", (cols,))
+    p = nodes.rms_norm_params(cols, 1e-6, rows)
+    p.nb01, p.nb02, p.nb03 = ld, ld * rows, ld * rows
+    d = torch.zeros(rows * cols, dtype=torch.float32, device="cuda")
+    nodes.rms_norm(p, dev(x), dev(w), d)
+    assert_rel_close(host(d).reshape(rows, cols), oracle_mod.rms_norm(np.ascontiguousarray(x[:, :cols]), w, 1e-6),
+                     1e-4, "rms_norm strided")
+
+
+@pytest.mark.parametrize("rows,count,pad", [(5, 1000, 0), (3, 4864, 0), (3, 1000, 8), (2, 1002, 0)])
+def test_swiglu_rows(cuda, oracle_mod, rows, count, pad):
+    """Split mode over several rows: dense rows take the flat float4 path, padded or odd rows the general one."""
+    ld = count + pad
+    g = synth.normal_f32(SEED, f"gr{rows}x{ld}", (rows, ld))
+    u = synth.normal_f32(SEED, f"ur{rows}x{ld}", (rows, ld))
+    p = nodes.swiglu_params(count, rows=rows)
+    p.nb01, p.nb11 = ld, ld
+    p.nb02 = p.nb03 = p.nb12 = p.nb13 = ld * rows
+    d = torch.empty(rows * count, dtype=torch.float32, device="cuda")
+    nodes.swiglu(p, dev(g), dev(u), d)
+    exp = oracle_mod.swiglu(np.ascontiguousarray(g[:, :count]), np.ascontiguousarray(u[:, :count]))
+    assert_rel_close(host(d).reshape(rows, count), exp, 1e-5, "swiglu rows")
 
 
 def test_swiglu_halves_modes(cuda, oracle_mod):
@@ -284,6 +313,17 @@ def test_argmax_ties_first_index(cuda, oracle_mod):
     assert _argmax_gpu(np.zeros(100, np.float32))[0] == 0
     rows = synth.normal_f32(SEED, "argrows", (5, 20000))
     assert list(_argmax_gpu(rows.reshape(-1), rows=5)) == [oracle_mod.argmax(r) for r in rows]
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 151937), (3, 99), (2, 8193), (4, 8192), (1, 5)])
+def test_argmax_scalar_and_vector_paths(cuda, oracle_mod, rows, cols):
+    """Row lengths that are not a multiple of 4 take the scalar scan; the others the float4 scan."""
+    x = synth.normal_f32(SEED, f"am{rows}x{cols}", (rows, cols))
+    x[:, -1] = 7.5  # the last column, on the ragged edge of both scans
+    if rows > 1:
+        x[1, 0] = 9.0
+    got = _argmax_gpu(x.reshape(-1), rows=rows)
+    assert list(got) == [oracle_mod.argmax(r) for r in x]
 
 
 def test_get_rows(cuda, oracle_mod):
