@@ -268,6 +268,10 @@ int muyo_model_create(const MuyoQwen2Config* c, int device, MuyoModel** out);
 int muyo_model_set_tensor(MuyoModel* m, const char* name, const void* host, size_t bytes);
 /* Load every tensor from a Qwen2 GGUF file (F16/F32 tensors, src/Gguf.cpp:337-348). */
 int muyo_model_load_gguf(MuyoModel* m, const char* path);
+/* Replaces ReadQwen2Config (src/FullModel.cpp:84-105): the qwen2.* dimensions, rms epsilon and
+ * rope base of a GGUF file, and the vocabulary size as the length of tokenizer.ggml.tokens; the
+ * cache capacity and KV type are the caller's. Reads the metadata only (no device work). */
+int muyo_gguf_read_qwen2_config(const char* path, uint32_t max_seq, uint32_t kv_dtype, MuyoQwen2Config* out);
 /* Check every tensor is present and build the step graph. */
 int muyo_model_finalize(MuyoModel* m, void* stream);
 /* Empty the KV cache (positions restart at 0). */
@@ -298,7 +302,8 @@ int muyo_model_destroy(MuyoModel* m);
  * "pdl" = 1 (default) launches each kernel with programmatic stream serialization, so it starts
  * while the previous kernel drains and waits on the device for that kernel's results; "prefetch" =
  * 1 (default) has each GEMV kernel stream the weights of the GEMV kernel two launches later into
- * L2. */
+ * L2; "smem_weights" = 1 (default) has the per-layer GEMV kernels copy their weight tile into shared
+ * memory before waiting for the previous kernel (bounded wait; MUYO_ETIMEOUT if it expires). */
 int muyo_model_set_option(MuyoModel* m, const char* key, int value);
 
 /* ---- row-sharded GEMV + cross-GPU greedy (multi-GPU LM head) --------------------------------------

@@ -111,6 +111,7 @@ SIGNATURES = {
     "muyo_model_create": (C.c_int, [P(Qwen2Config), C.c_int, P(VP)]),
     "muyo_model_set_tensor": (C.c_int, [VP, C.c_char_p, VP, C.c_size_t]),
     "muyo_model_load_gguf": (C.c_int, [VP, C.c_char_p]),
+    "muyo_gguf_read_qwen2_config": (C.c_int, [C.c_char_p, U32, U32, P(Qwen2Config)]),
     "muyo_model_finalize": (C.c_int, [VP, VP]),
     "muyo_model_reset": (C.c_int, [VP, VP]),
     "muyo_model_generate": (C.c_int, [VP, VP, C.c_int, C.c_int, VP, VP]),

@@ -22,6 +22,10 @@ INCLUDE = os.path.join(ROOT, "include")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CU_SOURCES = ["runtime.cu", "ops.cu", "decode.cu"]
 CPP_SOURCES = ["gguf_loader.cpp"]
+HOST = os.path.join(PKG, "host")
+HOST_SOURCES = ["checks.cpp", "forward.cpp", "main.cpp"]
+HOST_BIN = os.path.join(LIBDIR, "muyo-llm")  # the C++ command line over the library
+CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 
 
 def nvcc() -> str:
@@ -61,7 +65,22 @@ def build(verbose: bool = False) -> str:
     if _newer(LIB, objs):
         cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcudart_static", "-lrt", "-ldl", "-lpthread"]
         subprocess.run(cmd, check=True)
+    build_host()
     return LIB
+
+
+def build_host() -> str:
+    """The muyo-llm command line (host/): g++ against include/ and libmuyo_cuda.so (found beside it
+    through $ORIGIN), with the CUDA runtime for its own device buffers."""
+    srcs = [os.path.join(HOST, f) for f in HOST_SOURCES]
+    deps = srcs + [os.path.join(HOST, "host.h"), os.path.join(INCLUDE, "muyo_cuda.h"), LIB]
+    if _newer(HOST_BIN, deps):
+        cxx = shutil.which("g++") or "g++"
+        cmd = [cxx, "-O2", "-std=c++17", "-Wall", "-I", INCLUDE, "-I", HOST, "-I", os.path.join(CUDA_HOME, "include")]
+        cmd += srcs + ["-o", HOST_BIN, "-L", LIBDIR, "-lmuyo_cuda", "-L", os.path.join(CUDA_HOME, "lib64"), "-lcudart",
+                       "-Wl,-rpath,$ORIGIN", "-Wl,-rpath," + os.path.join(CUDA_HOME, "lib64")]
+        subprocess.run(cmd, check=True)
+    return HOST_BIN
 
 
 if __name__ == "__main__":

@@ -81,6 +81,10 @@ struct GemvFused {
     Control* ctrl;      // LOGITS: next-token selection and step advance
     int32_t* tokens_rw;
     PfSet pf;           // weights of a later kernel: every CTA asks L2 for its slice of them
+    // SW (weights in shared memory): byte offset of the weight tile in dynamic shared memory, and
+    // the error word a timed-out wait for the tile sets (MUYO_ETIMEOUT on the host)
+    unsigned wofs;
+    int* err;
 };
 
 // Stage the merged attention output (the O projection's input, K = heads * hd) from the split-K
@@ -121,31 +125,31 @@ __device__ __forceinline__ void stage_merge(const GemvFused& a, float4* xs4, flo
     }
     __syncthreads();
     constexpr int E = 4;  // elements per thread per pass
+    const size_t cstride = (size_t)G * stride;  // floats between chunk c and c + 1 of one head
     for (int e0 = 0; e0 < K; e0 += E * nt) {
         float o[E];
+        const float* src[E];  // element e's value in chunk 0
+        const float* w[E];    // its head's chunk weights
 #pragma unroll
-        for (int j = 0; j < E; ++j)
+        for (int j = 0; j < E; ++j) {
             o[j] = 0.0f;
+            const int e = min(e0 + tid + j * nt, K - 1), h = e / hd;
+            src[j] = part_at(h, 0) + 2 + (e - h * hd);
+            w[j] = mw + h * nchunks;
+        }
         for (int c = 0; c < nchunks; c += 4) {
             float v[E][4];
 #pragma unroll
-            for (int j = 0; j < E; ++j) {
-                const int e = e0 + tid + j * nt;
+            for (int j = 0; j < E; ++j)
 #pragma unroll
                 for (int u = 0; u < 4; ++u)
-                    v[j][u] = e < K && c + u < nchunks ? __ldcg(part_at(e / hd, c + u) + 2 + e % hd) : 0.0f;
-            }
+                    v[j][u] = c + u < nchunks ? __ldcg(src[j] + (size_t)(c + u) * cstride) : 0.0f;
 #pragma unroll
-            for (int j = 0; j < E; ++j) {
-                const int e = e0 + tid + j * nt;
-                if (e < K) {
-                    const float* w = mw + (e / hd) * nchunks;
+            for (int j = 0; j < E; ++j)
 #pragma unroll
-                    for (int u = 0; u < 4; ++u)
-                        if (c + u < nchunks)
-                            o[j] = fmaf(v[j][u], w[c + u], o[j]);
-                }
-            }
+                for (int u = 0; u < 4; ++u)
+                    if (c + u < nchunks)
+                        o[j] = fmaf(v[j][u], w[j][c + u], o[j]);
         }
 #pragma unroll
         for (int j = 0; j < E; ++j) {
@@ -258,19 +262,38 @@ __device__ __forceinline__ void stage_input(const GemvFused& a, float* xs, float
 
 // One CTA = 8 warps = (8 / KSPLIT) row groups of ROWS rows, the K range of each row group split
 // over KSPLIT warps; partial sums meet in shared memory and are added in a fixed order.
-template <int ROWS, int U, int NMAT, int KSPLIT, int PRO, int EPI>
+// With SW every CTA owns exactly one tile (grid == tiles) and bulk-copies the tile's weight rows
+// (row stride == K, so the tile is one contiguous block per matrix) into shared memory before it
+// waits for the previous kernel; it then computes from shared memory. A wait for the copies that
+// exceeds kWaitLimitNs sets *a.err and skips the arithmetic.
+template <int ROWS, int U, int NMAT, int KSPLIT, int PRO, int EPI, bool SW = false>
 __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvFused a)
 {
-    extern __shared__ float xs[];
+    extern __shared__ __align__(128) float xs[];
     __shared__ float red[32];
     __shared__ float ksum[kGemvWarps][NMAT][ROWS];
     __shared__ Pair best_sm[kGemvWarps];
     __shared__ int last_flag;
+    __shared__ __align__(8) uint64_t wbar;
     constexpr int RG = kGemvWarps / KSPLIT;
+    const unsigned tile_bytes = SW ? (unsigned)(RG * ROWS) * (unsigned)a.K * 2u : 0u;  // per matrix
 
-    // The weights do not depend on the previous kernel: start streaming this CTA's first tile into
-    // L2 while the input is staged.
-    if (threadIdx.x == 0 && (int)blockIdx.x * RG * ROWS < a.rows) {
+    if (SW) {
+        if (threadIdx.x == 0) {
+            const int r0 = blockIdx.x * RG * ROWS, nr = min(RG * ROWS, a.rows - r0);
+            const unsigned bytes = (unsigned)nr * (unsigned)a.K * 2u;
+            char* wsm = reinterpret_cast<char*>(xs) + a.wofs;
+            mbar_init(&wbar, 1);
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_expect_tx(&wbar, bytes * NMAT);
+            bulk_g2s(wsm, a.w0 + (size_t)r0 * a.K, bytes, &wbar);
+            if (NMAT > 1)
+                bulk_g2s(wsm + tile_bytes, a.w1 + (size_t)r0 * a.K, bytes, &wbar);
+        }
+    } else if (threadIdx.x == 0 && (int)blockIdx.x * RG * ROWS < a.rows) {
+        // The weights do not depend on the previous kernel: start streaming this CTA's first tile
+        // into L2 while the input is staged.
         const int r0 = blockIdx.x * RG * ROWS, nr = min(RG * ROWS, a.rows - r0);
         prefetch_rows_l2(a.w0, a.ldw, r0, nr);
         if (NMAT > 1)
@@ -296,7 +319,23 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvFused a)
     }
     pdl_wait();  // the input vector and the epilogue operands come from earlier kernels
     pdl_trigger();
-    stage_input<PRO>(a, xs, red);
+    stage_input<PRO>(a, xs, red);  // ends with __syncthreads: the barrier's init is visible
+    bool tile_ok = true;
+    if (SW) {
+        tile_ok = mbar_try_wait(&wbar, 0);
+        if (!tile_ok) {
+            const unsigned long long t0 = now_ns();
+            while (!(tile_ok = mbar_try_wait(&wbar, 0)) && now_ns() - t0 <= kWaitLimitNs) {
+            }
+            if (!tile_ok) {
+                atomicMax(a.err, 4);
+                // the copies may still be in flight: give them one more bounded wait before exit
+                const unsigned long long t1 = now_ns();
+                while (!mbar_try_wait(&wbar, 0) && now_ns() - t1 <= kWaitLimitNs) {
+                }
+            }
+        }
+    }
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int rg = warp / KSPLIT, ks = warp % KSPLIT;
@@ -314,7 +353,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvFused a)
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
         const int row0 = (tile * RG + rg) * ROWS;
         const int nvalid = min(ROWS, a.rows - row0);
-        if (threadIdx.x == 0 && tile + (int)gridDim.x < ntiles) {  // the next tile of this CTA, to L2
+        if (!SW && threadIdx.x == 0 && tile + (int)gridDim.x < ntiles) {  // the next tile of this CTA, to L2
             const int r1 = (tile + gridDim.x) * RG * ROWS, nr = min(RG * ROWS, a.rows - r1);
             prefetch_rows_l2(a.w0, a.ldw, r1, nr);
             if (NMAT > 1)
@@ -330,8 +369,18 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvFused a)
 #pragma unroll
             for (int r = 0; r < ROWS; ++r)
                 acc[m][r] = 0.0f;
-        if (nvalid > 0) {
-            warp_gemv_f16_range<ROWS, U, NMAT>(ga, row0, nvalid, xs, K8, c_begin, c_end, lane, acc);
+        if (nvalid > 0 && tile_ok) {
+            if (SW) {
+                unsigned wsm[NMAT];
+                const unsigned w0s = (unsigned)__cvta_generic_to_shared(reinterpret_cast<char*>(xs) + a.wofs);
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m)
+                    wsm[m] = w0s + (unsigned)m * tile_bytes;
+                warp_gemv_f16_smem<ROWS, U, NMAT>(wsm, (unsigned)a.K * 2u, rg * ROWS, nvalid, xs, K8, c_begin, c_end,
+                                                  lane, acc);
+            } else {
+                warp_gemv_f16_range<ROWS, U, NMAT>(ga, row0, nvalid, xs, K8, c_begin, c_end, lane, acc);
+            }
             warp_reduce_acc<ROWS, NMAT>(acc);
         }
         if (KSPLIT > 1) {
@@ -458,7 +507,9 @@ static int resident_ctas(Kernel k, int threads, size_t smem)
 
 // The grid is capped at the CTAs resident at once: CTAs stride over the tiles, so a tile beyond the
 // first wave reuses an already staged input instead of waiting for a second wave to start.
-template <int ROWS, int U, int NMAT, int KSPLIT, int PRO, int EPI>
+// With an error word (a.err) and row stride == K, the weights-in-shared-memory variant (ROWS_SW
+// rows per warp, U_SW chunks in flight) is used when one tile per CTA fits the device at once.
+template <int ROWS, int U, int NMAT, int KSPLIT, int PRO, int EPI, int ROWS_SW = ROWS, int U_SW = U>
 static int launch_gemv(const GemvFused& a, int max_ctas, cudaStream_t s, bool pdl)
 {
     constexpr int RG = kGemvWarps / KSPLIT;
@@ -466,6 +517,25 @@ static int launch_gemv(const GemvFused& a, int max_ctas, cudaStream_t s, bool pd
     size_t smem = (size_t)a.K * sizeof(float);
     if (PRO == PRO_MERGE)
         smem += 2 * sizeof(float) * (size_t)(a.K / a.hd) * a.max_chunks;  // merge statistics
+    if constexpr (EPI != EPI_LOGITS) {
+      if (a.err && a.ldw == (size_t)a.K) {
+        const int ntiles_sw = (a.rows + RG * ROWS_SW - 1) / (RG * ROWS_SW);
+        const size_t wofs = (smem + 127) / 128 * 128;
+        const size_t smem_sw = wofs + (size_t)NMAT * RG * ROWS_SW * a.K * 2;
+        auto ksw = k_gemv<ROWS_SW, U_SW, NMAT, KSPLIT, PRO, EPI, true>;
+        if (smem_sw <= 200 * 1024) {
+            if (smem_sw > 48 * 1024)
+                MUYO_CUDA_TRY(cudaFuncSetAttribute(ksw, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_sw));
+            if (resident_ctas(ksw, kGemvThreads, smem_sw) >= ntiles_sw) {
+                GemvFused b = a;
+                b.wofs = (unsigned)wofs;
+                MUYO_CUDA_TRY(launch_kernel(ksw, dim3(ntiles_sw), dim3(kGemvThreads), smem_sw, s, pdl, b));
+                MUYO_LAUNCH_CHECK();
+                return MUYO_OK;
+            }
+        }
+      }
+    }
     auto k = k_gemv<ROWS, U, NMAT, KSPLIT, PRO, EPI>;
     if (smem > 48 * 1024)
         MUYO_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -617,7 +687,7 @@ static int attention_fused(const Shape& s, const float* qkv, void* kc, void* vc,
 static int layer_forward(const Shape& s, const LayerPtrs& w, void* kc, void* vc, const int32_t* pos,
                          const float* x_in, float* x_out, const LayerScratch& ws, const __half* embd,
                          const int32_t* tokens, const Control* ctrl, float* embed_out, cudaStream_t st, bool pdl,
-                         const PfSet* pf = nullptr)
+                         const PfSet* pf = nullptr, int* err = nullptr)
 {
     const int sms = sm_count();
     int rc;
@@ -632,6 +702,7 @@ static int layer_forward(const Shape& s, const LayerPtrs& w, void* kc, void* vc,
     a.rows = s.qkv_rows;
     a.bias = w.bqkv;
     a.y = ws.qkv;
+    a.err = err;
     if (pf)
         a.pf = pf[0];
     if (embd) {
@@ -666,6 +737,7 @@ static int layer_forward(const Shape& s, const LayerPtrs& w, void* kc, void* vc,
     o.rows = s.hidden;
     o.res = residual;
     o.y = ws.h1;
+    o.err = err;
     if (pf)
         o.pf = pf[1];
     rc = launch_gemv<1, 4, 1, 2, PRO_MERGE, EPI_RESIDUAL>(o, sms * 8, st, pdl);
@@ -682,9 +754,10 @@ static int layer_forward(const Shape& s, const LayerPtrs& w, void* kc, void* vc,
     g.ldw = s.hidden;
     g.rows = s.ffn;
     g.y = ws.act;
+    g.err = err;
     if (pf)
         g.pf = pf[2];
-    rc = launch_gemv<1, 4, 2, 1, PRO_NORM, EPI_SWIGLU>(g, sms * 8, st, pdl);
+    rc = launch_gemv<1, 4, 2, 1, PRO_NORM, EPI_SWIGLU, 2, 2>(g, sms * 8, st, pdl);
     if (rc)
         return rc;
     // 5. down_proj + residual
@@ -696,6 +769,7 @@ static int layer_forward(const Shape& s, const LayerPtrs& w, void* kc, void* vc,
     d.rows = s.hidden;
     d.res = ws.h1;
     d.y = x_out;
+    d.err = err;
     if (pf)
         d.pf = pf[3];
     return launch_gemv<1, 4, 1, 4, PRO_PLAIN, EPI_RESIDUAL>(d, sms * 8, st, pdl);
@@ -741,6 +815,7 @@ struct MuyoModel {
     int engine = 1;                 // 0: persistent kernel, 1: CUDA graph of per-phase kernels (default)
     bool pdl = true;                // graph engine: kernels launch early and prefetch their weights
     bool prefetch_ahead = true;     // graph engine: each GEMV streams a later kernel's weights into L2
+    bool sw = true;                 // graph engine: per-layer GEMVs bulk-copy their weight tile to shared memory
     double* rope_cs = nullptr;      // [max_seq][head_dim] cos/sin table (float64)
     muyo::PLayer* d_layers = nullptr;
     unsigned* bar = nullptr;        // persistent kernel grid-barrier counter
@@ -807,10 +882,11 @@ static int record_step(MuyoModel* m, cudaStream_t st)
         char* vc = static_cast<char*>(m->vc) + m->kv_layer_bytes * l;
         if (l == 0)
             rc = layer_forward(s, w, kc, vc, pos, nullptr, m->h, m->ls, W(m, "token_embd.weight"), m->tokens,
-                               m->ctrl, m->ls.h1 /*embedding row lands in h1 first*/, st, m->pdl, &plan[4 * l]);
+                               m->ctrl, m->ls.h1 /*embedding row lands in h1 first*/, st, m->pdl, &plan[4 * l],
+                               m->sw ? m->err : nullptr);
         else
             rc = layer_forward(s, w, kc, vc, pos, m->h, m->h, m->ls, nullptr, nullptr, nullptr, nullptr, st, m->pdl,
-                               &plan[4 * l]);
+                               &plan[4 * l], m->sw ? m->err : nullptr);
         if (rc)
             return rc;
     }
@@ -1407,17 +1483,15 @@ static int run_steps(MuyoModel* m, int prompt_end, int total, int n_steps, cudaS
     return MUYO_OK;
 }
 
-// Error word of the persistent kernel (read after a synchronisation); clears it.
+// Error word of the decode kernels (read after a synchronisation); clears it.
 static int check_device_error(MuyoModel* m, cudaStream_t st)
 {
-    if (m->engine != 0)
-        return MUYO_OK;
     int e = 0;
     MUYO_CUDA_TRY(cudaMemcpyAsync(&e, m->err, sizeof(int), cudaMemcpyDeviceToHost, st));
     MUYO_CUDA_TRY(cudaStreamSynchronize(st));
     if (e != 0) {
         MUYO_CUDA_TRY(cudaMemsetAsync(m->err, 0, sizeof(int), st));
-        set_error("decode: a bounded device wait expired in the persistent kernel (error word %d)", e);
+        set_error("decode: a bounded device wait expired (error word %d: 3 persistent kernel, 4 weight-tile copy)", e);
         return MUYO_ETIMEOUT;
     }
     return MUYO_OK;
@@ -1574,6 +1648,12 @@ extern "C" int muyo_model_set_option(MuyoModel* m, const char* key, int value)
         MUYO_REQUIRE(value == 0 || value == 1, "set_option: prefetch must be 0 or 1");
         MUYO_REQUIRE(!m->exec, "set_option: prefetch must be set before muyo_model_finalize");
         m->prefetch_ahead = value != 0;
+        return MUYO_OK;
+    }
+    if (k == "smem_weights") {
+        MUYO_REQUIRE(value == 0 || value == 1, "set_option: smem_weights must be 0 or 1");
+        MUYO_REQUIRE(!m->exec, "set_option: smem_weights must be set before muyo_model_finalize");
+        m->sw = value != 0;
         return MUYO_OK;
     }
     if (k == "pdl") {

@@ -50,6 +50,25 @@ __device__ __forceinline__ void prefetch_rows_l2(const __half* w, size_t ldw, in
     }
 }
 
+// s + w[0..7] . (xa, xb): one 16-byte chunk of F16 weights against its 8 staged x values, in a
+// fixed order (every GEMV path here uses it, so their sums agree bit for bit).
+__device__ __forceinline__ float dot_chunk(uint4 w, float4 xa, float4 xb, float s)
+{
+    float2 f = h2_to_f2(w.x);
+    s = fmaf(f.x, xa.x, s);
+    s = fmaf(f.y, xa.y, s);
+    f = h2_to_f2(w.y);
+    s = fmaf(f.x, xa.z, s);
+    s = fmaf(f.y, xa.w, s);
+    f = h2_to_f2(w.z);
+    s = fmaf(f.x, xb.x, s);
+    s = fmaf(f.y, xb.y, s);
+    f = h2_to_f2(w.w);
+    s = fmaf(f.x, xb.z, s);
+    s = fmaf(f.y, xb.w, s);
+    return s;
+}
+
 template <int ROWS, int U, int NMAT>
 struct GemvArgs {
     const __half* w[NMAT];
@@ -96,23 +115,59 @@ __device__ __forceinline__ void warp_gemv_f16_range(const GemvArgs<ROWS, U, NMAT
 #pragma unroll
                 for (int m = 0; m < NMAT; ++m)
 #pragma unroll
-                    for (int r = 0; r < ROWS; ++r) {
-                        const uint4 w = wv[m][r][u];
-                        float s = acc[m][r];
-                        float2 f = h2_to_f2(w.x);
-                        s = fmaf(f.x, xa.x, s);
-                        s = fmaf(f.y, xa.y, s);
-                        f = h2_to_f2(w.y);
-                        s = fmaf(f.x, xa.z, s);
-                        s = fmaf(f.y, xa.w, s);
-                        f = h2_to_f2(w.z);
-                        s = fmaf(f.x, xb.x, s);
-                        s = fmaf(f.y, xb.y, s);
-                        f = h2_to_f2(w.w);
-                        s = fmaf(f.x, xb.z, s);
-                        s = fmaf(f.y, xb.w, s);
-                        acc[m][r] = s;
-                    }
+                    for (int r = 0; r < ROWS; ++r)
+                        acc[m][r] = dot_chunk(wv[m][r][u], xa, xb, acc[m][r]);
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ uint4 lds16(unsigned addr)
+{
+    uint4 r;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(addr));
+    return r;
+}
+
+// As warp_gemv_f16_range, with the weight rows already in shared memory: matrix m's row lrow0 + r
+// starts at shared address wsm[m] + (lrow0 + r) * row_bytes (rows of K8 16-byte chunks). The
+// products are accumulated in the same order, so the sums are bit-identical.
+template <int ROWS, int U, int NMAT>
+__device__ __forceinline__ void warp_gemv_f16_smem(const unsigned (&wsm)[NMAT], unsigned row_bytes, int lrow0,
+                                                   int nvalid, const float* __restrict__ xs, int K8, int c_begin,
+                                                   int c_end, int lane, float (&acc)[NMAT][ROWS])
+{
+    const float4* xlo = reinterpret_cast<const float4*>(xs);
+    const float4* xhi = reinterpret_cast<const float4*>(xs + 4 * K8);
+    unsigned rowa[NMAT][ROWS];
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r)
+            rowa[m][r] = wsm[m] + (unsigned)(lrow0 + (r < nvalid ? r : 0)) * row_bytes;
+    for (int base = c_begin; base < c_end; base += WARP * U) {
+        uint4 wv[NMAT][ROWS][U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int c = base + lane + WARP * u;
+            const bool ok = c < c_end;
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+                for (int r = 0; r < ROWS; ++r)
+                    wv[m][r][u] = ok ? lds16(rowa[m][r] + 16u * (unsigned)c) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int c = base + lane + WARP * u;
+            if (c < c_end) {
+                const float4 xa = xlo[c];
+                const float4 xb = xhi[c];
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+                    for (int r = 0; r < ROWS; ++r)
+                        acc[m][r] = dot_chunk(wv[m][r][u], xa, xb, acc[m][r]);
             }
         }
     }

@@ -165,3 +165,91 @@ extern "C" int muyo_model_load_gguf(MuyoModel* m, const char* path)
     }
     return MUYO_OK;
 }
+
+// Scalar metadata value of GGUF type `type` as a double (integers and floats), or false.
+static bool read_number(Reader& r, uint32_t type, double& out)
+{
+    switch (type) {
+        case 0: { uint8_t v = 0; r.bytes(&v, 1); out = v; return r.ok; }
+        case 1: { int8_t v = 0; r.bytes(&v, 1); out = v; return r.ok; }
+        case 2: { uint16_t v = 0; r.bytes(&v, 2); out = v; return r.ok; }
+        case 3: { int16_t v = 0; r.bytes(&v, 2); out = v; return r.ok; }
+        case 4: { out = r.u32(); return r.ok; }
+        case 5: { int32_t v = 0; r.bytes(&v, 4); out = v; return r.ok; }
+        case 6: { float v = 0; r.bytes(&v, 4); out = v; return r.ok; }
+        case 10: { out = (double)r.u64(); return r.ok; }
+        case 11: { int64_t v = 0; r.bytes(&v, 8); out = (double)v; return r.ok; }
+        case 12: { double v = 0; r.bytes(&v, 8); out = v; return r.ok; }
+        default: return false;
+    }
+}
+
+extern "C" int muyo_gguf_read_qwen2_config(const char* path, uint32_t max_seq, uint32_t kv_dtype,
+                                           MuyoQwen2Config* out)
+{
+    muyo::clear_error();
+    if (!path || !out) {
+        muyo::set_error("read_qwen2_config: null argument");
+        return MUYO_EINVAL;
+    }
+    Reader r(path);
+    char magic[4] = {};
+    if (r.ok)
+        r.bytes(magic, 4);
+    if (!r.ok || std::memcmp(magic, "GGUF", 4) != 0) {
+        muyo::set_error("read_qwen2_config: %s is not a readable GGUF file", path);
+        return MUYO_EINVAL;
+    }
+    const uint32_t version = r.u32();
+    r.u64();  // tensor count
+    const uint64_t n_kv = r.u64();
+    if (!r.ok || version < 2 || n_kv > (1u << 20)) {
+        muyo::set_error("read_qwen2_config: unsupported header (version %u)", version);
+        return MUYO_EINVAL;
+    }
+    double layers = 0, hidden = 0, ffn = 0, heads = 0, kv_heads = 0, eps = 0, base = 10000.0;
+    uint64_t vocab = 0;
+    for (uint64_t i = 0; i < n_kv && r.ok; ++i) {
+        const std::string key = r.str();
+        const uint32_t type = r.u32();
+        double* num = key == "qwen2.block_count"                        ? &layers
+                      : key == "qwen2.embedding_length"                 ? &hidden
+                      : key == "qwen2.feed_forward_length"              ? &ffn
+                      : key == "qwen2.attention.head_count"             ? &heads
+                      : key == "qwen2.attention.head_count_kv"          ? &kv_heads
+                      : key == "qwen2.attention.layer_norm_rms_epsilon" ? &eps
+                      : key == "qwen2.rope.freq_base"                   ? &base
+                                                                        : nullptr;
+        if (num && type != 8 && type != 9) {
+            if (!read_number(r, type, *num))
+                r.ok = false;
+        } else if (key == "tokenizer.ggml.tokens" && type == 9) {
+            const uint32_t et = r.u32();
+            const uint64_t n = r.u64();
+            vocab = n;
+            for (uint64_t k = 0; k < n && r.ok; ++k)
+                r.skip_value(et, 1);
+        } else {
+            r.skip_value(type);
+        }
+    }
+    if (!r.ok) {
+        muyo::set_error("read_qwen2_config: %s: truncated or malformed metadata", path);
+        return MUYO_EINVAL;
+    }
+    if (hidden <= 0 || heads <= 0 || kv_heads <= 0 || vocab == 0 || layers <= 0 || ffn <= 0) {
+        muyo::set_error("read_qwen2_config: %s is missing the qwen2 dimensions or the token list", path);
+        return MUYO_EINVAL;
+    }
+    out->layers = (uint32_t)layers;
+    out->hidden = (uint32_t)hidden;
+    out->ffn = (uint32_t)ffn;
+    out->heads = (uint32_t)heads;
+    out->kv_heads = (uint32_t)kv_heads;
+    out->vocab = (uint32_t)vocab;
+    out->max_seq = max_seq;
+    out->rms_eps = (float)eps;
+    out->rope_base = (float)base;
+    out->kv_dtype = kv_dtype;
+    return MUYO_OK;
+}

@@ -27,7 +27,7 @@ class Qwen2Model:
 
     def __init__(self, cfg: Qwen2Config, tensors: dict | None = None, gguf_path: str | None = None,
                  kv_dtype: int = _abi.KV_F16, device: int = 0, engine: int = 1, pdl: bool = True,
-                 prefetch: bool = True):
+                 prefetch: bool = True, smem_weights: bool = True):
         self.cfg = cfg
         self.kv_dtype = kv_dtype
         self._cfg = config_struct(cfg, kv_dtype)
@@ -46,6 +46,7 @@ class Qwen2Model:
             _abi.call("muyo_model_set_option", self._m, b"engine", engine)
             _abi.call("muyo_model_set_option", self._m, b"pdl", 1 if pdl else 0)
             _abi.call("muyo_model_set_option", self._m, b"prefetch", 1 if prefetch else 0)
+            _abi.call("muyo_model_set_option", self._m, b"smem_weights", 1 if smem_weights else 0)
             _abi.call("muyo_model_finalize", self._m, None)
         except Exception:
             self.close()

@@ -169,11 +169,12 @@ def test_engines_agree_on_05b_arch(cuda, kv_dtype):
 
 
 @pytest.mark.parametrize("kv_dtype", [_abi.KV_F32, _abi.KV_F16])
-def test_graph_engine_pdl_and_prefetch_are_bit_identical(cuda, tiny, kv_dtype):
-    """Programmatic dependent launch and the L2 prefetch of later kernels' weights change when
-    kernels start and where weights are cached, not what is computed: ids and logits of the graph
-    engine with both off and both on are bit-identical, on the tiny model and on an
-    0.5B-architecture sequence of 81 positions (two 64-key attention chunks, so the merge runs)."""
+def test_graph_engine_launch_options_are_bit_identical(cuda, tiny, kv_dtype):
+    """Programmatic dependent launch, the L2 prefetch of later kernels' weights and the weight tiles
+    copied to shared memory change when kernels start and where weights are read from, not what is
+    computed: ids and logits of the graph engine with all three off and all three on are
+    bit-identical, on the tiny model and on an 0.5B-architecture sequence of 81 positions (two
+    64-key attention chunks, so the merge runs)."""
     g, t = tiny
     cfg = synth.QWEN2_05B
     big = synth.make_model(cfg, 20261201)
@@ -182,7 +183,7 @@ def test_graph_engine_pdl_and_prefetch_are_bit_identical(cuda, tiny, kv_dtype):
         runs = []
         for pdl in (False, True):
             m = engine.Qwen2Model(c, tensors, kv_dtype=kv_dtype, engine=engine.Qwen2Model.ENGINE_GRAPH, pdl=pdl,
-                                  prefetch=pdl)
+                                  prefetch=pdl, smem_weights=pdl)
             ids = m.generate(prompt, n)
             _, logits = m.step(int(ids[-1]))
             runs.append((ids, logits))

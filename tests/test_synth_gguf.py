@@ -45,3 +45,26 @@ def test_gguf_roundtrip(tmp_path):
         assert (got.view(np.uint8) == ref.view(np.uint8)).all(), name
     # the tied LM head shares the embedding's bytes
     assert infos["output.weight"][2] == infos["token_embd.weight"][2]
+
+
+def test_gguf_qwen2_config_reader(tmp_path):
+    """muyo_gguf_read_qwen2_config reads the qwen2.* metadata and the token-list length
+    (ReadQwen2Config, src/FullModel.cpp:84-105); metadata only, so it runs without a GPU."""
+    import ctypes as C
+
+    from muyo_llm_b200 import _abi, build
+
+    build()
+    cfg = synth.QWEN2_TINY
+    path = str(tmp_path / "tiny.gguf")
+    gguf.write_synthetic_qwen2(path, cfg, 3)
+    out = _abi.Qwen2Config()
+    _abi.call("muyo_gguf_read_qwen2_config", path.encode(), 64, _abi.KV_F16, C.byref(out))
+    assert (out.layers, out.hidden, out.ffn, out.heads, out.kv_heads, out.vocab) == \
+        (cfg.layers, cfg.hidden, cfg.ffn, cfg.heads, cfg.kv_heads, cfg.vocab)
+    assert out.max_seq == 64 and out.kv_dtype == _abi.KV_F16
+    assert abs(out.rms_eps - cfg.rms_eps) < 1e-12 and out.rope_base == cfg.rope_base
+    bad = tmp_path / "bad.gguf"
+    bad.write_bytes(b"NOPE" + bytes(20))
+    rc = _abi.lib().muyo_gguf_read_qwen2_config(str(bad).encode(), 64, 0, C.byref(out))
+    assert _abi.ERRORS.get(rc) == "MUYO_EINVAL"
