@@ -43,6 +43,25 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 
 __host__ __device__ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Launches kernel k; with pdl the launch carries the programmatic-stream-serialization attribute,
+// so that (inside a captured graph) it may start while the kernel before it drains.
+template <typename... Params, typename... Args>
+inline cudaError_t launch_kernel(void (*k)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+                                 Args... args)
+{
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
 // Number of SMs of the current device (cached per device).
 int sm_count();
 

@@ -476,23 +476,13 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvFused a)
     }
 }
 
-// Launches kernel k; with pdl the launch carries the programmatic-stream-serialization attribute,
-// so that (inside a captured graph) it may start while the kernel before it drains.
-template <typename... Params, typename... Args>
-static cudaError_t launch_kernel(void (*k)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
-                                 Args... args)
+// Every kernel of the decode step asks for the largest shared-memory carveout: the L1/shared split
+// is set per SM, so a kernel that starts early (programmatic launch) can only be placed on SMs whose
+// split already leaves it room, and a uniform split lets consecutive kernels share SMs.
+template <typename Kernel>
+static cudaError_t max_shared_carveout(Kernel k)
 {
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, k, args...);
+    return cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
 }
 
 // CTAs of kernel k (block threads, smem bytes) resident on the whole device at once.
@@ -523,6 +513,7 @@ static int launch_gemv(const GemvFused& a, int max_ctas, cudaStream_t s, bool pd
         const size_t wofs = (smem + 127) / 128 * 128;
         const size_t smem_sw = wofs + (size_t)NMAT * RG * ROWS_SW * a.K * 2;
         auto ksw = k_gemv<ROWS_SW, U_SW, NMAT, KSPLIT, PRO, EPI, true>;
+        MUYO_CUDA_TRY(max_shared_carveout(ksw));
         if (smem_sw <= 200 * 1024) {
             if (smem_sw > 48 * 1024)
                 MUYO_CUDA_TRY(cudaFuncSetAttribute(ksw, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_sw));
@@ -537,6 +528,7 @@ static int launch_gemv(const GemvFused& a, int max_ctas, cudaStream_t s, bool pd
       }
     }
     auto k = k_gemv<ROWS, U, NMAT, KSPLIT, PRO, EPI>;
+    MUYO_CUDA_TRY(max_shared_carveout(k));
     if (smem > 48 * 1024)
         MUYO_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int grid = ntiles < max_ctas ? ntiles : max_ctas;
@@ -654,6 +646,7 @@ static int launch_attention_fused(const Shape& s, const float* qkv, void* kc, vo
     // Every chunk writes its partial (no output pointer, no inline merge): the O projection merges
     // them while staging its input.
     auto k = k_attention<KV, HD, true, false>;
+    MUYO_CUDA_TRY(max_shared_carveout(k));
     if (smem > 48 * 1024)
         MUYO_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     (void)out;
@@ -740,7 +733,7 @@ static int layer_forward(const Shape& s, const LayerPtrs& w, void* kc, void* vc,
     o.err = err;
     if (pf)
         o.pf = pf[1];
-    rc = launch_gemv<1, 4, 1, 2, PRO_MERGE, EPI_RESIDUAL>(o, sms * 8, st, pdl);
+    rc = launch_gemv<1, 4, 1, 2, PRO_MERGE, EPI_RESIDUAL, 2, 4>(o, sms * 8, st, pdl);
     if (rc)
         return rc;
     // 4. rms_norm -> gate, up -> SwiGLU
@@ -757,7 +750,7 @@ static int layer_forward(const Shape& s, const LayerPtrs& w, void* kc, void* vc,
     g.err = err;
     if (pf)
         g.pf = pf[2];
-    rc = launch_gemv<1, 4, 2, 1, PRO_NORM, EPI_SWIGLU, 2, 2>(g, sms * 8, st, pdl);
+    rc = launch_gemv<1, 4, 2, 1, PRO_NORM, EPI_SWIGLU, 3, 2>(g, sms * 8, st, pdl);
     if (rc)
         return rc;
     // 5. down_proj + residual
@@ -772,7 +765,7 @@ static int layer_forward(const Shape& s, const LayerPtrs& w, void* kc, void* vc,
     d.err = err;
     if (pf)
         d.pf = pf[3];
-    return launch_gemv<1, 4, 1, 4, PRO_PLAIN, EPI_RESIDUAL>(d, sms * 8, st, pdl);
+    return launch_gemv<1, 4, 1, 4, PRO_PLAIN, EPI_RESIDUAL, 2, 4>(d, sms * 8, st, pdl);
 }
 
 // ---- model ------------------------------------------------------------------------------------------

@@ -87,6 +87,8 @@ __global__ void __launch_bounds__(kThreads) k_mat_vec_f16(MatVecDev p, const __h
     if (p.k8 > 0 && threadIdx.x == 0 && (int)blockIdx.x * block_rows < p.rows)
         prefetch_rows_l2(Ab, (size_t)p.stride_a, blockIdx.x * block_rows,
                          min(block_rows, p.rows - (int)blockIdx.x * block_rows));
+    pdl_wait();  // the L2 prefetch above is only a hint; every read of A, x or D comes after this wait
+    pdl_trigger();
     stage_x_split(xs, Bb, p.ncols, p.k8);
     __syncthreads();
     GemvArgs<ROWS, U, 1> ga{{Ab}, (size_t)p.stride_a};
@@ -119,6 +121,8 @@ __global__ void __launch_bounds__(kThreads) k_mat_vec_f32(MatVecDev p, const flo
                                                           const float* __restrict__ B, float* __restrict__ D,
                                                           const float* __restrict__ f0, const float* __restrict__ f1)
 {
+    pdl_wait();  // launched with programmatic serialization: wait for the previous kernel
+    pdl_trigger();
     extern __shared__ float xs[];
     const int b = blockIdx.y;
     const float* Ab = A + batch_a_index(p, b) * p.batch_stride_a;
@@ -244,11 +248,11 @@ static int launch_mat_vec(bool f16, const MatVecDev& q, int batches, const void*
     if (f16) {
         auto k = k_mat_vec_f16<ROWS, 4>;
         MUYO_CUDA_TRY(set_smem(k, smem));
-        k<<<grid, kThreads, smem, s>>>(q, static_cast<const __half*>(a), b, d, f0, f1);
+        MUYO_CUDA_TRY(launch_kernel(k, dim3(grid), dim3(kThreads), smem, s, true, q, static_cast<const __half*>(a), b, d, f0, f1));
     } else {
         auto k = k_mat_vec_f32<ROWS, 4>;
         MUYO_CUDA_TRY(set_smem(k, smem));
-        k<<<grid, kThreads, smem, s>>>(q, static_cast<const float*>(a), b, d, f0, f1);
+        MUYO_CUDA_TRY(launch_kernel(k, dim3(grid), dim3(kThreads), smem, s, true, q, static_cast<const float*>(a), b, d, f0, f1));
     }
     MUYO_LAUNCH_CHECK();
     return MUYO_OK;
@@ -292,6 +296,8 @@ static Dims4 dims(uint32_t n0, uint32_t n1, uint32_t n2, uint32_t n3, uint32_t s
 __global__ void k_add_contig(const float4* __restrict__ a, const float4* __restrict__ b, float4* __restrict__ d,
                              long long n4)
 {
+    pdl_wait();  // launched with programmatic serialization: wait for the previous kernel
+    pdl_trigger();
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
         const float4 x = a[i], y = b[i];
         d[i] = make_float4(x.x + y.x, x.y + y.y, x.z + y.z, x.w + y.w);
@@ -301,6 +307,8 @@ __global__ void k_add_contig(const float4* __restrict__ a, const float4* __restr
 __global__ void k_add_general(Dims4 A, Dims4 B, Dims4 D, const float* __restrict__ a, const float* __restrict__ b,
                               float* __restrict__ d, long long n)
 {
+    pdl_wait();  // launched with programmatic serialization: wait for the previous kernel
+    pdl_trigger();
     for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < n;
          idx += (long long)gridDim.x * blockDim.x) {
         long long t = idx;
@@ -344,6 +352,8 @@ static int grid_for(long long n, int per_thread = 1)
 __global__ void __launch_bounds__(kThreads) k_rms_norm(Dims4 A, Dims4 W, Dims4 D, const float* __restrict__ a,
                                                        const float* __restrict__ w, float* __restrict__ d, float eps)
 {
+    pdl_wait();  // launched with programmatic serialization: wait for the previous kernel
+    pdl_trigger();
     __shared__ float red[32];
     const int row = blockIdx.x;
     const int i1 = row % A.ne[1], i2 = (row / A.ne[1]) % A.ne[2], i3 = row / (A.ne[1] * A.ne[2]);
@@ -368,6 +378,8 @@ template <int V>
 __global__ void __launch_bounds__(kThreads) k_rms_norm_rows(const float4* __restrict__ a, const float4* __restrict__ w,
                                                             float4* __restrict__ d, int n4, float eps)
 {
+    pdl_wait();  // launched with programmatic serialization: wait for the previous kernel
+    pdl_trigger();
     __shared__ float red[32];
     const float4* ar = a + (long long)blockIdx.x * n4;
     float4* dr = d + (long long)blockIdx.x * n4;
@@ -416,6 +428,8 @@ template <typename T>
 __global__ void k_get_rows(Dims4 A, Dims4 B, Dims4 D, const T* __restrict__ a, const int32_t* __restrict__ b,
                            float* __restrict__ d)
 {
+    pdl_wait();  // launched with programmatic serialization: wait for the previous kernel
+    pdl_trigger();
     const int i10 = blockIdx.y;
     const int z = blockIdx.z, i11 = z % B.ne[1], i12 = z / B.ne[1];
     const int idx = b[i10 * B.nb[0] + i11 * B.nb[1] + i12 * B.nb[2]];
@@ -436,6 +450,8 @@ struct GluDev {
 
 __global__ void k_swiglu(GluDev p, const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ d)
 {
+    pdl_wait();  // launched with programmatic serialization: wait for the previous kernel
+    pdl_trigger();
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < p.N; i += (long long)gridDim.x * blockDim.x) {
         const long long per3 = (long long)p.ne22 * p.ne21 * p.ne20, per2 = (long long)p.ne21 * p.ne20;
         const long long i23 = i / per3;
@@ -464,6 +480,8 @@ __global__ void k_swiglu(GluDev p, const float* __restrict__ a, const float* __r
 __global__ void k_swiglu_flat(const float4* __restrict__ a, const float4* __restrict__ b, float4* __restrict__ d,
                               long long n4)
 {
+    pdl_wait();  // launched with programmatic serialization: wait for the previous kernel
+    pdl_trigger();
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
         const float4 g = ld_stream16f(a + i), u = ld_stream16f(b + i);
         d[i] = make_float4(silu_mul(g.x, u.x), silu_mul(g.y, u.y), silu_mul(g.z, u.z), silu_mul(g.w, u.w));
@@ -501,6 +519,8 @@ __device__ __forceinline__ void rope_yarn(const RopeDev& p, float theta_extrap, 
 __global__ void k_rope(RopeDev p, const float* __restrict__ x, const int32_t* __restrict__ pos,
                        const float* __restrict__ ff, float* __restrict__ d)
 {
+    pdl_wait();  // launched with programmatic serialization: wait for the previous kernel
+    pdl_trigger();
     const int pairs = p.ne00 / 2;
     const long long total = (long long)p.nrows * pairs;
     for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < total;
@@ -551,6 +571,8 @@ __global__ void __launch_bounds__(kThreads) k_soft_max(SoftMaxDev p, const float
                                                        const float* __restrict__ mask,
                                                        const float* __restrict__ sinks, float* __restrict__ d)
 {
+    pdl_wait();  // launched with programmatic serialization: wait for the previous kernel
+    pdl_trigger();
     __shared__ float red[32];
     const int rowx = blockIdx.x;
     const int i03 = rowx / (p.ne01 * p.ne02);
@@ -620,6 +642,8 @@ __device__ __forceinline__ ArgPair block_argmax(float v, int i)
 __global__ void __launch_bounds__(kThreads) k_argmax_partial(const float* __restrict__ a, int KX, int per_row,
                                                              int index_base, ArgPair* __restrict__ part)
 {
+    pdl_wait();  // launched with programmatic serialization: wait for the previous kernel
+    pdl_trigger();
     const int row = blockIdx.y, blk = blockIdx.x;
     const float* ar = a + (long long)row * KX;
     const int c0 = blk * kArgmaxChunk, c1 = min(KX, c0 + kArgmaxChunk);
@@ -644,6 +668,8 @@ constexpr int kArgmaxVec = kArgmaxChunk / 4 / kThreads;  // float4s per thread
 __global__ void __launch_bounds__(kThreads) k_argmax_partial4(const float* __restrict__ a, int KX, int per_row,
                                                               int index_base, ArgPair* __restrict__ part)
 {
+    pdl_wait();  // launched with programmatic serialization: wait for the previous kernel
+    pdl_trigger();
     const int row = blockIdx.y, blk = blockIdx.x;
     const float4* ar = reinterpret_cast<const float4*>(a + (long long)row * KX);
     const int q0 = blk * (kArgmaxChunk / 4), q1 = min(KX / 4, q0 + kArgmaxChunk / 4);
@@ -679,6 +705,8 @@ __global__ void __launch_bounds__(kThreads) k_argmax_partial4(const float* __res
 __global__ void __launch_bounds__(kThreads) k_argmax_final(const ArgPair* __restrict__ part, int n,
                                                            int32_t* __restrict__ d)
 {
+    pdl_wait();  // launched with programmatic serialization: wait for the previous kernel
+    pdl_trigger();
     const int row = blockIdx.x;
     float bv = -INFINITY;
     int bi = INT_MAX;
@@ -697,6 +725,8 @@ __global__ void __launch_bounds__(kThreads) k_argmax_final(const ArgPair* __rest
 __global__ void k_copy(Dims4 S, Dims4 T, long long a_off, long long d_off, const float* __restrict__ a,
                        float* __restrict__ d, long long n)
 {
+    pdl_wait();  // launched with programmatic serialization: wait for the previous kernel
+    pdl_trigger();
     for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < n;
          idx += (long long)gridDim.x * blockDim.x) {
         long long t = idx, u = idx, si = a_off, di = d_off;
@@ -714,6 +744,8 @@ __global__ void k_copy(Dims4 S, Dims4 T, long long a_off, long long d_off, const
 // Reduces n partial pairs into one pair (the shard result of mat_vec_f16_argmax).
 __global__ void __launch_bounds__(kThreads) k_pairs_to_pair(const ArgPair* __restrict__ part, int n, ArgPair* __restrict__ out)
 {
+    pdl_wait();  // launched with programmatic serialization: wait for the previous kernel
+    pdl_trigger();
     float bv = -INFINITY;
     int bi = INT_MAX;
     for (int k = threadIdx.x; k < n; k += blockDim.x) {
@@ -761,11 +793,11 @@ extern "C" int muyo_cuda_add(const MuyoBinaryParams* p, const float* a, const fl
     const cudaStream_t s = as_stream(stream);
     if (contiguous(A) && contiguous(B) && contiguous(D) && count(B) == n && n % 4 == 0 && aligned16(a) &&
         aligned16(b) && aligned16(d)) {
-        k_add_contig<<<grid_for(n / 4), kThreads, 0, s>>>(reinterpret_cast<const float4*>(a),
+        MUYO_CUDA_TRY(launch_kernel(k_add_contig, dim3(grid_for(n / 4)), dim3(kThreads), 0, s, true, reinterpret_cast<const float4*>(a),
                                                           reinterpret_cast<const float4*>(b),
-                                                          reinterpret_cast<float4*>(d), n / 4);
+                                                          reinterpret_cast<float4*>(d), n / 4));
     } else {
-        k_add_general<<<grid_for(n), kThreads, 0, s>>>(A, B, D, a, b, d, n);
+        MUYO_CUDA_TRY(launch_kernel(k_add_general, dim3(grid_for(n)), dim3(kThreads), 0, s, true, A, B, D, a, b, d, n));
     }
     MUYO_LAUNCH_CHECK();
     return MUYO_OK;
@@ -791,15 +823,15 @@ extern "C" int muyo_cuda_rms_norm(const MuyoBinaryParams* p, const float* a, con
         const float4 *a4 = reinterpret_cast<const float4*>(a), *w4 = reinterpret_cast<const float4*>(w);
         float4* d4 = reinterpret_cast<float4*>(d);
         if (n4 <= kThreads)
-            k_rms_norm_rows<1><<<(unsigned)rows, kThreads, 0, s>>>(a4, w4, d4, n4, p->param1);
+            MUYO_CUDA_TRY(launch_kernel(k_rms_norm_rows<1>, dim3((unsigned)rows), dim3(kThreads), 0, s, true, a4, w4, d4, n4, p->param1));
         else if (n4 <= 2 * kThreads)
-            k_rms_norm_rows<2><<<(unsigned)rows, kThreads, 0, s>>>(a4, w4, d4, n4, p->param1);
+            MUYO_CUDA_TRY(launch_kernel(k_rms_norm_rows<2>, dim3((unsigned)rows), dim3(kThreads), 0, s, true, a4, w4, d4, n4, p->param1));
         else if (n4 <= 4 * kThreads)
-            k_rms_norm_rows<4><<<(unsigned)rows, kThreads, 0, s>>>(a4, w4, d4, n4, p->param1);
+            MUYO_CUDA_TRY(launch_kernel(k_rms_norm_rows<4>, dim3((unsigned)rows), dim3(kThreads), 0, s, true, a4, w4, d4, n4, p->param1));
         else
-            k_rms_norm_rows<8><<<(unsigned)rows, kThreads, 0, s>>>(a4, w4, d4, n4, p->param1);
+            MUYO_CUDA_TRY(launch_kernel(k_rms_norm_rows<8>, dim3((unsigned)rows), dim3(kThreads), 0, s, true, a4, w4, d4, n4, p->param1));
     } else {
-        k_rms_norm<<<(unsigned)rows, kThreads, 0, s>>>(A, W, D, a, w, d, p->param1);
+        MUYO_CUDA_TRY(launch_kernel(k_rms_norm, dim3((unsigned)rows), dim3(kThreads), 0, s, true, A, W, D, a, w, d, p->param1));
     }
     MUYO_LAUNCH_CHECK();
     return MUYO_OK;
@@ -816,9 +848,9 @@ static int get_rows_any(bool f16, const MuyoBinaryParams* p, const void* a, cons
     MUYO_REQUIRE(B.ne[0] <= 65535 && (long long)B.ne[1] * B.ne[2] <= 65535, "get_rows: too many ids");
     dim3 grid((A.ne[0] + kThreads - 1) / kThreads, B.ne[0], B.ne[1] * B.ne[2]);
     if (f16)
-        k_get_rows<__half><<<grid, kThreads, 0, as_stream(stream)>>>(A, B, D, static_cast<const __half*>(a), b, d);
+        MUYO_CUDA_TRY(launch_kernel(k_get_rows<__half>, dim3(grid), dim3(kThreads), 0, as_stream(stream), true, A, B, D, static_cast<const __half*>(a), b, d));
     else
-        k_get_rows<float><<<grid, kThreads, 0, as_stream(stream)>>>(A, B, D, static_cast<const float*>(a), b, d);
+        MUYO_CUDA_TRY(launch_kernel(k_get_rows<float>, dim3(grid), dim3(kThreads), 0, as_stream(stream), true, A, B, D, static_cast<const float*>(a), b, d));
     MUYO_LAUNCH_CHECK();
     return MUYO_OK;
 }
@@ -876,11 +908,11 @@ extern "C" int muyo_cuda_swiglu(const MuyoGluParams* p, const float* a, const fl
     const cudaStream_t s = as_stream(stream);
     if (g.mode == MUYO_GLU_SPLIT && g.N % 4 == 0 && dense(g.nb0) && dense(g.nb1) && dense(g.nb2) && aligned16(a) &&
         aligned16(b) && aligned16(d)) {
-        k_swiglu_flat<<<grid_for(g.N / 4), kThreads, 0, s>>>(reinterpret_cast<const float4*>(a),
+        MUYO_CUDA_TRY(launch_kernel(k_swiglu_flat, dim3(grid_for(g.N / 4)), dim3(kThreads), 0, s, true, reinterpret_cast<const float4*>(a),
                                                              reinterpret_cast<const float4*>(b),
-                                                             reinterpret_cast<float4*>(d), g.N / 4);
+                                                             reinterpret_cast<float4*>(d), g.N / 4));
     } else {
-        k_swiglu<<<grid_for(g.N), kThreads, 0, s>>>(g, a, b, d);
+        MUYO_CUDA_TRY(launch_kernel(k_swiglu, dim3(grid_for(g.N)), dim3(kThreads), 0, s, true, g, a, b, d));
     }
     MUYO_LAUNCH_CHECK();
     return MUYO_OK;
@@ -923,7 +955,7 @@ extern "C" int muyo_cuda_rope(const MuyoRopeParams* p, const float* x, const int
     r.a_offset = p->a_offset;
     r.d_offset = p->d_offset;
     const long long total = (long long)p->nrows * (p->ne00 / 2);
-    k_rope<<<grid_for(total), kThreads, 0, as_stream(stream)>>>(r, x, pos, freq_factors, d);
+    MUYO_CUDA_TRY(launch_kernel(k_rope, dim3(grid_for(total)), dim3(kThreads), 0, as_stream(stream), true, r, x, pos, freq_factors, d));
     MUYO_LAUNCH_CHECK();
     return MUYO_OK;
 }
@@ -954,7 +986,7 @@ extern "C" int muyo_cuda_soft_max(const MuyoSoftMaxParams* p, const float* x, co
     s.n_head_log2 = (int)p->n_head_log2;
     s.nrows_x = (int)p->nrows_x;
     s.has_sinks = (int)p->has_sinks;
-    k_soft_max<<<p->nrows_x, kThreads, 0, as_stream(stream)>>>(s, x, mask, sinks, d);
+    MUYO_CUDA_TRY(launch_kernel(k_soft_max, dim3(p->nrows_x), dim3(kThreads), 0, as_stream(stream), true, s, x, mask, sinks, d));
     MUYO_LAUNCH_CHECK();
     return MUYO_OK;
 }
@@ -974,12 +1006,12 @@ static int argmax_launch(const float* a, uint32_t KX, uint32_t KY, int index_bas
 {
     const int per_row = argmax_blocks(KX);
     if (KX % 4 == 0 && aligned16(a))
-        k_argmax_partial4<<<dim3(per_row, KY), kThreads, 0, s>>>(a, (int)KX, per_row, index_base, part);
+        MUYO_CUDA_TRY(launch_kernel(k_argmax_partial4, dim3(dim3(per_row, KY)), dim3(kThreads), 0, s, true, a, (int)KX, per_row, index_base, part));
     else
-        k_argmax_partial<<<dim3(per_row, KY), kThreads, 0, s>>>(a, (int)KX, per_row, index_base, part);
+        MUYO_CUDA_TRY(launch_kernel(k_argmax_partial, dim3(dim3(per_row, KY)), dim3(kThreads), 0, s, true, a, (int)KX, per_row, index_base, part));
     MUYO_LAUNCH_CHECK();
     if (d) {
-        k_argmax_final<<<KY, kThreads, 0, s>>>(part, per_row, d);
+        MUYO_CUDA_TRY(launch_kernel(k_argmax_final, dim3(KY), dim3(kThreads), 0, s, true, part, per_row, d));
         MUYO_LAUNCH_CHECK();
     }
     return MUYO_OK;
@@ -1009,7 +1041,7 @@ extern "C" int muyo_cuda_copy_f32(const MuyoUnaryParams* p, const float* a, floa
     MUYO_REQUIRE(p->ne > 0, "copy: ne must be positive");
     MUYO_REQUIRE((long long)p->ne <= count(S) && (long long)p->ne <= count(T),
                  "copy: ne exceeds the source or destination shape");
-    k_copy<<<grid_for(p->ne), kThreads, 0, as_stream(stream)>>>(S, T, p->a_offset, p->d_offset, a, d, p->ne);
+    MUYO_CUDA_TRY(launch_kernel(k_copy, dim3(grid_for(p->ne)), dim3(kThreads), 0, as_stream(stream), true, S, T, p->a_offset, p->d_offset, a, d, p->ne));
     MUYO_LAUNCH_CHECK();
     return MUYO_OK;
 }
@@ -1039,7 +1071,7 @@ extern "C" int muyo_cuda_mat_vec_f16_argmax(const MuyoMatVecParams* p, const voi
     if (rc != MUYO_OK)
         return rc;
     // One shard pair: reduce the partials into pair_out.
-    k_pairs_to_pair<<<1, kThreads, 0, s>>>(part, argmax_blocks(p->rows), static_cast<ArgPair*>(pair_out));
+    MUYO_CUDA_TRY(launch_kernel(k_pairs_to_pair, dim3(1), dim3(kThreads), 0, s, true, part, argmax_blocks(p->rows), static_cast<ArgPair*>(pair_out)));
     MUYO_LAUNCH_CHECK();
     return MUYO_OK;
 }
@@ -1049,7 +1081,7 @@ extern "C" int muyo_cuda_argmax_pairs(const void* pairs, uint32_t n_pairs, int32
     clear_error();
     MUYO_REQUIRE(pairs && d && n_pairs > 0, "argmax_pairs: null buffer or no pairs");
     MUYO_REQUIRE((reinterpret_cast<uintptr_t>(pairs) & 7u) == 0, "argmax_pairs: pairs must be 8-byte aligned");
-    k_argmax_final<<<1, kThreads, 0, as_stream(stream)>>>(static_cast<const ArgPair*>(pairs), (int)n_pairs, d);
+    MUYO_CUDA_TRY(launch_kernel(k_argmax_final, dim3(1), dim3(kThreads), 0, as_stream(stream), true, static_cast<const ArgPair*>(pairs), (int)n_pairs, d));
     MUYO_LAUNCH_CHECK();
     return MUYO_OK;
 }
