@@ -51,6 +51,7 @@ enum Epilogue { EPI_BIAS = 1, EPI_RESIDUAL = 2, EPI_SWIGLU = 3, EPI_LOGITS = 4 }
 struct PfSet {
     const void* p[2];
     size_t bytes[2];
+    size_t per_cta[2];  // slice of each range per CTA (a multiple of 16), set at launch
 };
 
 struct GemvFused {
@@ -303,7 +304,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvFused a)
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
             const size_t n = a.pf.bytes[r];
-            const size_t per = (n / gridDim.x + 16) / 16 * 16;
+            const size_t per = a.pf.per_cta[r];
             const size_t off = (size_t)blockIdx.x * per;
             if (n > 0 && off < n) {
                 const char* base = static_cast<const char*>(a.pf.p[r]) + off;
@@ -392,7 +393,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvFused a)
                         ksum[warp][m][r] = acc[m][r];
             }
             __syncthreads();
-            if (ks == 0 && lane == 0) {
+            if (ks == 0) {  // every lane: the epilogue of row r runs in lane r
 #pragma unroll
                 for (int m = 0; m < NMAT; ++m)
 #pragma unroll
@@ -406,29 +407,34 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvFused a)
             }
             __syncthreads();
         }
-        float epi[ROWS];
+        if (EPI == EPI_LOGITS) {
+            if (ks == 0 && lane == 0 && nvalid > 0) {
 #pragma unroll
-        for (int r = 0; r < ROWS; ++r)
-            epi[r] = __shfl_sync(0xffffffffu, epi_op, r);
-        if (ks == 0 && lane == 0 && nvalid > 0) {
-#pragma unroll
-            for (int r = 0; r < ROWS; ++r) {
-                if (r >= nvalid)
-                    break;
-                const int row = row0 + r;
-                if (EPI == EPI_BIAS) {
-                    a.y[row] = acc[0][r] + epi[r];
-                } else if (EPI == EPI_RESIDUAL) {
-                    a.y[row] = epi[r] + acc[0][r];
-                } else if (EPI == EPI_SWIGLU) {
-                    a.y[row] = silu_mul(acc[0][r], acc[NMAT - 1][r]);
-                } else {  // EPI_LOGITS
+                for (int r = 0; r < ROWS; ++r) {
+                    if (r >= nvalid)
+                        break;
+                    const int row = row0 + r;
                     const float v = acc[0][r];
                     a.y[row] = v;
                     if (pair_better(v, row, bv, bi))
                         bv = v, bi = row;
                 }
             }
+        } else if (ks == 0 && lane < ROWS && lane < nvalid) {
+            // After the butterfly every lane holds every row's sum: lane r finishes row r, whose
+            // epilogue operand it loaded itself.
+            float s0 = acc[0][0], s1 = acc[NMAT - 1][0];
+#pragma unroll
+            for (int r = 1; r < ROWS; ++r)
+                if (lane == r)
+                    s0 = acc[0][r], s1 = acc[NMAT - 1][r];
+            const int row = row0 + lane;
+            if (EPI == EPI_BIAS)
+                a.y[row] = s0 + epi_op;
+            else if (EPI == EPI_RESIDUAL)
+                a.y[row] = epi_op + s0;
+            else  // EPI_SWIGLU
+                a.y[row] = silu_mul(s0, s1);
         }
     }
 
@@ -476,6 +482,13 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvFused a)
     }
 }
 
+// Each CTA of a grid of `grid` CTAs prefetches one slice (a multiple of 16 bytes) of each range.
+static void set_prefetch_slices(PfSet& pf, int grid)
+{
+    for (int r = 0; r < 2; ++r)
+        pf.per_cta[r] = (pf.bytes[r] / (size_t)grid + 16) / 16 * 16;
+}
+
 // Every kernel of the decode step asks for the largest shared-memory carveout: the L1/shared split
 // is set per SM, so a kernel that starts early (programmatic launch) can only be placed on SMs whose
 // split already leaves it room, and a uniform split lets consecutive kernels share SMs.
@@ -520,6 +533,7 @@ static int launch_gemv(const GemvFused& a, int max_ctas, cudaStream_t s, bool pd
             if (resident_ctas(ksw, kGemvThreads, smem_sw) >= ntiles_sw) {
                 GemvFused b = a;
                 b.wofs = (unsigned)wofs;
+                set_prefetch_slices(b.pf, ntiles_sw);
                 MUYO_CUDA_TRY(launch_kernel(ksw, dim3(ntiles_sw), dim3(kGemvThreads), smem_sw, s, pdl, b));
                 MUYO_LAUNCH_CHECK();
                 return MUYO_OK;
@@ -535,7 +549,9 @@ static int launch_gemv(const GemvFused& a, int max_ctas, cudaStream_t s, bool pd
     const int resident = resident_ctas(k, kGemvThreads, smem);
     if (grid > resident)
         grid = resident;
-    MUYO_CUDA_TRY(launch_kernel(k, dim3(grid), dim3(kGemvThreads), smem, s, pdl, a));
+    GemvFused b = a;
+    set_prefetch_slices(b.pf, grid);
+    MUYO_CUDA_TRY(launch_kernel(k, dim3(grid), dim3(kGemvThreads), smem, s, pdl, b));
     MUYO_LAUNCH_CHECK();
     return MUYO_OK;
 }

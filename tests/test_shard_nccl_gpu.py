@@ -1,0 +1,89 @@
+"""Row-sharded LM-head GEMV with the cross-GPU greedy pick (muyo_llm_b200/shard.py) on real GPUs:
+two ranks, one per GPU, NCCL all-gathers of the (value, index) pairs and of the F32 slices.
+
+Each rank builds the same seeded 151936 x 896 F16 matrix (the Qwen2.5-0.5B LM head) and x, computes
+its contiguous row range through muyo_cuda_mat_vec_f16_argmax, and must agree with one GPU computing
+the whole GEMV: identical greedy index (argmax is compare-only) and identical logits (each row's
+arithmetic does not depend on the sharding). Planted maxima on either side of the shard boundary and a
+tie across it check the first-index rule. Needs 2 GPUs; skipped otherwise.
+"""
+from __future__ import annotations
+
+import datetime
+import os
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+ROWS, COLS = 151936, 896
+
+
+def _inputs(plant):
+    rng = np.random.default_rng(20261202)
+    w = (rng.uniform(-1, 1, (ROWS, COLS)) * 0.05).astype(np.float16)
+    x = rng.standard_normal(COLS).astype(np.float32)
+    for row, val in plant:
+        w[row] = np.float16(0.0)
+        w[row, 0] = np.float16(val)
+    x[0] = 1.0
+    return w, x
+
+
+def _worker(rank, world, port, results):
+    import torch
+    import torch.distributed as dist
+
+    from muyo_llm_b200 import _abi, nodes, shard
+
+    torch.cuda.set_device(rank)
+    _abi.call("muyo_cuda_init", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    try:
+        out = []
+        for plant in ([(1000, 40.0)], [(ROWS // 2 + 3, 40.0)], [(ROWS // 2 - 1, 40.0), (ROWS // 2, 40.0)]):
+            w, x = _inputs(plant)
+            begin, end = shard.shard_rows(ROWS, world, rank)
+            per = shard.rows_per_rank(ROWS, world)
+            wd = torch.from_numpy(w[begin:end]).cuda()
+            xd = torch.from_numpy(x).cuda()
+            be = shard.CudaNcclBackend(wd, begin, end - begin)
+            be.set_output(torch.zeros(per, dtype=torch.float32, device="cuda"))
+            token, logits = shard.RowShardedGemv(ROWS, world, rank, be)(xd)
+            torch.cuda.synchronize()
+            if rank == 0:
+                full = torch.empty(ROWS, dtype=torch.float32, device="cuda")
+                nodes.mat_vec_f16(nodes.mat_vec_params(COLS, ROWS), torch.from_numpy(w).cuda(), xd, full)
+                p = nodes.argmax_params(ROWS)
+                wsb = nodes.argmax_workspace_size(p)
+                ws = torch.empty(wsb, dtype=torch.uint8, device="cuda")
+                ref = torch.empty(1, dtype=torch.int32, device="cuda")
+                nodes.argmax(p, full, ref, ws, wsb)
+                torch.cuda.synchronize()
+                out.append((int(token.item()), int(ref.item()), bool(torch.equal(logits, full)), plant[0][0]))
+        if rank == 0:
+            results.put(out)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_row_sharded_lm_head_two_gpus(cuda):
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    port = 29000 + os.getpid() % 1000
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, results)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    for token, ref, same_logits, planted in results.get(timeout=10):
+        assert token == ref == planted
+        assert same_logits
