@@ -11,6 +11,7 @@ shard), summed. Timed on the device with CUDA events around K sequences, max ove
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--engine graph|persistent]
   python bench.py --suite gemv [--shapes 14336x4096,...]   # F16 GEMV sweep, one JSON line per shape
   python bench.py --suite ops                              # op latency + multi-row bandwidth sweep
+  torchrun --nproc-per-node N bench.py --suite gemv_sharded  # row-sharded GEMV + NCCL gathers (C5)
 
 `--impl reference` times the reference's CPU forward on the host cores instead: the C oracle port
 (oracle/oracle.c, the reference's numpy forward restated in C, row-parallel on all host threads;
@@ -268,9 +269,31 @@ def run_suite(args):
 
     from muyo_llm_b200 import _abi, sweep
 
-    torch.cuda.set_device(0)
-    _abi.call("muyo_cuda_init", 0)
+    rank, world, local_rank = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local_rank)
+    _abi.call("muyo_cuda_init", local_rank)
     peak, peak_kind = measured_peaks()
+    if args.suite == "gemv_sharded":
+        dist = None
+        if world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", local_rank))
+        shapes = [tuple(int(v) for v in s.split("x")) for s in args.shapes.split(",") if s] or None
+        with ClockSampler(local_rank) as clocks:
+            res = sweep.gemv_sharded(rank, world, dist, args.iters, peak, shapes=shapes)
+        if rank == 0:
+            for r in res:
+                r.update({"suite": args.suite, "peak_GB_s": peak, "peak_kind": peak_kind})
+                print(json.dumps(r), flush=True)
+            print(json.dumps({"suite": args.suite, "clocks": clocks.summary()}), flush=True)
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     with ClockSampler(0) as clocks:
         if args.suite == "gemv":
             shapes = [tuple(int(v) for v in s.split("x")) for s in args.shapes.split(",") if s] or None
@@ -291,7 +314,7 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--engine", default="graph", choices=["persistent", "graph"])
-    ap.add_argument("--suite", default="decode", choices=["decode", "gemv", "ops"],
+    ap.add_argument("--suite", default="decode", choices=["decode", "gemv", "ops", "gemv_sharded"],
                     help="decode: the config-4 headline line (default); gemv / ops: kernel sweeps, one JSON line "
                          "per case (1 GPU)")
     ap.add_argument("--shapes", default="", help="gemv suite: comma-separated ROWSxCOLS list (default: all)")

@@ -121,3 +121,98 @@ def ops(iters: int = 0, peak_gbs: float = 6462.1, seed: int = 7):
     ms = _time_calls(lambda i: nodes.get_rows_f16(p, table, ids, d), 1, iters or 200)
     out.append(_result("k_get_rows", "1 of 151936x896", 896 * 2 + 896 * 4 + 4, ms, peak_gbs, mode="latency"))
     return out
+
+
+SHARDED_SHAPES = [(151936, 896), (4096, 4096), (14336, 4096), (128256, 4096)]
+
+
+def gemv_sharded(rank: int, world: int, dist=None, iters: int = 0, peak_gbs: float = 6462.1, seed: int = 7,
+                 shapes=None):
+    """Row-sharded GEMV (muyo_llm_b200/shard.py) over `world` GPUs, one rank per GPU: each rank holds
+    ceil(M / world) rows of W. Per shape, two timings on the device (max over ranks):
+    * kernel: the local muyo_cuda_mat_vec_f16_argmax alone -> per-GPU GB/s of its shard;
+    * e2e: the whole sharded call - local GEMV + argmax, NCCL all-gather of the (value, index) pairs,
+      the cross-rank pick, NCCL all-gather of the output slices -> aggregate GB/s of the full matrix.
+    Shards rotate over enough copies that more than 4x L2 is touched between two reads of one copy."""
+    from . import shard
+
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed * 1000 + rank)
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+
+    out = []
+    for rows, cols in shapes or SHARDED_SHAPES:
+        begin, end = shard.shard_rows(rows, world, rank)
+        local, per = end - begin, shard.rows_per_rank(rows, world)
+        wbytes = max(local, 1) * cols * 2
+        n_buf = max(1, math.ceil(4 * L2_BYTES / wbytes)) if wbytes < 4 * L2_BYTES else 1
+        W = [torch.rand(max(local, 1) * cols, generator=g, device="cuda").mul_(2).sub_(1).half().view(max(local, 1), cols)
+             for _ in range(n_buf)]
+        x = torch.rand(cols, generator=g, device="cuda").mul_(2).sub_(1)
+        if dist is not None:
+            dist.broadcast(x, 0)  # x is replicated
+        backends = []
+        for w in W:
+            be = shard.CudaNcclBackend(w, begin, local) if dist is not None else _LocalBackend(w, begin, local)
+            be.set_output(torch.zeros(per, dtype=torch.float32, device="cuda"))
+            backends.append(be)
+        calls = [shard.RowShardedGemv(rows, world, rank, be) for be in backends]
+        n = iters or max(20, 4 * n_buf)
+
+        def timed(fn):
+            for i in range(3):
+                fn(i % n_buf)
+            barrier()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for i in range(n):
+                fn(i % n_buf)
+            e.record()
+            barrier()
+            return max_over_ranks(s.elapsed_time(e) / n)
+
+        ms_k = timed(lambda i: backends[i].gemv_argmax(x))
+        ms_e = timed(lambda i: calls[i](x))
+        total = rows * cols * 2 + cols * 4 + rows * 4
+        local_bytes = local * cols * 2 + cols * 4 + local * 4
+        out.append({"kernel": "k_mat_vec_f16 + argmax, row-sharded", "shape": f"{rows}x{cols}", "n_gpus": world,
+                    "rows_per_gpu": per, "kernel_us": ms_k * 1e3, "kernel_GB_s_per_gpu": local_bytes / (ms_k * 1e-3) / 1e9,
+                    "kernel_frac_of_peak": local_bytes / (ms_k * 1e-3) / 1e9 / peak_gbs,
+                    "e2e_us": ms_e * 1e3, "e2e_GB_s_aggregate": total / (ms_e * 1e-3) / 1e9,
+                    "e2e_includes": "local GEMV+argmax, NCCL all_gather of pairs and of the F32 output, pick",
+                    "shard_copies": n_buf, "calls": n})
+        del W, backends, calls
+        torch.cuda.empty_cache()
+    return out
+
+
+class _LocalBackend:
+    """One GPU, no process group: the gathers are the local tensors themselves."""
+
+    def __init__(self, w, begin, local):
+        from . import shard
+
+        self.inner = shard.CudaNcclBackend(w, begin, local)
+
+    def set_output(self, y):
+        self.inner.set_output(y)
+
+    def gemv_argmax(self, x):
+        return self.inner.gemv_argmax(x)
+
+    def all_gather(self, t):
+        return t[None]
+
+    def pick(self, pairs):
+        return self.inner.pick(pairs)
