@@ -340,6 +340,30 @@ int muyo_cuda_argmax_pairs(const void* pairs, uint32_t n_pairs, int32_t* d, void
 size_t muyo_cuda_argmax_noalloc_max_pairs(void);
 int muyo_cuda_argmax_noalloc(const MuyoGenericParams* p, const float* a, int32_t* d, void* stream);
 
+/* ---- row-sharded GEMV fused with its all-gather over NVLink peer memory ---------------------------
+ * No counterpart in the reference, which runs on one GPU: the multi-GPU form of its LM head +
+ * greedy pick (src/FullModel.cpp:973-998, src/Sampler.cpp:32-43). `world` processes, one per GPU
+ * of one node, each own a group. Set-up (allocates; not for the hot path):
+ *   muyo_p2p_create   allocates this rank's buffer (a header and the full [rows_total] F32 output)
+ *                     and writes its CUDA IPC handle (muyo_p2p_handle_bytes() bytes) to handle_out;
+ *   muyo_p2p_connect  opens every other rank's handle (handles: world of them, in rank order).
+ * muyo_cuda_mat_vec_f16_allgather is a collective: every rank calls it, in the same order, with its
+ * contiguous shard (rows [row_begin, row_begin + p->rows) of the full matrix). One kernel per GPU
+ * computes the shard, stores it into every rank's output over NVLink, exchanges the shards'
+ * (max, first index) pairs and flags through peer memory, and writes the greedy index to *token
+ * (device int32) on every rank; the full output is then at muyo_p2p_output on every rank. The wait
+ * for the peers is bounded (2 s): if a rank does not take part, the others finish with token 0 and
+ * muyo_p2p_check (synchronising) reports MUYO_ETIMEOUT. No multicast, no TMA: plain peer stores. */
+typedef struct MuyoP2PGroup MuyoP2PGroup;
+size_t muyo_p2p_handle_bytes(void);
+int muyo_p2p_create(int world, int rank, uint32_t rows_total, MuyoP2PGroup** out, void* handle_out);
+int muyo_p2p_connect(MuyoP2PGroup* g, const void* handles);
+int muyo_cuda_mat_vec_f16_allgather(MuyoP2PGroup* g, const MuyoMatVecParams* p, const void* a, const float* b,
+                                    uint32_t row_begin, int32_t* token, void* stream);
+int muyo_p2p_output(MuyoP2PGroup* g, float** y);
+int muyo_p2p_check(MuyoP2PGroup* g);
+int muyo_p2p_destroy(MuyoP2PGroup* g);
+
 #ifdef __cplusplus
 }
 #endif

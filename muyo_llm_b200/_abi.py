@@ -125,6 +125,13 @@ SIGNATURES = {
     "muyo_cuda_argmax_pairs": (C.c_int, [VP, U32, VP, VP]),
     "muyo_cuda_argmax_noalloc_max_pairs": (C.c_size_t, []),
     "muyo_cuda_argmax_noalloc": (C.c_int, [P(GenericParams), VP, VP, VP]),
+    "muyo_p2p_handle_bytes": (C.c_size_t, []),
+    "muyo_p2p_create": (C.c_int, [C.c_int, C.c_int, U32, P(VP), VP]),
+    "muyo_p2p_connect": (C.c_int, [VP, VP]),
+    "muyo_cuda_mat_vec_f16_allgather": (C.c_int, [VP, P(MatVecParams), VP, VP, U32, VP, VP]),
+    "muyo_p2p_output": (C.c_int, [VP, P(VP)]),
+    "muyo_p2p_check": (C.c_int, [VP]),
+    "muyo_p2p_destroy": (C.c_int, [VP]),
 }
 
 _lib = None

@@ -3,6 +3,8 @@
 // src/RmsNorm.cpp, src/Rope.cpp, ...) and its node-per-op graph; the fused decode path lives in
 // decode.cu.
 #include <climits>
+#include <cstddef>
+#include <new>
 #include <cmath>
 #include <mutex>
 
@@ -12,6 +14,13 @@
 namespace muyo {
 
 constexpr int kThreads = 256;
+
+__device__ __forceinline__ unsigned long long now_ns_ops()
+{
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 constexpr int kMaxStagedK = 56 * 1024;  // floats of x staged in shared memory (224 KB)
 
 // ---- GEMV ------------------------------------------------------------------------------------------
@@ -758,6 +767,139 @@ __global__ void __launch_bounds__(kThreads) k_pairs_to_pair(const ArgPair* __res
         *out = r;
 }
 
+
+// ---- row-sharded GEMV fused with its all-gather over NVLink peer memory ---------------------------
+// One GPU's share of y = W x over `world` GPUs of one node (one process each). Every rank owns a
+// P2PBuffer (header + the full [rows_total] output), and every rank's buffer is mapped into every
+// other rank through CUDA IPC. A call is one kernel per GPU:
+//   1. each CTA computes its rows and stores every value into every rank's output (NVLink stores);
+//   2. each CTA leaves its best (value, global index) in the local header, fences at system scope
+//      and counts itself in;
+//   3. the last CTA reduces the rank's pair, stores it into every rank's pair slot, fences, and
+//      releases its flag slot in every rank (system scope) with the call's epoch;
+//   4. it then waits (bounded) for every rank's flag in its own header, and writes the first-index
+//      maximum over the ranks' pairs as the token.
+// The epoch is the caller's call counter, identical on every rank, so flags never need resetting.
+constexpr int kP2PMaxRanks = 8;
+constexpr unsigned long long kP2PWaitNs = 2000000000ull;
+
+struct P2PHeader {
+    unsigned flags[kP2PMaxRanks];  // flags[r]: the last epoch rank r has published into this buffer
+    ArgPair pairs[kP2PMaxRanks];   // pairs[r]: rank r's (max value, first global index)
+    int counter;                   // arrivals of this rank's CTAs (reset by the last one)
+    int err;                       // 5: a wait for a peer's flag expired
+    int pad[14];
+};
+
+struct P2PArgs {
+    const __half* A;  // local shard [local_rows][lda]
+    const float* x;
+    int K, k8, local_rows, row_begin, rows_total, world, rank;
+    long long lda;
+    unsigned epoch;
+    float* y[kP2PMaxRanks];          // every rank's output (this rank's slice is written into each)
+    P2PHeader* hdr[kP2PMaxRanks];    // every rank's header
+    ArgPair* cta_pairs;              // local scratch: one pair per CTA
+    int32_t* token;
+};
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v)
+{
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p)
+{
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+template <int ROWS>
+__global__ void __launch_bounds__(kThreads) k_gemv_allgather(P2PArgs p)
+{
+    extern __shared__ float xs[];
+    __shared__ int last_sm;
+    pdl_wait();
+    pdl_trigger();
+    stage_x_split(xs, p.x, p.K, p.k8);
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    GemvArgs<ROWS, 4, 1> ga{{p.A}, (size_t)p.lda};
+    float bv = -INFINITY;
+    int bi = INT_MAX;
+    for (int row0 = (blockIdx.x * nw + warp) * ROWS; row0 < p.local_rows; row0 += gridDim.x * nw * ROWS) {
+        const int nvalid = min(ROWS, p.local_rows - row0);
+        float acc[1][ROWS];
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r)
+            acc[0][r] = 0.0f;
+        warp_gemv_f16<ROWS, 4, 1>(ga, row0, nvalid, xs, p.k8, lane, acc);
+        warp_gemv_f16_tail<ROWS, 1>(ga.w, ga.ldw, row0, nvalid, xs, p.k8, p.K, lane, acc);
+        warp_reduce_acc<ROWS, 1>(acc);
+        // lanes 0 .. world-1 each store the rows into one rank's output
+        if (lane < p.world) {
+            float* yr = p.y[lane] + p.row_begin;
+#pragma unroll
+            for (int r = 0; r < ROWS; ++r)
+                if (r < nvalid)
+                    yr[row0 + r] = acc[0][r];
+        }
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r)
+            if (r < nvalid && pair_better(acc[0][r], p.row_begin + row0 + r, bv, bi))
+                bv = acc[0][r], bi = p.row_begin + row0 + r;
+    }
+    const ArgPair cta = block_argmax(bv, bi);  // uniform across the CTA after its last __syncthreads
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        p.cta_pairs[blockIdx.x] = cta;
+        __threadfence_system();  // this CTA's output stores (to every rank) before its arrival
+        last_sm = atomicAdd(&p.hdr[p.rank]->counter, 1) == (int)gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!last_sm)
+        return;
+    __threadfence_system();
+    float v = -INFINITY;
+    int i = INT_MAX;
+    for (int k = threadIdx.x; k < (int)gridDim.x; k += blockDim.x) {
+        const ArgPair q{__ldcg(&p.cta_pairs[k].v), __ldcg(&p.cta_pairs[k].i)};
+        if (pair_better(q.v, q.i, v, i))
+            v = q.v, i = q.i;
+    }
+    const ArgPair mine = block_argmax(v, i);
+    if (threadIdx.x != 0)
+        return;
+    P2PHeader* own = p.hdr[p.rank];
+    own->counter = 0;
+    for (int r = 0; r < p.world; ++r)
+        p.hdr[r]->pairs[p.rank] = mine;
+    __threadfence_system();
+    for (int r = 0; r < p.world; ++r)
+        st_release_sys(&p.hdr[r]->flags[p.rank], p.epoch);
+    // every rank's slice and pair are in this buffer once its flag carries this epoch
+    const unsigned long long t0 = now_ns_ops();
+    bool ok = true;
+    for (int r = 0; r < p.world && ok; ++r) {
+        while ((int)(ld_acquire_sys(&own->flags[r]) - p.epoch) < 0) {
+            if (now_ns_ops() - t0 > kP2PWaitNs) {
+                ok = false;
+                atomicMax(&own->err, 5);
+                break;
+            }
+        }
+    }
+    float bv2 = -INFINITY;
+    int bi2 = INT_MAX;
+    if (ok)
+        for (int r = 0; r < p.world; ++r) {
+            const ArgPair q{__ldcg(&own->pairs[r].v), __ldcg(&own->pairs[r].i)};
+            if (pair_better(q.v, q.i, bv2, bi2))
+                bv2 = q.v, bi2 = q.i;
+        }
+    *p.token = bi2 == INT_MAX ? 0 : bi2;
+}
 }  // namespace muyo
 
 using namespace muyo;
@@ -1142,4 +1284,157 @@ extern "C" int muyo_cuda_argmax_noalloc(const MuyoGenericParams* p, const float*
     // Every partial is written by the first kernel before the second reads it, so no part of the
     // scratch has to start at zero.
     return argmax_launch(a, p->KX, KY, 0, part, d, as_stream(stream));
+}
+
+
+// ---- row-sharded GEMV + all-gather over NVLink: host side -------------------------------------------
+struct MuyoP2PGroup {
+    int device = -1, world = 0, rank = 0;
+    uint32_t rows_total = 0;
+    char* buf = nullptr;                 // own buffer: header, then the output
+    void* peer[kP2PMaxRanks] = {};       // opened peer buffers (nullptr for this rank)
+    ArgPair* cta_pairs = nullptr;        // per-CTA scratch (local)
+    int max_ctas = 0;
+    uint32_t epoch = 0;
+};
+
+static size_t p2p_bytes(uint32_t rows_total) { return sizeof(P2PHeader) + (size_t)rows_total * sizeof(float); }
+
+extern "C" size_t muyo_p2p_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+extern "C" int muyo_p2p_create(int world, int rank, uint32_t rows_total, MuyoP2PGroup** out, void* handle_out)
+{
+    clear_error();
+    MUYO_REQUIRE(out && handle_out, "p2p_create: null argument");
+    MUYO_REQUIRE(world >= 1 && world <= kP2PMaxRanks && rank >= 0 && rank < world,
+                 "p2p_create: world %d / rank %d outside 1..%d", world, rank, kP2PMaxRanks);
+    MUYO_REQUIRE(rows_total > 0 && rows_total <= (uint32_t)INT_MAX, "p2p_create: rows_total must be positive");
+    MuyoP2PGroup* g = new (std::nothrow) MuyoP2PGroup;
+    if (!g) {
+        set_error("p2p_create: out of host memory");
+        return MUYO_ENOMEM;
+    }
+    g->world = world, g->rank = rank, g->rows_total = rows_total;
+    int rc = MUYO_OK;
+    do {
+        if (cudaGetDevice(&g->device) != cudaSuccess) { rc = MUYO_ECUDA; break; }
+        g->max_ctas = sm_count() * 8;
+        if (cudaMalloc(&g->buf, p2p_bytes(rows_total)) != cudaSuccess ||
+            cudaMalloc(&g->cta_pairs, sizeof(ArgPair) * (size_t)g->max_ctas) != cudaSuccess) {
+            rc = MUYO_ENOMEM;
+            break;
+        }
+        if (cudaMemset(g->buf, 0, p2p_bytes(rows_total)) != cudaSuccess ||
+            cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle_out), g->buf) != cudaSuccess ||
+            cudaDeviceSynchronize() != cudaSuccess) {
+            rc = MUYO_ECUDA;
+            break;
+        }
+    } while (0);
+    if (rc != MUYO_OK) {
+        set_error("p2p_create: device allocation or IPC handle failed (%s)", cudaGetErrorString(cudaGetLastError()));
+        cudaFree(g->buf);
+        cudaFree(g->cta_pairs);
+        delete g;
+        return rc;
+    }
+    *out = g;
+    return MUYO_OK;
+}
+
+extern "C" int muyo_p2p_connect(MuyoP2PGroup* g, const void* handles)
+{
+    clear_error();
+    MUYO_REQUIRE(g && handles, "p2p_connect: null argument");
+    const cudaIpcMemHandle_t* h = static_cast<const cudaIpcMemHandle_t*>(handles);
+    for (int r = 0; r < g->world; ++r) {
+        if (r == g->rank || g->peer[r])
+            continue;
+        MUYO_CUDA_TRY(cudaIpcOpenMemHandle(&g->peer[r], h[r], cudaIpcMemLazyEnablePeerAccess));
+    }
+    return MUYO_OK;
+}
+
+extern "C" int muyo_p2p_output(MuyoP2PGroup* g, float** y)
+{
+    clear_error();
+    MUYO_REQUIRE(g && y, "p2p_output: null argument");
+    *y = reinterpret_cast<float*>(g->buf + sizeof(P2PHeader));
+    return MUYO_OK;
+}
+
+extern "C" int muyo_p2p_check(MuyoP2PGroup* g)
+{
+    clear_error();
+    MUYO_REQUIRE(g, "p2p_check: null group");
+    int e = 0;
+    MUYO_CUDA_TRY(cudaMemcpy(&e, g->buf + offsetof(P2PHeader, err), sizeof(int), cudaMemcpyDeviceToHost));
+    if (e) {
+        MUYO_CUDA_TRY(cudaMemset(g->buf + offsetof(P2PHeader, err), 0, sizeof(int)));
+        set_error("p2p: a wait for a peer's flag expired (a rank did not take part in the call)");
+        return MUYO_ETIMEOUT;
+    }
+    return MUYO_OK;
+}
+
+extern "C" int muyo_cuda_mat_vec_f16_allgather(MuyoP2PGroup* g, const MuyoMatVecParams* p, const void* a,
+                                               const float* b, uint32_t row_begin, int32_t* token, void* stream)
+{
+    clear_error();
+    MUYO_REQUIRE(g && token, "mat_vec_allgather: null group or token");
+    for (int r = 0; r < g->world; ++r)
+        MUYO_REQUIRE(r == g->rank || g->peer[r], "mat_vec_allgather: rank %d is not connected", r);
+    MUYO_REQUIRE(p && (p->batches <= 1) && p->fusion_flags == 0, "mat_vec_allgather: one batch, no fusion flags");
+    MUYO_REQUIRE((uint64_t)row_begin + p->rows <= g->rows_total, "mat_vec_allgather: rows [%u, %u) exceed %u", row_begin,
+                 row_begin + p->rows, g->rows_total);
+    MatVecDev q{};
+    int rc = mat_vec_prepare(p, a, b, reinterpret_cast<float*>(g->buf), nullptr, nullptr, 2, q);
+    if (rc != MUYO_OK)
+        return rc;
+    MUYO_REQUIRE(q.k8 > 0 && aligned16(b), "mat_vec_allgather: A and x must be 16-byte aligned with rows a multiple of 8");
+    P2PArgs args{};
+    args.A = static_cast<const __half*>(a);
+    args.x = b;
+    args.K = q.ncols, args.k8 = q.k8, args.local_rows = q.rows, args.row_begin = (int)row_begin;
+    args.rows_total = (int)g->rows_total, args.world = g->world, args.rank = g->rank, args.lda = q.stride_a;
+    args.epoch = ++g->epoch;
+    for (int r = 0; r < g->world; ++r) {
+        char* base = r == g->rank ? g->buf : static_cast<char*>(g->peer[r]);
+        args.hdr[r] = reinterpret_cast<P2PHeader*>(base);
+        args.y[r] = reinterpret_cast<float*>(base + sizeof(P2PHeader));
+    }
+    args.cta_pairs = g->cta_pairs;
+    args.token = token;
+    const bool two_rows = (q.rows + 15) / 16 >= 2 * sm_count();
+    const int rows_per_cta = (two_rows ? 2 : 1) * (kThreads / 32);
+    int grid = (q.rows + rows_per_cta - 1) / rows_per_cta;
+    if (grid > g->max_ctas)
+        grid = g->max_ctas;
+    const size_t smem = (size_t)q.ncols * sizeof(float);
+    const cudaStream_t s = as_stream(stream);
+    if (two_rows) {
+        MUYO_CUDA_TRY(set_smem(k_gemv_allgather<2>, smem));
+        MUYO_CUDA_TRY(launch_kernel(k_gemv_allgather<2>, dim3(grid), dim3(kThreads), smem, s, true, args));
+    } else {
+        MUYO_CUDA_TRY(set_smem(k_gemv_allgather<1>, smem));
+        MUYO_CUDA_TRY(launch_kernel(k_gemv_allgather<1>, dim3(grid), dim3(kThreads), smem, s, true, args));
+    }
+    MUYO_LAUNCH_CHECK();
+    return MUYO_OK;
+}
+
+extern "C" int muyo_p2p_destroy(MuyoP2PGroup* g)
+{
+    clear_error();
+    if (!g)
+        return MUYO_OK;
+    cudaSetDevice(g->device);
+    cudaDeviceSynchronize();
+    for (int r = 0; r < kP2PMaxRanks; ++r)
+        if (g->peer[r])
+            cudaIpcCloseMemHandle(g->peer[r]);
+    cudaFree(g->buf);
+    cudaFree(g->cta_pairs);
+    delete g;
+    return MUYO_OK;
 }

@@ -107,3 +107,72 @@ class CudaNcclBackend:
         self._abi.call("muyo_cuda_argmax_pairs", pairs.data_ptr(), pairs.shape[0], self.token.data_ptr(),
                        self.torch.cuda.current_stream().cuda_stream)
         return self.token
+
+
+class P2PShardedGemv:
+    """The same row-sharded GEMV + greedy pick as one kernel per GPU that writes its shard and its
+    (max, index) pair straight into every rank's buffer over NVLink (muyo_cuda_mat_vec_f16_allgather)
+    instead of two NCCL all-gathers. A collective: every rank constructs it (the CUDA IPC handles are
+    exchanged once over the process group) and calls it in the same order.
+
+    w_shard: torch float16 [rows_local, K] on this rank's GPU (rows [begin, end) of the full matrix).
+    """
+
+    def __init__(self, w_shard, rows: int, world: int, rank: int, group=None):
+        import ctypes as C
+
+        import torch
+        import torch.distributed as dist
+
+        from . import _abi, nodes
+
+        self.torch, self._abi, self.C = torch, _abi, C
+        self.rows, self.world, self.rank = rows, world, rank
+        self.begin, self.end = shard_rows(rows, world, rank)
+        self.w = w_shard
+        self.params = nodes.mat_vec_params(w_shard.shape[1], max(self.end - self.begin, 1))
+        self.params.rows = self.end - self.begin
+        n = int(_abi.lib().muyo_p2p_handle_bytes())
+        handle = (C.c_ubyte * n)()
+        g = C.c_void_p()
+        _abi.call("muyo_p2p_create", world, rank, rows, C.byref(g), handle)
+        self.g = g
+        mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=w_shard.device)
+        every = torch.empty(world * n, dtype=torch.uint8, device=w_shard.device)
+        dist.all_gather_into_tensor(every, mine, group=group)
+        blob = bytes(every.cpu().numpy().tobytes())
+        _abi.call("muyo_p2p_connect", g, C.create_string_buffer(blob, len(blob)))
+        dist.barrier(group=group)  # every rank has opened every handle before the first call
+        yp = C.c_void_p()
+        _abi.call("muyo_p2p_output", g, C.byref(yp))
+        self.y_ptr = yp.value
+        self.token = torch.empty(1, dtype=torch.int32, device=w_shard.device)
+
+    def __call__(self, x, stream=None):
+        """Returns the greedy index (device int32 [1]); the full output is at `output()`."""
+        s = stream if stream is not None else self.torch.cuda.current_stream().cuda_stream
+        self._abi.call("muyo_cuda_mat_vec_f16_allgather", self.g, self.params, self.w.data_ptr(), x.data_ptr(),
+                       self.begin, self.token.data_ptr(), s)
+        return self.token
+
+    def output(self):
+        """The full [rows] F32 output on this rank (a view of the group's buffer)."""
+        torch = self.torch
+        out = torch.empty(self.rows, dtype=torch.float32, device=self.w.device)
+        self._abi.call("muyo_cuda_copy_f32", _copy_params(self.rows), self.y_ptr, out.data_ptr(),
+                       torch.cuda.current_stream().cuda_stream)
+        return out
+
+    def check(self):
+        self._abi.call("muyo_p2p_check", self.g)
+
+    def close(self):
+        if getattr(self, "g", None):
+            self._abi.lib().muyo_p2p_destroy(self.g)
+            self.g = None
+
+
+def _copy_params(n: int):
+    from . import _abi
+
+    return _abi.UnaryParams(n, n, 1, 1, 1, 1, n, n, n, n, 1, 1, 1, 1, n, n, n, 0, 0)

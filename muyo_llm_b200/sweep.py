@@ -133,6 +133,8 @@ def gemv_sharded(rank: int, world: int, dist=None, iters: int = 0, peak_gbs: flo
     * kernel: the local muyo_cuda_mat_vec_f16_argmax alone -> per-GPU GB/s of its shard;
     * e2e: the whole sharded call - local GEMV + argmax, NCCL all-gather of the (value, index) pairs,
       the cross-rank pick, NCCL all-gather of the output slices -> aggregate GB/s of the full matrix.
+    * fused (N > 1): muyo_cuda_mat_vec_f16_allgather, the same result from one kernel per GPU that
+      stores its slice and pair into every GPU over NVLink.
     Shards rotate over enough copies that more than 4x L2 is touched between two reads of one copy."""
     from . import shard
 
@@ -184,6 +186,18 @@ def gemv_sharded(rank: int, world: int, dist=None, iters: int = 0, peak_gbs: flo
 
         ms_k = timed(lambda i: backends[i].gemv_argmax(x))
         ms_e = timed(lambda i: calls[i](x))
+        ms_p = None
+        if dist is not None and local > 0:
+            p2p = shard.P2PShardedGemv(W[0], rows, world, rank)
+
+            def fused(i):
+                p2p.w = W[i]
+                p2p(x)
+
+            ms_p = timed(fused)
+            p2p.check()
+            dist.barrier()
+            p2p.close()
         total = rows * cols * 2 + cols * 4 + rows * 4
         local_bytes = local * cols * 2 + cols * 4 + local * 4
         out.append({"kernel": "k_mat_vec_f16 + argmax, row-sharded", "shape": f"{rows}x{cols}", "n_gpus": world,
@@ -191,6 +205,10 @@ def gemv_sharded(rank: int, world: int, dist=None, iters: int = 0, peak_gbs: flo
                     "kernel_frac_of_peak": local_bytes / (ms_k * 1e-3) / 1e9 / peak_gbs,
                     "e2e_us": ms_e * 1e3, "e2e_GB_s_aggregate": total / (ms_e * 1e-3) / 1e9,
                     "e2e_includes": "local GEMV+argmax, NCCL all_gather of pairs and of the F32 output, pick",
+                    "fused_us": None if ms_p is None else ms_p * 1e3,
+                    "fused_GB_s_aggregate": None if ms_p is None else total / (ms_p * 1e-3) / 1e9,
+                    "fused_includes": "one kernel per GPU: local GEMV, output stored into every GPU over NVLink, pairs "
+                                      "and flags through peer memory, pick",
                     "shard_copies": n_buf, "calls": n})
         del W, backends, calls
         torch.cuda.empty_cache()

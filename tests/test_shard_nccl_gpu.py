@@ -87,3 +87,79 @@ def test_row_sharded_lm_head_two_gpus(cuda):
     for token, ref, same_logits, planted in results.get(timeout=10):
         assert token == ref == planted
         assert same_logits
+
+
+def _p2p_worker(rank, world, port, results):
+    import torch
+    import torch.distributed as dist
+
+    from muyo_llm_b200 import _abi, nodes, shard
+
+    torch.cuda.set_device(rank)
+    _abi.call("muyo_cuda_init", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    try:
+        out = []
+        plants = ([(1000, 40.0)], [(ROWS // 2 + 3, 40.0)], [(ROWS // 2 - 1, 40.0), (ROWS // 2, 40.0)])
+        begin, end = shard.shard_rows(ROWS, world, rank)
+        op = None
+        for plant in plants:
+            w, x = _inputs(plant)
+            wd = torch.from_numpy(w[begin:end]).cuda()
+            xd = torch.from_numpy(x).cuda()
+            if op is None:
+                op = shard.P2PShardedGemv(wd, ROWS, world, rank)
+            op.w = wd
+            for _ in range(3):  # repeated calls: the epoch advances, the flags never need resetting
+                token = op(xd)
+            y = op.output()
+            torch.cuda.synchronize()
+            op.check()
+            full = torch.empty(ROWS, dtype=torch.float32, device="cuda")
+            nodes.mat_vec_f16(nodes.mat_vec_params(COLS, ROWS), torch.from_numpy(w).cuda(), xd, full)
+            torch.cuda.synchronize()
+            out.append((int(token.item()), plant[0][0], bool(torch.equal(y, full))))
+        # rank 1 sits one call out: rank 0's wait for its flag must expire and be reported
+        dist.barrier()
+        timed_out = None
+        if rank == 0:
+            op(xd)
+            torch.cuda.synchronize()
+            try:
+                op.check()
+                timed_out = False
+            except _abi.MuyoError as e:
+                timed_out = e.rc == -3
+        dist.barrier()
+        results.put((rank, out, timed_out))
+        op.close()  # the ranks' epochs now differ, so the group is not used again
+    finally:
+        dist.destroy_process_group()
+
+
+def test_fused_gemv_allgather_two_gpus(cuda):
+    """muyo_cuda_mat_vec_f16_allgather: the shards go to every GPU over NVLink stores and the
+    pairs and flags through peer memory. The full output is bit-identical to one GPU's GEMV on
+    every rank, and the token is the planted first-index maximum. A rank that skips a call makes
+    the others' bounded wait expire with MUYO_ETIMEOUT (no hang)."""
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    port = 30000 + os.getpid() % 1000
+    procs = [ctx.Process(target=_p2p_worker, args=(r, 2, port, results)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    got = sorted(results.get(timeout=10) for _ in range(2))
+    for rank, out, timed_out in got:
+        for token, planted, same in out:
+            assert token == planted and same, (rank, token, planted, same)
+        if rank == 0:
+            assert timed_out is True
