@@ -67,6 +67,21 @@ def bytes_per_token(cfg, pos_avg: float, kv_bytes: int = 2) -> float:
     return L * (per_layer + kv) + V * H * 2 + H * 4 + H * 2
 
 
+def step_traffic(cfg, pos_avg: float):
+    """DRAM bytes of one graph-engine decode step from the committed ncu capture
+    (profiles/decode_step_dram_traffic_c4short.md, positions 0..7, warm caches), plus the algorithmic
+    difference in KV-cache reads between those positions and pos_avg. None if the summary is absent."""
+    path = os.path.join(ROOT, "profiles", "decode_step_dram_traffic_c4short.md")
+    try:
+        for line in open(path):
+            if line.startswith("dram bytes per decode step:"):
+                measured = float(line.split(":")[1])
+                return measured + bytes_per_token(cfg, pos_avg) - bytes_per_token(cfg, 3.5)
+    except OSError:
+        pass
+    return None
+
+
 class ClockSampler:
     """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
 
@@ -236,8 +251,10 @@ def run_b200(args, rank, world, local_rank):
         kernel = ("k_decode_persistent: one launch per sequence runs all 288 decode steps; algorithmic bytes "
                   "of the 288 steps / sequence time")
         launches = 2 * args.steps  # control kernel + persistent kernel per sequence
+    traffic = step_traffic(cfg, pos_avg) if args.engine == "graph" else None
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "traffic": None, "peak_kind": peak_kind, "kernel": kernel}
+                "traffic": traffic, "traffic_unit": "bytes per decode step", "algorithmic_bytes_per_step": alg,
+                "peak_kind": peak_kind, "kernel": kernel}
     cb = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = cpu_baseline(cfg, tensors, prompt, 8)

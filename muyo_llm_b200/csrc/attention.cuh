@@ -23,7 +23,7 @@
 namespace muyo {
 
 constexpr int kAttnKeys = 64;      // keys per work item
-constexpr int kAttnThreads = 256;  // threads of the standalone attention CTA
+constexpr int kAttnThreads = 512;  // threads of the standalone attention CTA
 constexpr int kAttnMaxGroup = 16;  // query heads per KV head
 
 struct AttnDev {
