@@ -255,8 +255,18 @@ static int launch_mat_vec(bool f16, const MatVecDev& q, int batches, const void*
     const size_t smem = (size_t)q.ncols * sizeof(float);
     dim3 grid(gx, batches);
     if (f16) {
+        // Loads in flight per lane grow with K so that a warp covers a long row in few round trips:
+        // U chunks of 16 bytes per row per lane (each lane still adds its chunks in column order).
+        const int lane_chunks = q.k8 / 32;
         auto k = k_mat_vec_f16<ROWS, 4>;
+        if (lane_chunks >= 8)
+            k = k_mat_vec_f16<ROWS, 8>;
         MUYO_CUDA_TRY(set_smem(k, smem));
+        // CTAs stride over the row tiles: the grid stops at what is resident at once
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, smem) == cudaSuccess && per_sm > 0 &&
+            batches == 1 && grid.x > (unsigned)(per_sm * sm_count()))
+            grid.x = per_sm * sm_count();
         MUYO_CUDA_TRY(launch_kernel(k, dim3(grid), dim3(kThreads), smem, s, true, q, static_cast<const __half*>(a), b, d, f0, f1));
     } else {
         auto k = k_mat_vec_f32<ROWS, 4>;
