@@ -93,14 +93,34 @@ struct GemvFused {
 // L = sum_c l_c exp(m_c - M), then x[h * hd + d] = sum_c o_c[d] w_c. Each pass issues its loads
 // together: the statistics of all heads and chunks, then four chunks of every element a thread
 // owns. `scratch` holds 2 * heads * max_chunks floats.
-__device__ __forceinline__ void stage_merge(const GemvFused& a, float4* xs4, float* scratch)
+__device__ __forceinline__ void stage_merge(const GemvFused& a, float4* xs4, float* scratch, int pos)
 {
     float* xs = reinterpret_cast<float*>(xs4);
     const int K = a.K, K8 = K / 8, hd = a.hd, G = a.gqa, heads = K / hd, stride = hd + 2;
     const int tid = threadIdx.x, nt = blockDim.x;
-    const int pos = __ldcg(a.pos);
     const int nchunks = pos >= 0 && pos < a.max_seq ? (pos + kAttnKeys) / kAttnKeys : 0;
     auto part_at = [&](int h, int c) { return a.attn_part + ((size_t)((h / G) * a.max_chunks + c) * G + h % G) * stride; };
+    constexpr int E = 4;                        // elements per thread per pass
+    const size_t cstride = (size_t)G * stride;  // floats between chunk c and c + 1 of one head
+    const float* src[E];                        // element e's value in chunk 0
+    int head[E];
+    auto locate = [&](int e0) {
+#pragma unroll
+        for (int j = 0; j < E; ++j) {
+            const int e = min(e0 + tid + j * nt, K - 1), h = e / hd;
+            head[j] = h;
+            src[j] = part_at(h, 0) + 2 + (e - h * hd);
+        }
+    };
+    // The first pass's values of chunks 0..3 do not depend on the statistics: their loads go out
+    // together with the statistics' loads.
+    locate(0);
+    float v0[E][4];
+#pragma unroll
+    for (int j = 0; j < E; ++j)
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            v0[j][u] = u < nchunks ? __ldcg(src[j] + (size_t)u * cstride) : 0.0f;
     float* mw = scratch;                   // [heads][nchunks]: m, then the normalised weight
     float* lw = scratch + heads * nchunks; // [heads][nchunks]: l
     for (int i = tid; i < heads * nchunks; i += nt) {
@@ -125,32 +145,29 @@ __device__ __forceinline__ void stage_merge(const GemvFused& a, float4* xs4, flo
             mw[h * nchunks + c] *= inv;
     }
     __syncthreads();
-    constexpr int E = 4;  // elements per thread per pass
-    const size_t cstride = (size_t)G * stride;  // floats between chunk c and c + 1 of one head
     for (int e0 = 0; e0 < K; e0 += E * nt) {
+        if (e0 > 0)
+            locate(e0);
         float o[E];
-        const float* src[E];  // element e's value in chunk 0
-        const float* w[E];    // its head's chunk weights
 #pragma unroll
-        for (int j = 0; j < E; ++j) {
+        for (int j = 0; j < E; ++j)
             o[j] = 0.0f;
-            const int e = min(e0 + tid + j * nt, K - 1), h = e / hd;
-            src[j] = part_at(h, 0) + 2 + (e - h * hd);
-            w[j] = mw + h * nchunks;
-        }
         for (int c = 0; c < nchunks; c += 4) {
             float v[E][4];
 #pragma unroll
             for (int j = 0; j < E; ++j)
 #pragma unroll
                 for (int u = 0; u < 4; ++u)
-                    v[j][u] = c + u < nchunks ? __ldcg(src[j] + (size_t)(c + u) * cstride) : 0.0f;
+                    v[j][u] = e0 == 0 && c == 0 ? v0[j][u]
+                                                : (c + u < nchunks ? __ldcg(src[j] + (size_t)(c + u) * cstride) : 0.0f);
 #pragma unroll
-            for (int j = 0; j < E; ++j)
+            for (int j = 0; j < E; ++j) {
+                const float* w = mw + head[j] * nchunks;
 #pragma unroll
                 for (int u = 0; u < 4; ++u)
                     if (c + u < nchunks)
-                        o[j] = fmaf(v[j][u], w[j][c + u], o[j]);
+                        o[j] = fmaf(v[j][u], w[c + u], o[j]);
+            }
         }
 #pragma unroll
         for (int j = 0; j < E; ++j) {
@@ -166,7 +183,7 @@ __device__ __forceinline__ void stage_merge(const GemvFused& a, float4* xs4, flo
 // apply the numpy reference's rms_norm, x / sqrt(mean(x^2) + eps) * w (tools/reference_qwen2.py:81-82),
 // in F32: the sum of squares with per-thread FMA partials and a shuffle tree.
 template <int PRO>
-__device__ __forceinline__ void stage_input(const GemvFused& a, float* xs, float* red)
+__device__ __forceinline__ void stage_input(const GemvFused& a, float* xs, float* red, int pos = 0)
 {
     // Every thread issues all loads of a pass (V float4s of x or of the embedding row, and of the
     // norm weight) before its first store, so a pass costs one memory round trip; K <= 4 * V * 256
@@ -196,7 +213,7 @@ __device__ __forceinline__ void stage_input(const GemvFused& a, float* xs, float
         return;
     }
     if (PRO == PRO_MERGE) {
-        stage_merge(a, xs4, xs + K);
+        stage_merge(a, xs4, xs + K, pos);
         return;
     }
     const __half* erow = nullptr;
@@ -318,9 +335,12 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvFused a)
             }
         }
     }
+    // MERGE: the position was written two or more launches back (by the previous step's LM head,
+    // or before a launch without programmatic serialisation), so it is read before the wait.
+    const int pos = PRO == PRO_MERGE ? __ldcg(a.pos) : 0;
     pdl_wait();  // the input vector and the epilogue operands come from earlier kernels
     pdl_trigger();
-    stage_input<PRO>(a, xs, red);  // ends with __syncthreads: the barrier's init is visible
+    stage_input<PRO>(a, xs, red, pos);  // ends with __syncthreads: the barrier's init is visible
     bool tile_ok = true;
     if (SW) {
         tile_ok = mbar_try_wait(&wbar, 0);
