@@ -340,6 +340,30 @@ int muyo_cuda_argmax_pairs(const void* pairs, uint32_t n_pairs, int32_t* d, void
 size_t muyo_cuda_argmax_noalloc_max_pairs(void);
 int muyo_cuda_argmax_noalloc(const MuyoGenericParams* p, const float* a, int32_t* d, void* stream);
 
+/* ---- token sampler ------------------------------------------------------------------------------
+ * Replaces Sampler::Sample (src/Sampler.cpp:10-98; parameters src/Sampler.h:14-22) on the device,
+ * with the std::mt19937_64 stream kept in device memory (muyo_sampler_state_bytes bytes, 8-byte
+ * aligned, seeded by muyo_sampler_seed as the engine's constructor seeds it). Same steps and order:
+ * repetition penalty over the last repeat_last_n history tokens (negative: all; once per
+ * occurrence), greedy when temperature <= 0 (first index of the maximum), else logits /= temperature,
+ * top-k (top_k <= 0: the whole vocabulary), weights exp(double(l - l_max)), nucleus cut at top_p,
+ * and a draw u = canonical double from the engine. logits is modified in place, as the reference
+ * does. Equal logits are ordered by lower index (the reference's partial_sort leaves their order
+ * unspecified). At most 4096 top-k candidates (MUYO_EUNSUPPORTED beyond). *token is a device int32. */
+typedef struct MuyoSamplerParams {
+    float temperature;
+    int32_t top_k;
+    float top_p;
+    float repeat_penalty;
+    int32_t repeat_last_n;
+    uint32_t reserved;
+    uint64_t seed; /* used by muyo_model_set_sampler */
+} MuyoSamplerParams;
+size_t muyo_sampler_state_bytes(void);
+int muyo_sampler_seed(void* state, uint64_t seed, void* stream);
+int muyo_cuda_sample(const MuyoSamplerParams* p, float* logits, uint32_t vocab, const int32_t* history,
+                     uint32_t hist_len, void* state, int32_t* token, void* stream);
+
 /* ---- row-sharded GEMV fused with its all-gather over NVLink peer memory ---------------------------
  * No counterpart in the reference, which runs on one GPU: the multi-GPU form of its LM head +
  * greedy pick (src/FullModel.cpp:973-998, src/Sampler.cpp:32-43). `world` processes, one per GPU

@@ -80,6 +80,11 @@ class Qwen2Config(C.Structure):
                [("rms_eps", F32), ("rope_base", F32), ("kv_dtype", U32)]
 
 
+class SamplerParams(C.Structure):
+    _fields_ = [("temperature", F32), ("top_k", C.c_int32), ("top_p", F32), ("repeat_penalty", F32),
+                ("repeat_last_n", C.c_int32), ("reserved", U32), ("seed", C.c_uint64)]
+
+
 class LayerWeights(C.Structure):
     _fields_ = [(n, VP) for n in ("attn_norm", "wqkv", "bqkv", "wo", "ffn_norm", "wgate", "wup", "wdown")]
 
@@ -125,6 +130,9 @@ SIGNATURES = {
     "muyo_cuda_argmax_pairs": (C.c_int, [VP, U32, VP, VP]),
     "muyo_cuda_argmax_noalloc_max_pairs": (C.c_size_t, []),
     "muyo_cuda_argmax_noalloc": (C.c_int, [P(GenericParams), VP, VP, VP]),
+    "muyo_sampler_state_bytes": (C.c_size_t, []),
+    "muyo_sampler_seed": (C.c_int, [VP, C.c_uint64, VP]),
+    "muyo_cuda_sample": (C.c_int, [P(SamplerParams), VP, U32, VP, U32, VP, VP, VP]),
     "muyo_p2p_handle_bytes": (C.c_size_t, []),
     "muyo_p2p_create": (C.c_int, [C.c_int, C.c_int, U32, P(VP), VP]),
     "muyo_p2p_connect": (C.c_int, [VP, VP]),

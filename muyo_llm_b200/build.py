@@ -20,7 +20,7 @@ LIB = os.path.join(LIBDIR, "libmuyo_cuda.so")
 INCLUDE = os.path.join(ROOT, "include")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CU_SOURCES = ["runtime.cu", "ops.cu", "decode.cu"]
+CU_SOURCES = ["runtime.cu", "ops.cu", "decode.cu", "sampler.cu"]
 CPP_SOURCES = ["gguf_loader.cpp"]
 HOST = os.path.join(PKG, "host")
 HOST_SOURCES = ["checks.cpp", "forward.cpp", "main.cpp"]

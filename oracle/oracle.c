@@ -535,3 +535,131 @@ void oracle_set_num_threads(int n)
     if (n > 0)
         g_threads = n;
 }
+
+/* ---- sampler (src/Sampler.cpp:10-98, src/Sampler.h:14-43) -------------------------------------
+ * std::mt19937_64 restated from its published definition (Matsumoto & Nishimura, 64-bit MT):
+ * n = 312, m = 156, r = 31, a = 0xB5026F5AA96619E9, tempering (u, d) = (29, 0x5555555555555555),
+ * (s, b) = (17, 0x71D67FFFEDA60000), (t, c) = (37, 0xFFF7EEE000000000), l = 43, seeding multiplier
+ * f = 6364136223846793005. */
+typedef struct OracleMt64 {
+    uint64_t mt[312];
+    int idx;
+} OracleMt64;
+
+void oracle_mt64_seed(OracleMt64* s, uint64_t seed)
+{
+    s->mt[0] = seed;
+    for (int i = 1; i < 312; ++i)
+        s->mt[i] = 6364136223846793005ULL * (s->mt[i - 1] ^ (s->mt[i - 1] >> 62)) + (uint64_t)i;
+    s->idx = 312;
+}
+
+uint64_t oracle_mt64_next(OracleMt64* s)
+{
+    const uint64_t upper = 0xFFFFFFFF80000000ULL, lower = 0x7FFFFFFFULL, a = 0xB5026F5AA96619E9ULL;
+    if (s->idx >= 312) {
+        for (int i = 0; i < 312; ++i) {
+            const uint64_t x = (s->mt[i] & upper) | (s->mt[(i + 1) % 312] & lower);
+            uint64_t xa = x >> 1;
+            if (x & 1ULL)
+                xa ^= a;
+            s->mt[i] = s->mt[(i + 156) % 312] ^ xa;
+        }
+        s->idx = 0;
+    }
+    uint64_t y = s->mt[s->idx++];
+    y ^= (y >> 29) & 0x5555555555555555ULL;
+    y ^= (y << 17) & 0x71D67FFFEDA60000ULL;
+    y ^= (y << 37) & 0xFFF7EEE000000000ULL;
+    y ^= y >> 43;
+    return y;
+}
+
+/* std::uniform_real_distribution<double>(0, 1) over a 64-bit engine: one draw x, x / 2^64 rounded
+ * to double, and a value that rounds up to 1 is replaced by the largest double below 1. */
+double oracle_mt64_canonical(OracleMt64* s)
+{
+    const double u = (double)oracle_mt64_next(s) * 0x1p-64;
+    return u >= 1.0 ? nextafter(1.0, 0.0) : u;
+}
+
+static const float* g_sort_logits;
+static int by_logit_desc(const void* pa, const void* pb)
+{
+    const int a = *(const int*)pa, b = *(const int*)pb;
+    const float la = g_sort_logits[a], lb = g_sort_logits[b];
+    if (la > lb)
+        return -1;
+    if (la < lb)
+        return 1;
+    return a < b ? -1 : (a > b);  /* equal logits: the lower index first */
+}
+
+/* Sampler::Sample. logits is modified in place (penalty, temperature), as the reference does. The
+ * top-k order is by logit, then by index among equal logits (std::partial_sort leaves their order
+ * unspecified). Not thread-safe (qsort's comparator reads a static). */
+int oracle_sample(float* logits, int vocab, float temperature, int top_k, float top_p, float repeat_penalty,
+                  int repeat_last_n, const int32_t* history, int hist_len, OracleMt64* rng)
+{
+    if (repeat_penalty != 1.0f && hist_len > 0) {  /* src/Sampler.cpp:12-29 */
+        int begin = 0;
+        if (repeat_last_n >= 0 && repeat_last_n < hist_len)
+            begin = hist_len - repeat_last_n;
+        for (int i = begin; i < hist_len; ++i) {
+            const int t = history[i];
+            if (t < 0 || t >= vocab)
+                continue;
+            const float v = logits[t];
+            logits[t] = v > 0.0f ? v / repeat_penalty : v * repeat_penalty;
+        }
+    }
+    if (temperature <= 0.0f) {  /* :31-41 greedy: the first index of the maximum */
+        int best = 0;
+        for (int i = 1; i < vocab; ++i)
+            if (logits[i] > logits[best])
+                best = i;
+        return best;
+    }
+    for (int i = 0; i < vocab; ++i)  /* :43-46 */
+        logits[i] /= temperature;
+    const int k = top_k <= 0 ? vocab : (top_k < vocab ? top_k : vocab);  /* :48-55 */
+    int* order = (int*)malloc(sizeof(int) * (size_t)vocab);
+    double* w = (double*)malloc(sizeof(double) * (size_t)k);
+    for (int i = 0; i < vocab; ++i)
+        order[i] = i;
+    g_sort_logits = logits;
+    qsort(order, (size_t)vocab, sizeof(int), by_logit_desc);
+    const float max_logit = logits[order[0]];  /* :57-64 */
+    double total = 0.0;
+    for (int i = 0; i < k; ++i) {
+        w[i] = exp((double)(logits[order[i]] - max_logit));
+        total += w[i];
+    }
+    int kept = k;  /* :66-77 nucleus */
+    double cumulative = 0.0;
+    for (int i = 0; i < k; ++i) {
+        cumulative += w[i] / total;
+        if (cumulative >= (double)top_p) {
+            kept = i + 1;
+            break;
+        }
+    }
+    double kept_total = 0.0;
+    for (int i = 0; i < kept; ++i)
+        kept_total += w[i];
+    const double target = oracle_mt64_canonical(rng) * kept_total;  /* :83-95 */
+    double acc = 0.0;
+    int token = order[kept - 1];
+    for (int i = 0; i < kept; ++i) {
+        acc += w[i];
+        if (acc >= target) {
+            token = order[i];
+            break;
+        }
+    }
+    free(order);
+    free(w);
+    return token;
+}
+
+size_t oracle_mt64_bytes(void) { return sizeof(OracleMt64); }

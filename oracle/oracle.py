@@ -51,6 +51,13 @@ def lib() -> C.CDLL:
         L.oracle_qwen2_step.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
                                         _f32p, C.c_void_p]
         L.oracle_qwen2_step.restype = C.c_int
+        L.oracle_mt64_seed.argtypes = [C.c_void_p, C.c_uint64]
+        L.oracle_mt64_next.argtypes = [C.c_void_p]
+        L.oracle_mt64_next.restype = C.c_uint64
+        L.oracle_mt64_bytes.restype = C.c_size_t
+        L.oracle_sample.argtypes = [_f32p, C.c_int, C.c_float, C.c_int, C.c_float, C.c_float, C.c_int,
+                                    C.c_void_p, C.c_int, C.c_void_p]
+        L.oracle_sample.restype = C.c_int
         L.oracle_set_num_threads.argtypes = [C.c_int]
         L.oracle_num_threads.restype = C.c_int
         _lib = L
@@ -236,3 +243,55 @@ def qwen2_greedy(cfg, tensors, forced: list[int], n_total: int, kv_f16: bool = F
         if step + 1 >= len(seq):
             seq.append(arg)
     return seq, margins
+
+
+class Sampler:
+    """Restatement of the reference's Sampler (src/Sampler.cpp, oracle.c's oracle_sample) with its own
+    mt19937_64 state. sample() modifies `logits` in place, as the reference does."""
+
+    def __init__(self, temperature=0.0, top_k=40, top_p=0.95, repeat_penalty=1.0, repeat_last_n=64, seed=0):
+        self.params = (float(temperature), int(top_k), float(top_p), float(repeat_penalty), int(repeat_last_n))
+        self.state = C.create_string_buffer(int(lib().oracle_mt64_bytes()))
+        lib().oracle_mt64_seed(self.state, int(seed))
+
+    def sample(self, logits: np.ndarray, history) -> int:
+        assert logits.dtype == np.float32 and logits.flags["C_CONTIGUOUS"]
+        h = np.ascontiguousarray(history, dtype=np.int32)
+        t, k, p, rp, n = self.params
+        return int(lib().oracle_sample(logits, logits.size, t, k, p, rp, n, h.ctypes.data if h.size else None,
+                                       h.size, self.state))
+
+
+REF_SAMPLER = os.path.join(HERE, "_ref", "libsampler_ref.so")
+
+
+def build_ref() -> str | None:
+    """Compile the reference's own sampler into oracle/_ref (needs the reference tree); None if absent."""
+    if not os.path.exists(os.path.join("/root/reference", "src", "Sampler.cpp")):
+        return REF_SAMPLER if os.path.exists(REF_SAMPLER) else None
+    subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
+    return REF_SAMPLER
+
+
+class RefSampler:
+    """The reference's Sampler itself (oracle/_ref/libsampler_ref.so, built from src/Sampler.cpp)."""
+
+    def __init__(self, temperature=0.0, top_k=40, top_p=0.95, repeat_penalty=1.0, repeat_last_n=64, seed=0):
+        L = C.CDLL(REF_SAMPLER)
+        L.ref_sampler_create.argtypes = [C.c_float, C.c_int, C.c_float, C.c_float, C.c_int, C.c_ulonglong]
+        L.ref_sampler_create.restype = C.c_void_p
+        L.ref_sampler_sample.argtypes = [C.c_void_p, _f32p, C.c_int, C.c_void_p, C.c_int]
+        L.ref_sampler_sample.restype = C.c_int
+        L.ref_sampler_destroy.argtypes = [C.c_void_p]
+        self.L = L
+        self.h = L.ref_sampler_create(temperature, top_k, top_p, repeat_penalty, repeat_last_n, seed)
+
+    def sample(self, logits: np.ndarray, history) -> int:
+        h = np.ascontiguousarray(history, dtype=np.int32)
+        return int(self.L.ref_sampler_sample(self.h, logits, logits.size, h.ctypes.data if h.size else None, h.size))
+
+    def __del__(self):
+        try:
+            self.L.ref_sampler_destroy(self.h)
+        except Exception:
+            pass

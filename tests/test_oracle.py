@@ -220,3 +220,48 @@ def test_qwen2_05b_first_steps_match_reference(oracle_mod):
         top = doc["reference_top5_first_steps"][str(step)]
         for tid, val in top:
             assert abs(float(logits[tid]) - val) <= 1e-4 + 1e-3 * abs(val), (step, tid, logits[tid], val)
+
+
+SAMPLER_CASES = [
+    dict(temperature=0.8, top_k=40, top_p=0.95, repeat_penalty=1.1, repeat_last_n=64, seed=7),
+    dict(temperature=1.0, top_k=0, top_p=0.9, repeat_penalty=1.0, repeat_last_n=64, seed=123),
+    dict(temperature=0.5, top_k=1, top_p=0.95, repeat_penalty=1.3, repeat_last_n=-1, seed=5),
+    dict(temperature=1.2, top_k=200, top_p=1.0, repeat_penalty=0.9, repeat_last_n=8, seed=2**63 + 11),
+    dict(temperature=0.0, top_k=40, top_p=0.95, repeat_penalty=1.2, repeat_last_n=16, seed=1),
+]
+
+
+@pytest.mark.parametrize("case", range(len(SAMPLER_CASES)))
+def test_sampler_restatement_matches_the_reference_sampler(oracle_mod, case):
+    """oracle_sample (with its own mt19937_64) against the reference's Sampler compiled unmodified
+    from src/Sampler.cpp (oracle/_ref): 40 consecutive draws, identical tokens and identical
+    penalised / scaled logits. Logits are continuous random values (no exact ties, whose order
+    std::partial_sort leaves unspecified); the history repeats tokens, so penalties compound."""
+    if oracle_mod.build_ref() is None:
+        pytest.skip("the reference sampler (oracle/_ref) is not built here")
+    kw = SAMPLER_CASES[case]
+    ours, ref = oracle_mod.Sampler(**kw), oracle_mod.RefSampler(**kw)
+    rng = np.random.default_rng(1000 + case)
+    vocab = 151936
+    history = list(rng.integers(0, vocab, 20))
+    history += history[:5]
+    for step in range(40):
+        logits = (rng.standard_normal(vocab) * 3).astype(np.float32)
+        la, lb = logits.copy(), logits.copy()
+        ta, tb = ours.sample(la, history), ref.sample(lb, history)
+        assert ta == tb, (case, step, ta, tb)
+        assert np.array_equal(la, lb)
+        history.append(ta)
+
+
+def test_mt19937_64_known_answer(oracle_mod):
+    """std::mt19937_64's standard check value: the 10000th output of a default-seeded (5489)
+    engine is 9981545732273789042 (C++11 [rand.predef])."""
+    import ctypes as C
+
+    L = oracle_mod.lib()
+    st = C.create_string_buffer(int(L.oracle_mt64_bytes()))
+    L.oracle_mt64_seed(st, 5489)
+    for _ in range(9999):
+        L.oracle_mt64_next(st)
+    assert L.oracle_mt64_next(st) == 9981545732273789042
