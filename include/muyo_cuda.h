@@ -364,6 +364,19 @@ int muyo_sampler_seed(void* state, uint64_t seed, void* stream);
 int muyo_cuda_sample(const MuyoSamplerParams* p, float* logits, uint32_t vocab, const int32_t* history,
                      uint32_t hist_len, void* state, int32_t* token, void* stream);
 
+/* Non-greedy decoding inside the model's step graph (RunFullModel's Sampler, src/FullModel.cpp:1058,
+ * 1111-1116). Seeds a device engine with p->seed (synchronously on `stream`) and re-records the step
+ * graph with a sampler node after the LM head. muyo_model_generate then samples every generated id
+ * on the device: one draw per generated token, with every id in the cache (earlier turns, the prompt,
+ * the ids generated so far) as the penalty history, and the engine's stream continuing across calls
+ * as the reference's one Sampler does across turns. The logits buffer holds the penalised,
+ * temperature-scaled logits afterwards, as the reference's mapped logits do. muyo_model_step is not
+ * affected (it returns the logits and the greedy id; sample them with muyo_cuda_sample).
+ * p == NULL, or temperature <= 0 with repeat_penalty == 1 (the reference's default), restores the
+ * LM head's greedy pick. Needs the graph engine ("engine" 1); the persistent engine returns
+ * MUYO_EUNSUPPORTED while a sampler is set. Limits as muyo_cuda_sample. */
+int muyo_model_set_sampler(MuyoModel* m, const MuyoSamplerParams* p, void* stream);
+
 /* ---- row-sharded GEMV fused with its all-gather over NVLink peer memory ---------------------------
  * No counterpart in the reference, which runs on one GPU: the multi-GPU form of its LM head +
  * greedy pick (src/FullModel.cpp:973-998, src/Sampler.cpp:32-43). `world` processes, one per GPU

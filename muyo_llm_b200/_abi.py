@@ -133,6 +133,7 @@ SIGNATURES = {
     "muyo_sampler_state_bytes": (C.c_size_t, []),
     "muyo_sampler_seed": (C.c_int, [VP, C.c_uint64, VP]),
     "muyo_cuda_sample": (C.c_int, [P(SamplerParams), VP, U32, VP, U32, VP, VP, VP]),
+    "muyo_model_set_sampler": (C.c_int, [VP, P(SamplerParams), VP]),
     "muyo_p2p_handle_bytes": (C.c_size_t, []),
     "muyo_p2p_create": (C.c_int, [C.c_int, C.c_int, U32, P(VP), VP]),
     "muyo_p2p_connect": (C.c_int, [VP, VP]),

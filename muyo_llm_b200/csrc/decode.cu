@@ -11,6 +11,7 @@
 #include <algorithm>
 #include <climits>
 #include <cmath>
+#include <cstddef>
 #include <cstring>
 #include <map>
 #include <new>
@@ -19,6 +20,13 @@
 
 #include "attention.cuh"
 #include "common.cuh"
+
+// sampler.cu: parameter check and launch of the device sampler (gate = the model's {step,
+// prompt_end, total}, see k_sample).
+int sample_check(const MuyoSamplerParams* p, uint32_t vocab);
+int sample_launch(const MuyoSamplerParams* p, float* logits, uint32_t vocab, const int32_t* history,
+                  uint32_t hist_len, void* state, int32_t* token, const int32_t* gate, int32_t* tokens,
+                  int max_seq, bool pdl, cudaStream_t s);
 #include "gemv.cuh"
 
 namespace muyo {
@@ -35,6 +43,7 @@ struct Control {
     int32_t total;       // tokens[] is written for positions < total
     int32_t greedy;      // the last step's raw argmax
 };
+static_assert(offsetof(Control, prompt_end) == 4 && offsetof(Control, total) == 8, "sampler gate layout");
 }  // namespace muyo
 
 #include "decode_persistent.cuh"
@@ -845,6 +854,9 @@ struct MuyoModel {
     bool pdl = true;                // graph engine: kernels launch early and prefetch their weights
     bool prefetch_ahead = true;     // graph engine: each GEMV streams a later kernel's weights into L2
     bool sw = true;                 // graph engine: per-layer GEMVs bulk-copy their weight tile to shared memory
+    bool sampling = false;          // graph engine: a device sampler node follows the LM head
+    MuyoSamplerParams sp{};         // its parameters (baked into the recorded graph)
+    void* rng = nullptr;            // its mt19937_64 state, followed by the last sampled id (int32)
     double* rope_cs = nullptr;      // [max_seq][head_dim] cos/sin table (float64)
     muyo::PLayer* d_layers = nullptr;
     unsigned* bar = nullptr;        // persistent kernel grid-barrier counter
@@ -878,7 +890,12 @@ static LayerPtrs layer_ptrs(const MuyoModel* m, int l)
     return w;
 }
 
-// Records one whole decode step on stream st (5 kernels per layer + the LM head).
+static int32_t* sampled_id(MuyoModel* m)
+{
+    return reinterpret_cast<int32_t*>(static_cast<char*>(m->rng) + (muyo_sampler_state_bytes() + 15) / 16 * 16);
+}
+
+// Records one whole decode step on stream st (5 kernels per layer + the LM head, + the sampler).
 static int record_step(MuyoModel* m, cudaStream_t st)
 {
     const Shape& s = m->s;
@@ -934,7 +951,13 @@ static int record_step(MuyoModel* m, cudaStream_t st)
     a.tokens_rw = m->tokens;
     a.max_seq = s.max_seq;
     a.pf = plan[n_mats - 1];
-    return launch_gemv<2, 4, 1, 1, PRO_NORM, EPI_LOGITS>(a, m->lm_grid, st, m->pdl);
+    rc = launch_gemv<2, 4, 1, 1, PRO_NORM, EPI_LOGITS>(a, m->lm_grid, st, m->pdl);
+    if (rc || !m->sampling)
+        return rc;
+    // Non-greedy decoding: the sampler replaces the LM head's pick at generated positions
+    // (Sampler::Sample on the logits with every cached id as history, src/FullModel.cpp:1111-1116).
+    return sample_launch(&m->sp, m->logits, (uint32_t)s.vocab, nullptr, 0, m->rng, sampled_id(m), &m->ctrl->step,
+                         m->tokens, s.max_seq, false, st);
 }
 
 // ---- persistent engine ----------------------------------------------------------------------------
@@ -1248,6 +1271,7 @@ static void free_model(MuyoModel* m)
     cudaFree(m->kc);
     cudaFree(m->vc);
     cudaFree(m->scratch);
+    cudaFree(m->rng);
     if (m->pinned)
         cudaFreeHost(m->pinned);
     delete m;
@@ -1410,6 +1434,32 @@ extern "C" int muyo_model_set_tensor(MuyoModel* m, const char* name, const void*
     return MUYO_OK;
 }
 
+// (Re)records the decode-step graph.
+static int record_graph(MuyoModel* m)
+{
+    if (m->exec) {
+        cudaGraphExecDestroy(m->exec);
+        m->exec = nullptr;
+    }
+    if (m->graph) {
+        cudaGraphDestroy(m->graph);
+        m->graph = nullptr;
+    }
+    MUYO_CUDA_TRY(cudaStreamBeginCapture(m->cap_stream, cudaStreamCaptureModeThreadLocal));
+    int rc = record_step(m, m->cap_stream);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(m->cap_stream, &g);
+    if (rc != MUYO_OK) {
+        if (g)
+            cudaGraphDestroy(g);
+        return rc;
+    }
+    MUYO_CUDA_TRY(e);
+    m->graph = g;
+    MUYO_CUDA_TRY(cudaGraphInstantiate(&m->exec, g, 0));
+    return MUYO_OK;
+}
+
 extern "C" int muyo_model_finalize(MuyoModel* m, void* stream)
 {
     clear_error();
@@ -1456,26 +1506,9 @@ extern "C" int muyo_model_finalize(MuyoModel* m, void* stream)
             return rc;
         m->p_grid = 0;
     }
-    if (m->exec) {
-        cudaGraphExecDestroy(m->exec);
-        m->exec = nullptr;
-    }
-    if (m->graph) {
-        cudaGraphDestroy(m->graph);
-        m->graph = nullptr;
-    }
-    MUYO_CUDA_TRY(cudaStreamBeginCapture(m->cap_stream, cudaStreamCaptureModeThreadLocal));
-    int rc = record_step(m, m->cap_stream);
-    cudaGraph_t g = nullptr;
-    cudaError_t e = cudaStreamEndCapture(m->cap_stream, &g);
-    if (rc != MUYO_OK) {
-        if (g)
-            cudaGraphDestroy(g);
+    const int rc = record_graph(m);
+    if (rc)
         return rc;
-    }
-    MUYO_CUDA_TRY(e);
-    m->graph = g;
-    MUYO_CUDA_TRY(cudaGraphInstantiate(&m->exec, g, 0));
     m->finalized = true;
     return MUYO_OK;
 }
@@ -1498,6 +1531,10 @@ extern "C" int muyo_model_reset(MuyoModel* m, void* stream)
 // forced up to `prompt_end`, and replays the step graph n_steps times.
 static int run_steps(MuyoModel* m, int prompt_end, int total, int n_steps, cudaStream_t st)
 {
+    if (m->engine == 0 && m->sampling) {
+        set_error("decode: the device sampler runs in the graph engine (engine 1), not the persistent kernel");
+        return MUYO_EUNSUPPORTED;
+    }
     k_set_control<<<1, 1, 0, st>>>(m->ctrl, Control{m->host_pos, prompt_end, total, 0});
     MUYO_LAUNCH_CHECK();
     if (m->engine == 0) {
@@ -1661,6 +1698,31 @@ extern "C" int muyo_model_destroy(MuyoModel* m)
         free_model(m);
     }
     return MUYO_OK;
+}
+
+extern "C" int muyo_model_set_sampler(MuyoModel* m, const MuyoSamplerParams* p, void* stream)
+{
+    clear_error();
+    MUYO_REQUIRE(m, "set_sampler: null model");
+    MUYO_CUDA_TRY(cudaSetDevice(m->device));
+    // temperature <= 0 with no penalty is the reference's plain greedy pick, which the LM head makes.
+    const bool on = p && (p->temperature > 0.0f || p->repeat_penalty != 1.0f);
+    if (on) {
+        int rc = sample_check(p, (uint32_t)m->s.vocab);
+        if (rc)
+            return rc;
+        if (!m->rng)
+            MUYO_CUDA_TRY(cudaMalloc(&m->rng, (muyo_sampler_state_bytes() + 15) / 16 * 16 + 16));
+        const cudaStream_t st = as_stream(stream);
+        rc = muyo_sampler_seed(m->rng, p->seed, st);
+        if (rc)
+            return rc;
+        MUYO_CUDA_TRY(cudaStreamSynchronize(st));
+        m->sp = *p;
+    }
+    const bool rerecord = m->finalized && (on || m->sampling);
+    m->sampling = on;
+    return rerecord ? record_graph(m) : MUYO_OK;
 }
 
 extern "C" int muyo_model_set_option(MuyoModel* m, const char* key, int value)

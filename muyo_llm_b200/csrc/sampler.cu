@@ -109,10 +109,15 @@ struct SampleArgs {
     float* logits;
     const int32_t* history;
     int hist_len;
-    const int32_t* hist_len_dev;  // when set: the history length is *hist_len_dev + hist_len
     Mt64State* rng;
     int32_t* token;
-    int32_t* token2;  // optional second destination: token2[*hist_len_dev + 1] (the model's next position)
+    // Decode-graph mode (gate != nullptr): gate = {step, prompt_end, total} of the model's control
+    // block, read after the LM head advanced step to n. The sampler runs only for a generated
+    // position (prompt_end <= n < total, n < max_seq), with history = tokens[0, n) (every id in the
+    // cache) and the id also stored at tokens[n]; otherwise it returns without drawing.
+    const int32_t* gate;
+    int32_t* tokens;
+    int max_seq;
 };
 
 __global__ void __launch_bounds__(kSampleThreads) k_sample(SampleArgs a)
@@ -131,7 +136,16 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample(SampleArgs a)
     pdl_trigger();
     const int tid = threadIdx.x, V = a.vocab;
     float* lg = a.logits;
-    const int hist_len = a.hist_len + (a.hist_len_dev ? *a.hist_len_dev : 0);
+    int hist_len = a.hist_len;
+    const int32_t* history = a.history;
+    int n = 0;
+    if (a.gate) {  // uniform over the block: every thread reads the same words
+        n = __ldcg(a.gate);
+        if (n < __ldcg(a.gate + 1) || n >= __ldcg(a.gate + 2) || n >= a.max_seq)
+            return;
+        hist_len = n;
+        history = a.tokens;
+    }
 
     // 1. repetition penalty, in history order
     if (tid == 0 && a.repeat_penalty != 1.0f && hist_len > 0) {
@@ -139,7 +153,7 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample(SampleArgs a)
         if (a.repeat_last_n >= 0 && a.repeat_last_n < hist_len)
             begin = hist_len - a.repeat_last_n;
         for (int i = begin; i < hist_len; ++i) {
-            const int t = a.history[i];
+            const int t = history[i];
             if (t < 0 || t >= V)
                 continue;
             const float v = lg[t];
@@ -296,8 +310,8 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample(SampleArgs a)
     }
     if (tid == 0) {
         *a.token = sh_token;
-        if (a.token2 && a.hist_len_dev)
-            a.token2[*a.hist_len_dev + 1] = sh_token;
+        if (a.gate)
+            a.tokens[n] = sh_token;
     }
 }
 
@@ -316,14 +330,11 @@ extern "C" int muyo_sampler_seed(void* state, uint64_t seed, void* stream)
     return MUYO_OK;
 }
 
-int sample_launch(const MuyoSamplerParams* p, float* logits, uint32_t vocab, const int32_t* history,
-                  uint32_t hist_len, const int32_t* hist_len_dev, void* state, int32_t* token, int32_t* token2,
-                  cudaStream_t s)
+// Checks a parameter block against what the device sampler supports (MUYO_OK or an error code).
+int sample_check(const MuyoSamplerParams* p, uint32_t vocab)
 {
-    MUYO_REQUIRE(p && logits && state && token, "sample: null parameter block or buffer");
+    MUYO_REQUIRE(p, "sample: null parameter block");
     MUYO_REQUIRE(vocab > 0 && vocab <= (uint32_t)INT_MAX, "sample: vocab must be positive");
-    MUYO_REQUIRE((reinterpret_cast<uintptr_t>(state) & 7u) == 0, "sample: state must be 8-byte aligned");
-    MUYO_REQUIRE(hist_len == 0 || history || hist_len_dev, "sample: history is null");
     MUYO_REQUIRE(!(p->temperature > 0.0f) || p->repeat_penalty == p->repeat_penalty, "sample: repeat_penalty is NaN");
     if (p->temperature > 0.0f) {
         const uint32_t k = p->top_k <= 0 ? vocab : ((uint32_t)p->top_k < vocab ? (uint32_t)p->top_k : vocab);
@@ -332,14 +343,31 @@ int sample_launch(const MuyoSamplerParams* p, float* logits, uint32_t vocab, con
             return MUYO_EUNSUPPORTED;
         }
     }
+    return MUYO_OK;
+}
+
+// gate/tokens/max_seq: the decode-graph mode of k_sample (gate == nullptr for a plain call).
+// pdl = false in the decode graph: launched early, the 1024-thread CTA would hold an SM slot that
+// the LM head's single-wave grid counts on.
+int sample_launch(const MuyoSamplerParams* p, float* logits, uint32_t vocab, const int32_t* history,
+                  uint32_t hist_len, void* state, int32_t* token, const int32_t* gate, int32_t* tokens,
+                  int max_seq, bool pdl, cudaStream_t s)
+{
+    MUYO_REQUIRE(p && logits && state && token, "sample: null parameter block or buffer");
+    MUYO_REQUIRE((reinterpret_cast<uintptr_t>(state) & 7u) == 0, "sample: state must be 8-byte aligned");
+    MUYO_REQUIRE(hist_len == 0 || history, "sample: history is null");
+    MUYO_REQUIRE(!gate || tokens, "sample: gated call without a token buffer");
+    const int rc = sample_check(p, vocab);
+    if (rc)
+        return rc;
     SampleArgs a{};
     a.temperature = p->temperature, a.top_k = p->top_k, a.top_p = p->top_p, a.repeat_penalty = p->repeat_penalty;
     a.repeat_last_n = p->repeat_last_n, a.vocab = (int)vocab, a.logits = logits, a.history = history;
-    a.hist_len = (int)hist_len, a.hist_len_dev = hist_len_dev, a.rng = static_cast<Mt64State*>(state);
-    a.token = token, a.token2 = token2;
+    a.hist_len = (int)hist_len, a.rng = static_cast<Mt64State*>(state), a.token = token;
+    a.gate = gate, a.tokens = tokens, a.max_seq = max_seq;
     const size_t smem = 16 * (size_t)kSampleMaxK;  // keys + indices + weights
     MUYO_CUDA_TRY(cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    MUYO_CUDA_TRY(launch_kernel(k_sample, dim3(1), dim3(kSampleThreads), smem, s, true, a));
+    MUYO_CUDA_TRY(launch_kernel(k_sample, dim3(1), dim3(kSampleThreads), smem, s, pdl, a));
     MUYO_LAUNCH_CHECK();
     return MUYO_OK;
 }
@@ -348,5 +376,6 @@ extern "C" int muyo_cuda_sample(const MuyoSamplerParams* p, float* logits, uint3
                                 uint32_t hist_len, void* state, int32_t* token, void* stream)
 {
     clear_error();
-    return sample_launch(p, logits, vocab, history, hist_len, nullptr, state, token, nullptr, as_stream(stream));
+    return sample_launch(p, logits, vocab, history, hist_len, state, token, nullptr, nullptr, 0, true,
+                         as_stream(stream));
 }

@@ -72,8 +72,16 @@ class Qwen2Model:
         _abi.call("muyo_model_position", self._m, C.byref(p))
         return p.value
 
+    def set_sampler(self, temperature: float = 0.0, top_k: int = 40, top_p: float = 0.95,
+                    repeat_penalty: float = 1.0, repeat_last_n: int = 64, seed: int = 0, stream=None) -> None:
+        """Sample generated ids on the device (SamplerParams, src/Sampler.h:14-22; same defaults).
+        The defaults (temperature 0, no penalty) are the greedy pick. Re-seeds the engine."""
+        p = _abi.SamplerParams(temperature, top_k, top_p, repeat_penalty, repeat_last_n, 0, seed)
+        _abi.call("muyo_model_set_sampler", self._m, C.byref(p), stream)
+
     def generate(self, prompt, n_predict: int, stream=None) -> np.ndarray:
-        """Feed ``prompt`` (host ids) and return ``n_predict`` greedy ids (host). Blocking."""
+        """Feed ``prompt`` (host ids) and return ``n_predict`` generated ids (host): greedy, or drawn by
+        the sampler that set_sampler installed. Blocking."""
         p = np.ascontiguousarray(prompt, dtype=np.int32)
         out = np.empty(max(n_predict, 1), np.int32)
         _abi.call("muyo_model_generate", self._m, p.ctypes.data, p.size, n_predict, out.ctypes.data, stream)
