@@ -356,7 +356,7 @@ typedef struct MuyoSamplerParams {
     float top_p;
     float repeat_penalty;
     int32_t repeat_last_n;
-    uint32_t reserved;
+    uint32_t cluster_ctas; /* 0: automatic (16 CTAs where the device places them, else 8); 8 or 16 to force */
     uint64_t seed; /* used by muyo_model_set_sampler */
 } MuyoSamplerParams;
 size_t muyo_sampler_state_bytes(void);

@@ -82,7 +82,7 @@ class Qwen2Config(C.Structure):
 
 class SamplerParams(C.Structure):
     _fields_ = [("temperature", F32), ("top_k", C.c_int32), ("top_p", F32), ("repeat_penalty", F32),
-                ("repeat_last_n", C.c_int32), ("reserved", U32), ("seed", C.c_uint64)]
+                ("repeat_last_n", C.c_int32), ("cluster_ctas", U32), ("seed", C.c_uint64)]
 
 
 class LayerWeights(C.Structure):

@@ -23,7 +23,7 @@
 
 // sampler.cu: parameter check and launch of the device sampler (gate = the model's {step,
 // prompt_end, total}, see k_sample).
-int sample_check(const MuyoSamplerParams* p, uint32_t vocab);
+int sample_check(const MuyoSamplerParams* p, uint32_t vocab, long long max_hist);
 int sample_launch(const MuyoSamplerParams* p, float* logits, uint32_t vocab, const int32_t* history,
                   uint32_t hist_len, void* state, int32_t* token, const int32_t* gate, int32_t* tokens,
                   int max_seq, bool pdl, cudaStream_t s);
@@ -1708,7 +1708,7 @@ extern "C" int muyo_model_set_sampler(MuyoModel* m, const MuyoSamplerParams* p, 
     // temperature <= 0 with no penalty is the reference's plain greedy pick, which the LM head makes.
     const bool on = p && (p->temperature > 0.0f || p->repeat_penalty != 1.0f);
     if (on) {
-        int rc = sample_check(p, (uint32_t)m->s.vocab);
+        int rc = sample_check(p, (uint32_t)m->s.vocab, m->s.max_seq);
         if (rc)
             return rc;
         if (!m->rng)

@@ -1,5 +1,6 @@
 // RunFullModel (src/FullModel.cpp:487-1291) on the B200 decode engine: the GGUF's weights go to the
-// device once, the prompt ids are fed one position at a time and the greedy ids come back in one
+// device once, the prompt ids are fed one position at a time and the generated ids (greedy, or drawn
+// by the device sampler with --temp / --top-k / --top-p / --repeat-penalty / --seed) come back in one
 // call (muyo_model_generate). The cache is F32, as the reference's (src/FullModel.cpp:622-625).
 #include <cstdio>
 #include <string>
@@ -33,10 +34,6 @@ int RunFullModel(const std::string& ggufPath, const ForwardOptions& options)
                              "build does not include\n");
         return 2;
     }
-    if (options.sampler.temperature > 0.0F) {
-        std::fprintf(stderr, "[forward] only greedy decoding (--temp 0) runs on the device in this build\n");
-        return 2;
-    }
     if (options.tokens.size() + options.nPredict > K_MAX_SEQ) {
         std::fprintf(stderr, "[forward] %zu prompt + %u generated positions exceed the %u-position cache\n",
                      options.tokens.size(), options.nPredict, K_MAX_SEQ);
@@ -52,12 +49,17 @@ int RunFullModel(const std::string& ggufPath, const ForwardOptions& options)
     MuyoModel* m = nullptr;
     if (muyo_model_create(&cfg, 0, &m) != MUYO_OK)
         return Fail("create");
+    // One Sampler per run (src/FullModel.cpp:1058): the device engine draws once per generated id.
+    const SamplerParams& o = options.sampler;
+    const MuyoSamplerParams sp{o.temperature, o.topK, o.topP, o.repeatPenalty, o.repeatLastN, 0, o.seed};
     int rc = 0;
     std::vector<int32_t> out(options.nPredict > 0 ? options.nPredict : 1);
     if (muyo_model_load_gguf(m, ggufPath.c_str()) != MUYO_OK)
         rc = Fail("load");
     else if (muyo_model_finalize(m, nullptr) != MUYO_OK)
         rc = Fail("finalize");
+    else if (muyo_model_set_sampler(m, &sp, nullptr) != MUYO_OK)
+        rc = Fail("sampler");
     else if (muyo_model_generate(m, options.tokens.data(), (int)options.tokens.size(), (int)options.nPredict,
                                  out.data(), nullptr) != MUYO_OK)
         rc = Fail("generate");

@@ -13,8 +13,8 @@
 
 namespace muyo_llm
 {
-/// Sampling controls of src/Sampler.h:14-22. Only greedy decoding (temperature 0) runs on the
-/// device here; RunFullModel rejects the others.
+/// Sampling controls of src/Sampler.h:14-22, passed to the device sampler (MuyoSamplerParams).
+/// The whole-vocabulary top-k (topK <= 0 with temperature > 0) is limited to 4096 candidates.
 struct SamplerParams
 {
     float temperature = 0.0F;

@@ -31,7 +31,8 @@ void Usage(const char* argv0)
 {
     std::fprintf(stderr,
                  "usage: %s --add | --matvec | --rmsnorm | --rope | --swiglu | --getrows | --argmax | --softmax |\n"
-                 "       --attention | --kvcache | --layer | --forward <gguf> --tokens id,id [-n N] [--temp 0]\n",
+                 "       --attention | --kvcache | --layer | --forward <gguf> --tokens id,id [-n N] [--temp T] [--top-k K]\n"
+                 "       [--top-p P] [--repeat-penalty R] [--repeat-last-n N] [--seed S]\n",
                  argv0);
 }
 }  // namespace

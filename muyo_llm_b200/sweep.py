@@ -123,6 +123,90 @@ def ops(iters: int = 0, peak_gbs: float = 6462.1, seed: int = 7):
     return out
 
 
+SAMPLER_CASES = [  # (label, SamplerParams fields): the reference's flags (src/main.cpp:372-394)
+    ("T0.8 top-k 40 top-p 0.95 penalty 1.1", dict(temperature=0.8, top_k=40, top_p=0.95, repeat_penalty=1.1)),
+    ("greedy + penalty 1.1", dict(temperature=0.0, top_k=40, top_p=0.95, repeat_penalty=1.1)),
+    ("T0.8 top-k 4096 top-p 0.95", dict(temperature=0.8, top_k=4096, top_p=0.95, repeat_penalty=1.0)),
+]
+
+
+def sampler(iters: int = 0, peak_gbs: float = 6462.1, seed: int = 7, n_prompt: int = 32, n_predict: int = 256):
+    """muyo_cuda_sample on a 151936-entry logits row (N(0, 3^2), 64 history ids), device time per call:
+    a CUDA graph of `iters` (restore copy of the row, sample) pairs, minus a graph of the copies
+    alone. Then whole decode steps with the sampler in the step graph (config 4: Qwen2.5-0.5B
+    architecture, F16 KV, 32 prompt + 256 generated ids) against the greedy graph."""
+    import ctypes as C
+
+    from . import _abi, engine, synth
+
+    V, n = 151936, iters or 200
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    base = torch.randn(V, generator=g, device="cuda") * 3
+    lg = base.clone()
+    hist = torch.randint(0, V, (64,), generator=g, device="cuda", dtype=torch.int32)
+    state = torch.zeros(int(_abi.lib().muyo_sampler_state_bytes()), dtype=torch.uint8, device="cuda")
+    tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.Stream()
+
+    def graph_ms(body):
+        with torch.cuda.stream(stream):
+            body()  # first call outside the capture (attribute and placement checks)
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream, capture_error_mode="thread_local"):
+            for _ in range(n):
+                body()
+        for _ in range(3):
+            gr.replay()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        gr.replay()
+        e.record()
+        torch.cuda.synchronize()
+        return s.elapsed_time(e) / n
+
+    copy_ms = graph_ms(lambda: lg.copy_(base))
+    out = []
+    runs = [(label, kw, 0) for label, kw in SAMPLER_CASES]
+    runs += [(SAMPLER_CASES[0][0], SAMPLER_CASES[0][1], c) for c in (8, 16)]  # forced cluster sizes
+    for label, kw, cluster in runs:
+        _abi.call("muyo_sampler_seed", C.c_void_p(state.data_ptr()), seed, None)
+        p = _abi.SamplerParams(kw["temperature"], kw["top_k"], kw["top_p"], kw["repeat_penalty"], 64, cluster, seed)
+
+        def body():
+            lg.copy_(base)
+            _abi.call("muyo_cuda_sample", C.byref(p), C.c_void_p(lg.data_ptr()), V, C.c_void_p(hist.data_ptr()), 64,
+                      C.c_void_p(state.data_ptr()), C.c_void_p(tok.data_ptr()), C.c_void_p(stream.cuda_stream))
+
+        ms = graph_ms(body) - copy_ms
+        alg = V * 4 * (2 if kw["temperature"] > 0 else 1) + 64 * 4  # logits read (+ written back), history
+        out.append(_result("k_sample", f"{V} ({label})", alg, ms, peak_gbs, mode="latency (L2-resident row)",
+                           restore_copy_us=copy_ms * 1e3, cluster_ctas=cluster or "auto"))
+    cfg = synth.QWEN2_05B
+    m = engine.Qwen2Model(cfg, synth.make_model(cfg, seed), kv_dtype=_abi.KV_F16,
+                          engine=engine.Qwen2Model.ENGINE_GRAPH)
+    prompt = [int(i) for i in synth.prompt_ids(seed, n_prompt, cfg.vocab)]
+    for label, kw in [("greedy", None)] + SAMPLER_CASES[:1]:
+        if kw:
+            m.set_sampler(repeat_last_n=64, seed=seed, **kw)
+        best = float("inf")
+        for _ in range(3):
+            m.reset()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            m.generate(prompt, n_predict)
+            e.record()
+            torch.cuda.synchronize()
+            best = min(best, s.elapsed_time(e))
+        steps = n_prompt + n_predict
+        out.append({"kernel": "decode step graph", "shape": f"config 4 ({label})", "us": best * 1e3 / steps,
+                    "tokens_per_s": steps / (best * 1e-3), "mode": f"{n_prompt} prompt + {n_predict} generated ids"})
+    m.close()
+    return out
+
+
 SHARDED_SHAPES = [(151936, 896), (4096, 4096), (14336, 4096), (128256, 4096)]
 
 

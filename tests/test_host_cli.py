@@ -38,8 +38,6 @@ def test_forward_rejects_unsupported_options_before_any_device_work(tmp_path):
     path = str(tmp_path / "missing.gguf")
     r = _run("--forward", path, "-p", "hello")
     assert r.returncode == 2 and "tokenizer" in r.stderr
-    r = _run("--forward", path, "--tokens", "1,2", "--temp", "0.8")
-    assert r.returncode == 2 and "greedy" in r.stderr
     r = _run("--forward", path, "--tokens", "1,2", "--chat")
     assert r.returncode == 2
     r = _run("--forward", path, "--tokens", "1,2", "--bogus")
@@ -67,4 +65,21 @@ def test_forward_on_tiny_gguf(cuda, tmp_path):
     assert got[0] == int(g["argmax"][-1])  # the reference forward's pick after the last prompt id
     m = engine.Qwen2Model(synth.QWEN2_TINY, gguf_path=path, kv_dtype=_abi.KV_F32)
     assert got == list(m.generate(ids, 12))
+    m.close()
+
+
+@pytest.mark.gpu
+def test_forward_sampled_on_tiny_gguf(cuda, tmp_path):
+    """--temp / --top-k / --top-p / --repeat-penalty / --seed (src/main.cpp:372-394) drive the device
+    sampler: the CLI's ids equal the engine's with the same SamplerParams."""
+    path = str(tmp_path / "tiny.gguf")
+    gguf.write_synthetic_qwen2(path, synth.QWEN2_TINY, 4)
+    ids = [3, 1, 4, 1, 5]
+    flags = ["--temp", "0.9", "--top-k", "30", "--top-p", "0.9", "--repeat-penalty", "1.2", "--seed", "42"]
+    r = _run("--forward", path, "--tokens", ",".join(map(str, ids)), "-n", "16", *flags)
+    assert r.returncode == 0, r.stderr
+    got = [int(v) for v in r.stdout.strip().split(",")]
+    m = engine.Qwen2Model(synth.QWEN2_TINY, gguf_path=path, kv_dtype=_abi.KV_F32)
+    m.set_sampler(temperature=0.9, top_k=30, top_p=0.9, repeat_penalty=1.2, seed=42)
+    assert got == list(m.generate(ids, 16))
     m.close()
