@@ -80,40 +80,69 @@ __device__ __forceinline__ void stage_x_split(float* xs, const float* x, int n, 
     }
 }
 
-template <int ROWS, int U>
+template <int ROWS, int U, int KSPLIT>
 __global__ void __launch_bounds__(kThreads) k_mat_vec_f16(MatVecDev p, const __half* __restrict__ A,
                                                           const float* __restrict__ B, float* __restrict__ D,
                                                           const float* __restrict__ f0, const float* __restrict__ f1)
 {
+    // 8 warps = (8 / KSPLIT) row groups of ROWS rows; the KSPLIT warps of a group split the row's
+    // chunks into contiguous ranges, and their sums meet in shared memory in a fixed order.
+    constexpr int RG = kThreads / 32 / KSPLIT;
     extern __shared__ float xs[];
+    __shared__ float ksum[kThreads / 32][ROWS];
     const int b = blockIdx.y;
     const __half* Ab = A + batch_a_index(p, b) * p.batch_stride_a;
     const float* Bb = B + (long long)b * p.batch_stride_b;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    const int block_rows = nw * ROWS, stride_rows = gridDim.x * block_rows;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int rg = warp / KSPLIT, ks = warp % KSPLIT;
+    const int block_rows = RG * ROWS, ntiles = (p.rows + block_rows - 1) / block_rows;
     // The vector path's rows are 16-byte aligned: start streaming this CTA's first row block into L2
     // while x is staged.
-    if (p.k8 > 0 && threadIdx.x == 0 && (int)blockIdx.x * block_rows < p.rows)
+    if (p.k8 > 0 && threadIdx.x == 0 && (int)blockIdx.x < ntiles)
         prefetch_rows_l2(Ab, (size_t)p.stride_a, blockIdx.x * block_rows,
                          min(block_rows, p.rows - (int)blockIdx.x * block_rows));
     pdl_wait();  // the L2 prefetch above is only a hint; every read of A, x or D comes after this wait
     pdl_trigger();
     stage_x_split(xs, Bb, p.ncols, p.k8);
     __syncthreads();
+    const int c_begin = (int)((long long)p.k8 * ks / KSPLIT), c_end = (int)((long long)p.k8 * (ks + 1) / KSPLIT);
     GemvArgs<ROWS, U, 1> ga{{Ab}, (size_t)p.stride_a};
-    for (int row0 = (blockIdx.x * nw + warp) * ROWS; row0 < p.rows; row0 += stride_rows) {
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {  // the same trip count in every warp
+        const int row0 = tile * block_rows + rg * ROWS;
         const int nvalid = min(ROWS, p.rows - row0);
-        const int next0 = row0 - warp * ROWS + stride_rows;  // the CTA's next row block
+        const int next0 = (tile + (int)gridDim.x) * block_rows;  // the CTA's next row block
         if (p.k8 > 0 && warp == 0 && lane == 0 && next0 < p.rows)
             prefetch_rows_l2(Ab, (size_t)p.stride_a, next0, min(block_rows, p.rows - next0));
         float acc[1][ROWS];
 #pragma unroll
         for (int r = 0; r < ROWS; ++r)
             acc[0][r] = 0.0f;
-        warp_gemv_f16<ROWS, U, 1>(ga, row0, nvalid, xs, p.k8, lane, acc);
-        warp_gemv_f16_tail<ROWS, 1>(ga.w, ga.ldw, row0, nvalid, xs, p.k8, p.ncols, lane, acc);
-        warp_reduce_acc<ROWS, 1>(acc);
-        if (lane == 0) {
+        if (nvalid > 0) {
+            warp_gemv_f16_range<ROWS, U, 1>(ga, row0, nvalid, xs, p.k8, c_begin, c_end, lane, acc);
+            if (ks == KSPLIT - 1)  // columns past the last full chunk
+                warp_gemv_f16_tail<ROWS, 1>(ga.w, ga.ldw, row0, nvalid, xs, p.k8, p.ncols, lane, acc);
+            warp_reduce_acc<ROWS, 1>(acc);
+        }
+        if (KSPLIT > 1) {
+            if (lane == 0) {
+#pragma unroll
+                for (int r = 0; r < ROWS; ++r)
+                    ksum[warp][r] = acc[0][r];
+            }
+            __syncthreads();
+            if (ks == 0) {
+#pragma unroll
+                for (int r = 0; r < ROWS; ++r) {
+                    float t = ksum[warp][r];
+#pragma unroll
+                    for (int j = 1; j < KSPLIT; ++j)
+                        t += ksum[warp + j][r];
+                    acc[0][r] = t;
+                }
+            }
+            __syncthreads();
+        }
+        if (ks == 0 && lane == 0 && nvalid > 0) {
 #pragma unroll
             for (int r = 0; r < ROWS; ++r)
                 if (r < nvalid) {
@@ -255,12 +284,22 @@ static int launch_mat_vec(bool f16, const MatVecDev& q, int batches, const void*
     const size_t smem = (size_t)q.ncols * sizeof(float);
     dim3 grid(gx, batches);
     if (f16) {
+        // Few row blocks per SM (with long rows): 2 or 4 warps per row, so the blocks are smaller and
+        // spread evenly over the SMs, and more loads are in flight at the start and in the tail.
+        const int tiles1 = (q.rows + 8 * ROWS - 1) / (8 * ROWS);
+        const int ksplit = q.k8 < 256 || batches > 1 ? 1 : (tiles1 < 2 * sm_count() ? 4 : (tiles1 < 6 * sm_count() ? 2 : 1));
+        if (ksplit > 1)
+            grid.x = (unsigned)((q.rows + 8 / ksplit * ROWS - 1) / (8 / ksplit * ROWS));
         // Loads in flight per lane grow with K so that a warp covers a long row in few round trips:
         // U chunks of 16 bytes per row per lane (each lane still adds its chunks in column order).
-        const int lane_chunks = q.k8 / 32;
-        auto k = k_mat_vec_f16<ROWS, 4>;
-        if (lane_chunks >= 8)
-            k = k_mat_vec_f16<ROWS, 8>;
+        const int lane_chunks = q.k8 / ksplit / 32;
+        auto k = k_mat_vec_f16<ROWS, 4, 1>;
+        if (ksplit == 4)
+            k = lane_chunks >= 8 ? k_mat_vec_f16<ROWS, 8, 4> : k_mat_vec_f16<ROWS, 4, 4>;
+        else if (ksplit == 2)
+            k = lane_chunks >= 8 ? k_mat_vec_f16<ROWS, 8, 2> : k_mat_vec_f16<ROWS, 4, 2>;
+        else if (lane_chunks >= 8)
+            k = k_mat_vec_f16<ROWS, 8, 1>;
         MUYO_CUDA_TRY(set_smem(k, smem));
         // CTAs stride over the row tiles: the grid stops at what is resident at once
         int per_sm = 0;
