@@ -12,6 +12,7 @@ shard), summed. Timed on the device with CUDA events around K sequences, max ove
   python bench.py --suite gemv [--shapes 14336x4096,...]   # F16 GEMV sweep, one JSON line per shape
   python bench.py --suite ops                              # op latency + multi-row bandwidth sweep
   python bench.py --suite sampler                          # device sampler per call + sampled decode steps
+  python bench.py --suite prefill                          # batched-prefill GEMM, prompt-to-first-token, config 4
   torchrun --nproc-per-node N bench.py --suite gemv_sharded  # row-sharded GEMV + NCCL gathers (C5)
 
 `--impl reference` times the reference's CPU forward on the host cores instead: the C oracle port
@@ -316,6 +317,8 @@ def run_suite(args):
         if args.suite == "gemv":
             shapes = [tuple(int(v) for v in s.split("x")) for s in args.shapes.split(",") if s] or None
             res = sweep.gemv(shapes, args.iters, peak)
+        elif args.suite == "prefill":
+            res = sweep.prefill(args.iters, peak, n_prompt=args.n_prompt, n_predict=args.n_predict)
         elif args.suite == "sampler":
             res = sweep.sampler(args.iters, peak, n_prompt=args.n_prompt, n_predict=args.n_predict)
         else:
@@ -334,7 +337,7 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--engine", default="graph", choices=["persistent", "graph"])
-    ap.add_argument("--suite", default="decode", choices=["decode", "gemv", "ops", "gemv_sharded", "sampler"],
+    ap.add_argument("--suite", default="decode", choices=["decode", "gemv", "ops", "gemv_sharded", "sampler", "prefill"],
                     help="decode: the config-4 headline line (default); gemv / ops: kernel sweeps, one JSON line "
                          "per case (1 GPU)")
     ap.add_argument("--shapes", default="", help="gemv suite: comma-separated ROWSxCOLS list (default: all)")

@@ -305,6 +305,34 @@ int muyo_model_destroy(MuyoModel* m);
  * L2; "smem_weights" = 1 (default) has the per-layer GEMV kernels copy their weight tile into shared
  * memory before waiting for the previous kernel (bounded wait; MUYO_ETIMEOUT if it expires). */
 int muyo_model_set_option(MuyoModel* m, const char* key, int value);
+/* Option "prefill" = 1 (default 0; allocates activations for 128 positions on first use): in
+ * muyo_model_generate(_device), every prompt position but the last goes through the layers in one
+ * batched pass per 128 positions (muyo_cuda_mat_mul_f16's GEMM for the projections, a causal
+ * attention kernel over the cache), writing the same KV cache; the decode step then runs from the
+ * prompt's last position. The reference feeds a prompt one position at a time (src/FullModel.cpp:
+ * 1174-1181): results agree to float rounding, not bit for bit (the projections sum in another
+ * order). No logits are formed for the batched positions. */
+
+/* ---- batched F16 GEMM (the prefill projections) ---------------------------------------------------
+ * y[t][n] = sum_k A[n][k] * x[t][k] for n < rows, t < tokens: ggml's mul_mm with src0 = A (F16,
+ * [rows][ncols] row-major) and src1 = x (F32, tokens rows of stride_x), the batched counterpart of
+ * muyo_cuda_mat_vec_f16 (the reference's shaders/llama/mul_mm.comp, which its engine never
+ * dispatches). BIAS adds bias[n]; ACCUMULATE adds to y. x enters the tensor cores as two F16 halves
+ * (hi = f16(x), lo = f16(x - hi)) with F32 accumulation. ncols a multiple of 8; a, x and the
+ * workspace 16-byte aligned. */
+#define MUYO_MATMUL_BIAS 0x1u
+#define MUYO_MATMUL_ACCUMULATE 0x2u
+typedef struct MuyoMatMulParams {
+    uint32_t ncols;    /* K */
+    uint32_t rows;     /* N: output features */
+    uint32_t tokens;   /* T: rows of x and y */
+    uint32_t stride_x; /* 0 = ncols (a multiple of 4) */
+    uint32_t stride_y; /* 0 = rows */
+    uint32_t flags;
+} MuyoMatMulParams;
+size_t muyo_cuda_mat_mul_f16_workspace_size(const MuyoMatMulParams* p);
+int muyo_cuda_mat_mul_f16(const MuyoMatMulParams* p, const void* a, const float* x, float* y, const float* bias,
+                          void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- row-sharded GEMV + cross-GPU greedy (multi-GPU LM head) --------------------------------------
  * One GPU's share of a row-sharded GEMV with the argmax folded into its epilogue: rows

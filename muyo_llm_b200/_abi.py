@@ -19,6 +19,7 @@ MUYO_OK = 0
 ERRORS = {-1: "MUYO_EINVAL", -2: "MUYO_ECUDA", -3: "MUYO_ETIMEOUT", -4: "MUYO_ENOMEM", -5: "MUYO_EUNSUPPORTED",
           -6: "MUYO_ESTATE"}
 MATVEC_BIAS0, MATVEC_BIAS1, MATVEC_SCALE0, MATVEC_SCALE1 = 1, 2, 4, 8
+MATMUL_BIAS, MATMUL_ACCUMULATE = 1, 2
 GLU_HALVES, GLU_SWAPPED, GLU_SPLIT = 0, 1, 2
 ROPE_NORMAL, ROPE_NEOX = 0, 2
 KV_F32, KV_F16 = 0, 1
@@ -80,6 +81,10 @@ class Qwen2Config(C.Structure):
                [("rms_eps", F32), ("rope_base", F32), ("kv_dtype", U32)]
 
 
+class MatMulParams(C.Structure):
+    _fields_ = [(n, U32) for n in ("ncols", "rows", "tokens", "stride_x", "stride_y", "flags")]
+
+
 class SamplerParams(C.Structure):
     _fields_ = [("temperature", F32), ("top_k", C.c_int32), ("top_p", F32), ("repeat_penalty", F32),
                 ("repeat_last_n", C.c_int32), ("cluster_ctas", U32), ("seed", C.c_uint64)]
@@ -134,6 +139,8 @@ SIGNATURES = {
     "muyo_sampler_seed": (C.c_int, [VP, C.c_uint64, VP]),
     "muyo_cuda_sample": (C.c_int, [P(SamplerParams), VP, U32, VP, U32, VP, VP, VP]),
     "muyo_model_set_sampler": (C.c_int, [VP, P(SamplerParams), VP]),
+    "muyo_cuda_mat_mul_f16_workspace_size": (C.c_size_t, [P(MatMulParams)]),
+    "muyo_cuda_mat_mul_f16": (C.c_int, [P(MatMulParams), VP, VP, VP, VP, VP, C.c_size_t, VP]),
     "muyo_p2p_handle_bytes": (C.c_size_t, []),
     "muyo_p2p_create": (C.c_int, [C.c_int, C.c_int, U32, P(VP), VP]),
     "muyo_p2p_connect": (C.c_int, [VP, VP]),

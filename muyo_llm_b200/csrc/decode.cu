@@ -20,6 +20,7 @@
 
 #include "attention.cuh"
 #include "common.cuh"
+#include "prefill.cuh"
 
 // sampler.cu: parameter check and launch of the device sampler (gate = the model's {step,
 // prompt_end, total}, see k_sample).
@@ -857,6 +858,10 @@ struct MuyoModel {
     bool sampling = false;          // graph engine: a device sampler node follows the LM head
     MuyoSamplerParams sp{};         // its parameters (baked into the recorded graph)
     void* rng = nullptr;            // its mt19937_64 state, followed by the last sampled id (int32)
+    bool prefill = false;           // generate: the prompt's positions but the last in one batched pass
+    char* pf_buf = nullptr;         // batched-prefill activations for kPfCap positions
+    float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_att = nullptr, *pf_gu = nullptr;
+    __half *pf_hi = nullptr, *pf_lo = nullptr;
     double* rope_cs = nullptr;      // [max_seq][head_dim] cos/sin table (float64)
     muyo::PLayer* d_layers = nullptr;
     unsigned* bar = nullptr;        // persistent kernel grid-barrier counter
@@ -1272,6 +1277,7 @@ static void free_model(MuyoModel* m)
     cudaFree(m->vc);
     cudaFree(m->scratch);
     cudaFree(m->rng);
+    cudaFree(m->pf_buf);
     if (m->pinned)
         cudaFreeHost(m->pinned);
     delete m;
@@ -1563,6 +1569,139 @@ static int check_device_error(MuyoModel* m, cudaStream_t st)
     return MUYO_OK;
 }
 
+// ---- batched prefill ---------------------------------------------------------------------------------
+
+constexpr int kPfCap = 128;  // positions per prefill pass (longer prompts take several passes)
+
+static int pf_alloc(MuyoModel* m)
+{
+    if (m->pf_buf)
+        return MUYO_OK;
+    const Shape& s = m->s;
+    const size_t wide = (size_t)std::max(std::max(s.hidden, s.q_dim), s.ffn);
+    const size_t f32 = (size_t)kPfCap * ((size_t)s.hidden + s.qkv_rows + 2 * (size_t)s.q_dim + 2 * (size_t)s.ffn);
+    const size_t bytes = f32 * sizeof(float) + 2 * (size_t)kPfCap * wide * sizeof(__half) + 256;
+    if (cudaMalloc(&m->pf_buf, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        m->pf_buf = nullptr;
+        set_error("prefill: cannot allocate %zu bytes of activations", bytes);
+        return MUYO_ENOMEM;
+    }
+    char* p = m->pf_buf;
+    auto take = [&](size_t n) {
+        char* r = p;
+        p += (n + 255) / 256 * 256;
+        return r;
+    };
+    m->pf_x = reinterpret_cast<float*>(take((size_t)kPfCap * s.hidden * 4));
+    m->pf_qkv = reinterpret_cast<float*>(take((size_t)kPfCap * s.qkv_rows * 4));
+    m->pf_q = reinterpret_cast<float*>(take((size_t)kPfCap * s.q_dim * 4));
+    m->pf_att = reinterpret_cast<float*>(take((size_t)kPfCap * s.q_dim * 4));
+    m->pf_gu = reinterpret_cast<float*>(take((size_t)kPfCap * 2 * s.ffn * 4));
+    m->pf_hi = reinterpret_cast<__half*>(take((size_t)kPfCap * wide * 2));
+    m->pf_lo = reinterpret_cast<__half*>(take((size_t)kPfCap * wide * 2));
+    if ((size_t)(p - m->pf_buf) > bytes + 256 * 8) {
+        set_error("prefill: buffer plan overflow");
+        return MUYO_EINVAL;
+    }
+    for (auto k : {k_pf_gemm<PF_STORE>, k_pf_gemm<PF_BIAS>, k_pf_gemm<PF_ADD>})
+        MUYO_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPfGemmSmem));
+    return MUYO_OK;
+}
+
+template <int EPI>
+static int pf_gemm(const __half* w0, const __half* w1, int n_split, int N, int K, int T, const __half* xhi,
+                   const __half* xlo, int ldx, float* y, int ldy, const float* bias, cudaStream_t st)
+{
+    PfGemm g{w0, w1 ? w1 : w0, n_split, N, K, T, xhi, xlo, ldx, y, ldy, bias};
+    const dim3 grid((N + kPfBM - 1) / kPfBM, (T + kPfBN - 1) / kPfBN);
+    MUYO_CUDA_TRY(launch_kernel(k_pf_gemm<EPI>, grid, dim3(kPfThreads), kPfGemmSmem, st, true, g));
+    return MUYO_OK;
+}
+
+template <typename KV, int HD>
+static int pf_attention_t(const Shape& s, float* q, float* out, const float* qkv, char* kc, char* vc, int p0, int T,
+                          cudaStream_t st)
+{
+    PfRope r{qkv, s.qkv_rows, q, p0, s.heads, s.kv_heads, s.max_seq, s.rope_cs};
+    MUYO_CUDA_TRY(launch_kernel(k_pf_rope_append<KV, HD>, dim3(T, s.heads + s.kv_heads), dim3(HD), 0, st, true, r,
+                                reinterpret_cast<KV*>(kc), reinterpret_cast<KV*>(vc)));
+    PfAttn a{q, out, p0, s.heads, s.kv_heads, s.gqa, s.max_seq, 1.0f / sqrtf((float)s.head_dim)};
+    const size_t smem = pf_attn_smem(HD, s.gqa);
+    if (smem > 48 * 1024)
+        MUYO_CUDA_TRY(cudaFuncSetAttribute(k_pf_attention<KV, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    MUYO_CUDA_TRY(launch_kernel(k_pf_attention<KV, HD>, dim3(s.kv_heads, T), dim3(kPfAttnThreads), smem, st, true, a,
+                                reinterpret_cast<const KV*>(kc), reinterpret_cast<const KV*>(vc)));
+    return MUYO_OK;
+}
+
+static int pf_attention(const Shape& s, float* q, float* out, const float* qkv, char* kc, char* vc, int p0, int T,
+                        cudaStream_t st)
+{
+#define MUYO_PF_ATTN(KV)                                                                        switch (s.head_dim) {                                                                           case 16: return pf_attention_t<KV, 16>(s, q, out, qkv, kc, vc, p0, T, st);                  case 32: return pf_attention_t<KV, 32>(s, q, out, qkv, kc, vc, p0, T, st);                  case 64: return pf_attention_t<KV, 64>(s, q, out, qkv, kc, vc, p0, T, st);                  default: return pf_attention_t<KV, 128>(s, q, out, qkv, kc, vc, p0, T, st);             }
+    if (s.kv_f16)
+        MUYO_PF_ATTN(__half)
+    MUYO_PF_ATTN(float)
+#undef MUYO_PF_ATTN
+}
+
+// Positions [p0, p0 + n) of m->tokens through every layer: their keys and values go to the cache.
+// No logits are formed (the decode step at position p0 + n forms the next ones).
+static int prefill_run(MuyoModel* m, int p0, int n, cudaStream_t st)
+{
+    const Shape& s = m->s;
+    const int H = s.hidden, QD = s.q_dim, F = s.ffn;
+    const int ldh = std::max(std::max(H, QD), F);
+    int rc;
+    for (int c0 = 0; c0 < n; c0 += kPfCap) {
+        const int T = std::min(kPfCap, n - c0), pos0 = p0 + c0;
+        MUYO_CUDA_TRY(launch_kernel(k_pf_embed, dim3(T), dim3(256), 0, st, true, W(m, "token_embd.weight"),
+                                    (const int32_t*)(m->tokens + pos0), s.vocab, H, m->pf_x));
+        for (int l = 0; l < s.layers; ++l) {
+            const LayerPtrs w = layer_ptrs(m, l);
+            char* kc = static_cast<char*>(m->kc) + m->kv_layer_bytes * l;
+            char* vc = static_cast<char*>(m->vc) + m->kv_layer_bytes * l;
+            MUYO_CUDA_TRY(launch_kernel(k_pf_norm_split, dim3(T), dim3(256), 0, st, true, (const float*)m->pf_x, H,
+                                        w.attn_norm, s.eps, H, m->pf_hi, m->pf_lo, ldh));
+            if ((rc = pf_gemm<PF_BIAS>(w.wqkv, nullptr, s.qkv_rows, s.qkv_rows, H, T, m->pf_hi, m->pf_lo, ldh,
+                                       m->pf_qkv, s.qkv_rows, w.bqkv, st)))
+                return rc;
+            if ((rc = pf_attention(s, m->pf_q, m->pf_att, m->pf_qkv, kc, vc, pos0, T, st)))
+                return rc;
+            MUYO_CUDA_TRY(launch_kernel(k_pf_split, dim3(T), dim3(256), 0, st, true, (const float*)m->pf_att, QD, QD,
+                                        m->pf_hi, m->pf_lo, ldh));
+            if ((rc = pf_gemm<PF_ADD>(w.wo, nullptr, H, H, QD, T, m->pf_hi, m->pf_lo, ldh, m->pf_x, H, nullptr, st)))
+                return rc;
+            MUYO_CUDA_TRY(launch_kernel(k_pf_norm_split, dim3(T), dim3(256), 0, st, true, (const float*)m->pf_x, H,
+                                        w.ffn_norm, s.eps, H, m->pf_hi, m->pf_lo, ldh));
+            if ((rc = pf_gemm<PF_STORE>(w.wgate, w.wup, F, 2 * F, H, T, m->pf_hi, m->pf_lo, ldh, m->pf_gu, 2 * F,
+                                        nullptr, st)))
+                return rc;
+            MUYO_CUDA_TRY(launch_kernel(k_pf_swiglu_split, dim3(T), dim3(256), 0, st, true, (const float*)m->pf_gu, F,
+                                        m->pf_hi, m->pf_lo, ldh));
+            if ((rc = pf_gemm<PF_ADD>(w.wdown, nullptr, H, H, F, T, m->pf_hi, m->pf_lo, ldh, m->pf_x, H, nullptr, st)))
+                return rc;
+        }
+    }
+    MUYO_LAUNCH_CHECK();
+    return MUYO_OK;
+}
+
+// generate: with batched prefill, every prompt position but the last goes through prefill_run;
+// returns the number of positions it fed (0 when prefill is off or the prompt has one id).
+static int feed_prompt(MuyoModel* m, int n_prompt, cudaStream_t st, int& fed)
+{
+    fed = 0;
+    if (!m->prefill || n_prompt < 2)
+        return MUYO_OK;
+    const int rc = prefill_run(m, m->host_pos, n_prompt - 1, st);
+    if (rc)
+        return rc;
+    fed = n_prompt - 1;
+    m->host_pos += fed;
+    return MUYO_OK;
+}
+
 static int check_generate(MuyoModel* m, int n_prompt, int n_predict)
 {
     MUYO_REQUIRE(m, "generate: null model");
@@ -1592,7 +1731,10 @@ extern "C" int muyo_model_generate_device(MuyoModel* m, const int32_t* prompt_de
     const int p0 = m->host_pos;
     MUYO_CUDA_TRY(cudaMemcpyAsync(m->tokens + p0, prompt_dev, sizeof(int32_t) * n_prompt, cudaMemcpyDeviceToDevice, st));
     const int total = p0 + n_prompt + n_predict;
-    rc = run_steps(m, p0 + n_prompt, total, n_prompt + n_predict, st);
+    int fed = 0;
+    if ((rc = feed_prompt(m, n_prompt, st, fed)))
+        return rc;
+    rc = run_steps(m, p0 + n_prompt, total, n_prompt - fed + n_predict, st);
     if (rc)
         return rc;
     if (n_predict > 0)
@@ -1615,7 +1757,10 @@ extern "C" int muyo_model_generate(MuyoModel* m, const int32_t* prompt, int n_pr
     std::memcpy(m->pinned, prompt, sizeof(int32_t) * n_prompt);
     MUYO_CUDA_TRY(cudaMemcpyAsync(m->tokens + p0, m->pinned, sizeof(int32_t) * n_prompt, cudaMemcpyHostToDevice, st));
     const int total = p0 + n_prompt + n_predict;
-    rc = run_steps(m, p0 + n_prompt, total, n_prompt + n_predict, st);
+    int fed = 0;
+    if ((rc = feed_prompt(m, n_prompt, st, fed)))
+        return rc;
+    rc = run_steps(m, p0 + n_prompt, total, n_prompt - fed + n_predict, st);
     if (rc)
         return rc;
     if (n_predict > 0) {
@@ -1747,6 +1892,17 @@ extern "C" int muyo_model_set_option(MuyoModel* m, const char* key, int value)
         m->sw = value != 0;
         return MUYO_OK;
     }
+    if (k == "prefill") {
+        MUYO_REQUIRE(value == 0 || value == 1, "set_option: prefill must be 0 or 1");
+        MUYO_CUDA_TRY(cudaSetDevice(m->device));
+        if (value) {
+            const int rc = pf_alloc(m);
+            if (rc)
+                return rc;
+        }
+        m->prefill = value != 0;
+        return MUYO_OK;
+    }
     if (k == "pdl") {
         MUYO_REQUIRE(value == 0 || value == 1, "set_option: pdl must be 0 or 1");
         MUYO_REQUIRE(!m->exec, "set_option: pdl must be set before muyo_model_finalize");
@@ -1755,4 +1911,51 @@ extern "C" int muyo_model_set_option(MuyoModel* m, const char* key, int value)
     }
     MUYO_REQUIRE(false, "set_option: unknown option %s", key);
     return MUYO_EINVAL;
+}
+
+// ---- op level: batched F16 GEMM (the prefill's projection) -----------------------------------------
+
+extern "C" size_t muyo_cuda_mat_mul_f16_workspace_size(const MuyoMatMulParams* p)
+{
+    if (!p)
+        return 0;
+    return 2 * (size_t)p->tokens * ((size_t)p->ncols + 7) / 8 * 8 * sizeof(__half) + 256;
+}
+
+extern "C" int muyo_cuda_mat_mul_f16(const MuyoMatMulParams* p, const void* a, const float* x, float* y,
+                                     const float* bias, void* workspace, size_t workspace_bytes, void* stream)
+{
+    clear_error();
+    MUYO_REQUIRE(p && a && x && y, "mat_mul: null parameter block or buffer");
+    const int K = (int)p->ncols, N = (int)p->rows, T = (int)p->tokens;
+    const int ldx = p->stride_x ? (int)p->stride_x : K, ldy = p->stride_y ? (int)p->stride_y : N;
+    MUYO_REQUIRE(K > 0 && N > 0 && T > 0, "mat_mul: ncols, rows and tokens must be positive");
+    MUYO_REQUIRE(K % 8 == 0, "mat_mul: ncols %d must be a multiple of 8", K);
+    MUYO_REQUIRE(ldx >= K && ldx % 4 == 0 && ldy >= N, "mat_mul: strides too small or x stride not a multiple of 4");
+    MUYO_REQUIRE((p->flags & ~(MUYO_MATMUL_BIAS | MUYO_MATMUL_ACCUMULATE)) == 0 &&
+                     (p->flags & (MUYO_MATMUL_BIAS | MUYO_MATMUL_ACCUMULATE)) != (MUYO_MATMUL_BIAS | MUYO_MATMUL_ACCUMULATE),
+                 "mat_mul: flags are BIAS or ACCUMULATE");
+    MUYO_REQUIRE(!(p->flags & MUYO_MATMUL_BIAS) || bias, "mat_mul: BIAS without a bias vector");
+    MUYO_REQUIRE(aligned16(a) && aligned16(x), "mat_mul: a and x must be 16-byte aligned");
+    MUYO_REQUIRE(workspace && workspace_bytes >= muyo_cuda_mat_mul_f16_workspace_size(p) && aligned16(workspace),
+                 "mat_mul: workspace of muyo_cuda_mat_mul_f16_workspace_size bytes, 16-byte aligned, required");
+    const cudaStream_t st = as_stream(stream);
+    const int ldh = (K + 7) / 8 * 8;
+    __half* hi = static_cast<__half*>(workspace);
+    __half* lo = hi + (size_t)T * ldh;
+    for (auto k : {k_pf_gemm<PF_STORE>, k_pf_gemm<PF_BIAS>, k_pf_gemm<PF_ADD>})
+        MUYO_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPfGemmSmem));
+    MUYO_CUDA_TRY(launch_kernel(k_pf_split, dim3(T), dim3(256), 0, st, true, x, ldx, K, hi, lo, ldh));
+    const __half* w = static_cast<const __half*>(a);
+    int rc;
+    if (p->flags & MUYO_MATMUL_BIAS)
+        rc = pf_gemm<PF_BIAS>(w, nullptr, N, N, K, T, hi, lo, ldh, y, ldy, bias, st);
+    else if (p->flags & MUYO_MATMUL_ACCUMULATE)
+        rc = pf_gemm<PF_ADD>(w, nullptr, N, N, K, T, hi, lo, ldh, y, ldy, nullptr, st);
+    else
+        rc = pf_gemm<PF_STORE>(w, nullptr, N, N, K, T, hi, lo, ldh, y, ldy, nullptr, st);
+    if (rc)
+        return rc;
+    MUYO_LAUNCH_CHECK();
+    return MUYO_OK;
 }

@@ -1,0 +1,429 @@
+// Batched prefill: the prompt's positions go through each layer together instead of one decode
+// step per token (the reference feeds a prompt one position at a time, src/FullModel.cpp:1096-1108,
+// 1174-1181; its unused batched GEMM shader is shaders/llama/mul_mm.comp). The positions' keys and
+// values land in the same KV cache the decode step reads; the decode step then takes over at the
+// prompt's last position.
+//
+// Per layer, for T positions:
+//   k_pf_norm_split   RMSNorm of the residual rows (the decode prologue's arithmetic and thread
+//                     layout, so each row's value is bit-identical), written as two F16 halves
+//   k_pf_gemm<BIAS>   QKV projection + bias
+//   k_pf_rope_append  RoPE (float64 angles, as the decode step) on q and k; k and v into the cache
+//   k_pf_attention    causal GQA over the cache, one CTA per (kv head, position)
+//   k_pf_split        attention rows -> two F16 halves
+//   k_pf_gemm<ADD>    O projection added to the residual
+//   k_pf_norm_split, k_pf_gemm<STORE> (gate | up, two matrices in one launch), k_pf_swiglu_split,
+//   k_pf_gemm<ADD>    the MLP
+//
+// The GEMM is weight-read bound for prompts of up to a few hundred positions (2 flops per weight
+// byte per position), so it uses the warp-level mma.sync m16n8k16 (F16 x F16 -> F32) on tiles
+// staged by cp.async: an activation x enters as hi = f16(x) and lo = f16(x - hi), two products into
+// one F32 accumulator, which keeps the product error near F32's (2^-22 relative to |x|).
+#pragma once
+
+#include <cuda_fp16.h>
+
+#include "attention.cuh"
+#include "common.cuh"
+
+namespace muyo {
+
+constexpr int kPfBM = 64;  // feature rows per CTA (4 warps x 16)
+constexpr int kPfBN = 64;  // positions per CTA
+constexpr int kPfBK = 64;  // reduction chunk per pipeline stage
+constexpr int kPfLD = kPfBK + 8;  // padded row (144 bytes): ldmatrix rows fall in distinct banks
+constexpr int kPfStages = 3;
+constexpr int kPfThreads = 128;
+constexpr int kPfStageHalfs = 3 * 64 * kPfLD;  // W tile, x-hi tile, x-lo tile
+constexpr size_t kPfGemmSmem = (size_t)kPfStages * kPfStageHalfs * sizeof(__half);
+
+enum PfEpi { PF_STORE = 0, PF_BIAS = 1, PF_ADD = 2 };
+
+// y[t][n] (= | += | = b[n] +) sum_k W[n][k] * x[t][k] for n < N, t < T. W rows are K halves apart;
+// rows [0, n_split) come from w0 and rows [n_split, N) from w1 (row n - n_split).
+struct PfGemm {
+    const __half* w0;
+    const __half* w1;
+    int n_split;
+    int N, K, T;
+    const __half* xhi;  // [T][ldx]
+    const __half* xlo;
+    int ldx;
+    float* y;  // [T][ldy]
+    int ldy;
+    const float* bias;
+};
+
+__device__ __forceinline__ void cp_async16(unsigned dst, const void* src, bool full)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(full ? 16 : 0));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait()
+{
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+__device__ __forceinline__ void ldsm_x4(unsigned addr, unsigned& r0, unsigned& r1, unsigned& r2, unsigned& r3)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+// d += a (16x16, row-major) * b (16x8, k-major per column), F16 inputs, F32 accumulation.
+__device__ __forceinline__ void mma_16816(float (&d)[4], unsigned a0, unsigned a1, unsigned a2, unsigned a3,
+                                          unsigned b0, unsigned b1)
+{
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// One CTA: 64 feature rows x 64 positions. Warp w owns rows [16w, 16w + 16) of the tile and all 64
+// positions (8 accumulator fragments of 16 x 8). K advances 64 at a time through a 3-stage cp.async
+// ring; chunks past N, T or K are zero-filled (K is a multiple of 8).
+template <int EPI>
+__global__ void __launch_bounds__(kPfThreads) k_pf_gemm(PfGemm g)
+{
+    extern __shared__ __align__(16) __half pf_smem[];
+    pdl_wait();
+    pdl_trigger();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int n0 = blockIdx.x * kPfBM, t0 = blockIdx.y * kPfBN;
+    const int nk = (g.K + kPfBK - 1) / kPfBK;
+    const unsigned sbase = (unsigned)__cvta_generic_to_shared(pf_smem);
+
+    auto load_stage = [&](int buf, int kt) {
+        const int k0 = kt * kPfBK;
+        const unsigned st = sbase + (unsigned)(buf * kPfStageHalfs * 2);
+        for (int c = tid; c < 3 * 64 * 8; c += kPfThreads) {  // 3 tiles x 64 rows x 8 16-byte chunks
+            const int tile = c >> 9, r = (c >> 3) & 63, ch = c & 7;
+            const int k = k0 + ch * 8;
+            const unsigned dst = st + (unsigned)((tile * 64 * kPfLD + r * kPfLD + ch * 8) * 2);
+            if (tile == 0) {
+                const int n = n0 + r;
+                const bool ok = n < g.N && k < g.K;
+                const __half* src = g.w0;
+                if (ok)
+                    src = n < g.n_split ? g.w0 + (size_t)n * g.K + k : g.w1 + (size_t)(n - g.n_split) * g.K + k;
+                cp_async16(dst, src, ok);
+            } else {
+                const int t = t0 + r;
+                const bool ok = t < g.T && k < g.K;
+                const __half* xb = tile == 1 ? g.xhi : g.xlo;
+                cp_async16(dst, ok ? xb + (size_t)t * g.ldx + k : xb, ok);
+            }
+        }
+    };
+
+    float acc[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            acc[j][e] = 0.0f;
+#pragma unroll
+    for (int s = 0; s < kPfStages - 1; ++s) {
+        if (s < nk)
+            load_stage(s, s);
+        cp_async_commit();
+    }
+    const int mat = lane >> 3;
+    for (int kt = 0; kt < nk; ++kt) {
+        cp_async_wait<kPfStages - 2>();
+        __syncthreads();  // stage kt is visible, and every warp is done with the buffer refilled next
+        {
+            const int nxt = kt + kPfStages - 1;
+            if (nxt < nk)
+                load_stage(nxt % kPfStages, nxt);
+            cp_async_commit();
+        }
+        const unsigned ws = sbase + (unsigned)((kt % kPfStages) * kPfStageHalfs * 2);
+        const unsigned xh = ws + 64 * kPfLD * 2, xl = ws + 2 * 64 * kPfLD * 2;
+#pragma unroll
+        for (int kk = 0; kk < kPfBK; kk += 16) {
+            unsigned a0, a1, a2, a3;
+            {  // matrices: rows 0-7 / 8-15 x k 0-7 / 8-15 of the warp's 16 rows -> a0..a3
+                const int r = warp * 16 + (mat & 1) * 8 + (lane & 7), c = kk + (mat >> 1) * 8;
+                ldsm_x4(ws + (unsigned)((r * kPfLD + c) * 2), a0, a1, a2, a3);
+            }
+#pragma unroll
+            for (int j2 = 0; j2 < 4; ++j2) {  // positions 16*j2 .. +15: two 8-wide fragments
+                const int r = j2 * 16 + (mat >> 1) * 8 + (lane & 7), c = kk + (mat & 1) * 8;
+                unsigned h0, h1, h2, h3, l0, l1, l2, l3;
+                ldsm_x4(xh + (unsigned)((r * kPfLD + c) * 2), h0, h1, h2, h3);
+                ldsm_x4(xl + (unsigned)((r * kPfLD + c) * 2), l0, l1, l2, l3);
+                mma_16816(acc[2 * j2], a0, a1, a2, a3, h0, h1);
+                mma_16816(acc[2 * j2], a0, a1, a2, a3, l0, l1);
+                mma_16816(acc[2 * j2 + 1], a0, a1, a2, a3, h2, h3);
+                mma_16816(acc[2 * j2 + 1], a0, a1, a2, a3, l2, l3);
+            }
+        }
+    }
+    cp_async_wait<0>();
+    // fragment (j, e): feature row 16w + lane/4 (+8 for e >= 2), position 8j + 2*(lane%4) + (e & 1)
+    const int gr = lane >> 2, tq = lane & 3;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int n = n0 + warp * 16 + gr + (e >> 1) * 8;
+            const int t = t0 + j * 8 + tq * 2 + (e & 1);
+            if (n < g.N && t < g.T) {
+                float* yp = g.y + (size_t)t * g.ldy + n;
+                float v = acc[j][e];
+                if (EPI == PF_BIAS)
+                    v = v + g.bias[n];
+                if (EPI == PF_ADD)
+                    v = *yp + v;
+                *yp = v;
+            }
+        }
+}
+
+__device__ __forceinline__ void split_store(__half* hi, __half* lo, float4 v)
+{
+    const __half2 h01 = __floats2half2_rn(v.x, v.y), h23 = __floats2half2_rn(v.z, v.w);
+    const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+    const __half2 l01 = __floats2half2_rn(v.x - f01.x, v.y - f01.y), l23 = __floats2half2_rn(v.z - f23.x, v.w - f23.y);
+    reinterpret_cast<__half2*>(hi)[0] = h01;
+    reinterpret_cast<__half2*>(hi)[1] = h23;
+    reinterpret_cast<__half2*>(lo)[0] = l01;
+    reinterpret_cast<__half2*>(lo)[1] = l23;
+}
+
+// Row t of x [T][ldx] (F32) -> hi/lo [T][ldh]; K a multiple of 4, rows 16-byte aligned.
+__global__ void __launch_bounds__(256) k_pf_split(const float* __restrict__ x, int ldx, int K, __half* hi, __half* lo,
+                                                  int ldh)
+{
+    pdl_wait();
+    pdl_trigger();
+    const int t = blockIdx.x;
+    for (int q = threadIdx.x; q < K / 4; q += blockDim.x) {
+        const float4 v = reinterpret_cast<const float4*>(x + (size_t)t * ldx)[q];
+        split_store(hi + (size_t)t * ldh + 4 * q, lo + (size_t)t * ldh + 4 * q, v);
+    }
+}
+
+// RMSNorm of row t (x / sqrt(mean(x^2) + eps) * w) -> hi/lo. 256 threads, each adding the squares
+// of the float4s q = tid + 256 j in that order, then block_sum: the decode prologue's arithmetic.
+__global__ void __launch_bounds__(256) k_pf_norm_split(const float* __restrict__ x, int ldx,
+                                                       const float* __restrict__ w, float eps, int K, __half* hi,
+                                                       __half* lo, int ldh)
+{
+    __shared__ float red[32];
+    pdl_wait();
+    pdl_trigger();
+    const int t = blockIdx.x, tid = threadIdx.x, Q = K / 4;
+    const float4* x4 = reinterpret_cast<const float4*>(x + (size_t)t * ldx);
+    float ss = 0.0f;
+    for (int q = tid; q < Q; q += blockDim.x) {
+        const float4 v = x4[q];
+        ss = fmaf(v.x, v.x, ss);
+        ss = fmaf(v.y, v.y, ss);
+        ss = fmaf(v.z, v.z, ss);
+        ss = fmaf(v.w, v.w, ss);
+    }
+    ss = block_sum(ss, red);
+    const float s = __fsqrt_rn(__fdiv_rn(ss, (float)K) + eps);
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+    for (int q = tid; q < Q; q += blockDim.x) {
+        const float4 v = x4[q], ww = w4[q];
+        const float4 y = make_float4(__fdiv_rn(v.x, s) * ww.x, __fdiv_rn(v.y, s) * ww.y, __fdiv_rn(v.z, s) * ww.z,
+                                     __fdiv_rn(v.w, s) * ww.w);
+        split_store(hi + (size_t)t * ldh + 4 * q, lo + (size_t)t * ldh + 4 * q, y);
+    }
+}
+
+// act = silu(gate) * up for row t of gu [T][2F] (gate | up) -> hi/lo [T][ldh].
+__global__ void __launch_bounds__(256) k_pf_swiglu_split(const float* __restrict__ gu, int F, __half* hi, __half* lo,
+                                                         int ldh)
+{
+    pdl_wait();
+    pdl_trigger();
+    const int t = blockIdx.x;
+    const float4* g4 = reinterpret_cast<const float4*>(gu + (size_t)t * 2 * F);
+    const float4* u4 = reinterpret_cast<const float4*>(gu + (size_t)t * 2 * F + F);
+    for (int q = threadIdx.x; q < F / 4; q += blockDim.x) {
+        const float4 gv = g4[q], uv = u4[q];
+        const float4 a = make_float4(silu_mul(gv.x, uv.x), silu_mul(gv.y, uv.y), silu_mul(gv.z, uv.z),
+                                     silu_mul(gv.w, uv.w));
+        split_store(hi + (size_t)t * ldh + 4 * q, lo + (size_t)t * ldh + 4 * q, a);
+    }
+}
+
+// x[t][:] = embedding row of tokens[t] (F16 -> F32); an id outside [0, vocab) gathers row 0, as the
+// decode step does.
+__global__ void __launch_bounds__(256) k_pf_embed(const __half* __restrict__ embd, const int32_t* tokens, int vocab,
+                                                  int H, float* x)
+{
+    pdl_wait();
+    pdl_trigger();
+    const int t = blockIdx.x;
+    int tok = tokens[t];
+    if (tok < 0 || tok >= vocab)
+        tok = 0;
+    const __half* row = embd + (size_t)tok * H;
+    for (int k = threadIdx.x; k < H; k += blockDim.x)
+        x[(size_t)t * H + k] = __half2float(row[k]);
+}
+
+struct PfRope {
+    const float* qkv;  // [T][ldqkv]: q (heads*HD) | k (kv_heads*HD) | v (kv_heads*HD)
+    int ldqkv;
+    float* q;  // [T][heads*HD], rotated
+    int p0, heads, kv_heads, max_seq;
+    const double* cs;  // [max_seq][HD] cos | sin
+};
+
+// Block (t, h): q head h < heads is rotated into q; kv head h - heads has its key rotated and its
+// key and value written at position p0 + t of the cache (the decode step's rounding to KV).
+template <typename KV, int HD>
+__global__ void __launch_bounds__(HD) k_pf_rope_append(PfRope r, KV* kc, KV* vc)
+{
+    pdl_wait();
+    pdl_trigger();
+    const int t = blockIdx.x, h = blockIdx.y, j = threadIdx.x, pos = r.p0 + t;
+    const float* row = r.qkv + (size_t)t * r.ldqkv;
+    const double c = j < HD / 2 ? __ldg(r.cs + (size_t)pos * HD + j) : 0.0;
+    const double s = j < HD / 2 ? __ldg(r.cs + (size_t)pos * HD + HD / 2 + j) : 0.0;
+    if (h < r.heads) {
+        if (j < HD / 2) {
+            const float* src = row + h * HD;
+            float y0, y1;
+            rope_pair_f64(src[j], src[j + HD / 2], c, s, y0, y1);
+            float* dst = r.q + (size_t)t * r.heads * HD + h * HD;
+            dst[j] = y0;
+            dst[j + HD / 2] = y1;
+        }
+        return;
+    }
+    const int kh = h - r.heads;
+    const size_t at = ((size_t)kh * r.max_seq + pos) * HD;
+    if (j < HD / 2) {
+        const float* src = row + (r.heads + kh) * HD;
+        float y0, y1;
+        rope_pair_f64(src[j], src[j + HD / 2], c, s, y0, y1);
+        kc[at + j] = kv_round<KV>(y0);
+        kc[at + j + HD / 2] = kv_round<KV>(y1);
+    }
+    vc[at + j] = kv_round<KV>(row[(r.heads + r.kv_heads + kh) * HD + j]);
+}
+
+struct PfAttn {
+    const float* q;  // [T][heads*HD], rotated
+    float* out;      // [T][heads*HD]
+    int p0, heads, kv_heads, gqa, max_seq;
+    float scale;
+};
+
+constexpr int kPfAttnKeys = 64;
+constexpr int kPfAttnThreads = 256;
+
+// CTA (kv head kh, position t): the gqa query heads of kh at position pos = p0 + t attend to keys
+// 0..pos of the cache. Keys go through shared memory 64 at a time with an online softmax (running
+// max m, sum l, output o rescaled by exp(m_old - m_new)); scores, exponentials and the P.V products
+// are formed as in the decode step's attention.
+template <typename KV, int HD>
+__global__ void __launch_bounds__(kPfAttnThreads) k_pf_attention(PfAttn a, const KV* __restrict__ kc,
+                                                                  const KV* __restrict__ vc)
+{
+    constexpr int LD = HD + 1;
+    extern __shared__ float pa_smem[];
+    const int G = a.gqa;
+    float* Ks = pa_smem;                   // [64][LD]
+    float* Vs = Ks + kPfAttnKeys * LD;     // [64][LD]
+    float* Qs = Vs + kPfAttnKeys * LD;     // [G][HD]
+    float* Os = Qs + G * HD;               // [G][HD]
+    float* Ps = Os + G * HD;               // [G][64]
+    float* Ms = Ps + G * kPfAttnKeys;      // [G] running max
+    float* Ls = Ms + G;                    // [G] running sum
+    float* As = Ls + G;                    // [G] rescale of this chunk
+    pdl_wait();
+    pdl_trigger();
+    const int kh = blockIdx.x, t = blockIdx.y, tid = threadIdx.x, nt = blockDim.x;
+    const int pos = a.p0 + t, n = pos + 1;
+    const size_t head_base = (size_t)kh * a.max_seq * HD;
+    for (int e = tid; e < G * HD; e += nt) {
+        Qs[e] = a.q[(size_t)t * a.heads * HD + (size_t)kh * G * HD + e];
+        Os[e] = 0.0f;
+    }
+    if (tid < G) {
+        Ms[tid] = -INFINITY;
+        Ls[tid] = 0.0f;
+    }
+    for (int key0 = 0; key0 < n; key0 += kPfAttnKeys) {
+        const int nk = min(kPfAttnKeys, n - key0);
+        __syncthreads();  // the previous chunk's readers are done
+        for (int e = tid; e < nk * HD; e += nt) {
+            const int r = e / HD, d = e % HD;
+            const size_t off = head_base + (size_t)(key0 + r) * HD + d;
+            Ks[r * LD + d] = kv_value<KV>(kc[off]);
+            Vs[r * LD + d] = kv_value<KV>(vc[off]);
+        }
+        __syncthreads();
+        {
+            const int kt = tid % kPfAttnKeys, h0 = tid / kPfAttnKeys, hs = nt / kPfAttnKeys;
+            for (int gq = h0; gq < G; gq += hs) {
+                float sc = -INFINITY;
+                if (kt < nk) {
+                    float dot = 0.0f;
+#pragma unroll 16
+                    for (int d = 0; d < HD; ++d)
+                        dot = fmaf(Qs[gq * HD + d], Ks[kt * LD + d], dot);
+                    sc = dot * a.scale;
+                }
+                Ps[gq * kPfAttnKeys + kt] = sc;
+            }
+        }
+        __syncthreads();
+        {
+            const int lane = tid & 31, warp = tid >> 5, nw = nt / 32;
+            for (int gq = warp; gq < G; gq += nw) {
+                float m = -INFINITY;
+                for (int k = lane; k < kPfAttnKeys; k += 32)
+                    m = fmaxf(m, Ps[gq * kPfAttnKeys + k]);
+                m = warp_max(m);
+                const float m_old = Ms[gq], m_new = fmaxf(m_old, m);
+                float l = 0.0f;
+                for (int k = lane; k < kPfAttnKeys; k += 32) {
+                    const float e = k < nk ? expf(Ps[gq * kPfAttnKeys + k] - m_new) : 0.0f;
+                    Ps[gq * kPfAttnKeys + k] = e;
+                    l += e;
+                }
+                l = warp_sum(l);
+                if (lane == 0) {
+                    const float alpha = expf(m_old - m_new);  // 0 for the first chunk (m_old = -inf)
+                    As[gq] = alpha;
+                    Ls[gq] = Ls[gq] * alpha + l;
+                    Ms[gq] = m_new;
+                }
+            }
+        }
+        __syncthreads();
+        for (int e = tid; e < G * HD; e += nt) {
+            const int gq = e / HD, d = e % HD;
+            float o = Os[e] * As[gq];
+            for (int k = 0; k < nk; ++k)
+                o = fmaf(Ps[gq * kPfAttnKeys + k], Vs[k * LD + d], o);
+            Os[e] = o;
+        }
+    }
+    __syncthreads();
+    for (int e = tid; e < G * HD; e += nt) {
+        const int gq = e / HD;
+        a.out[(size_t)t * a.heads * HD + (size_t)kh * G * HD + e] = __fdiv_rn(Os[e], Ls[gq]);
+    }
+}
+
+inline size_t pf_attn_smem(int hd, int gqa)
+{
+    return sizeof(float) * ((size_t)2 * kPfAttnKeys * (hd + 1) + (size_t)2 * gqa * hd + (size_t)gqa * kPfAttnKeys +
+                            3 * (size_t)gqa);
+}
+
+}  // namespace muyo

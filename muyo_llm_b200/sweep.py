@@ -207,6 +207,90 @@ def sampler(iters: int = 0, peak_gbs: float = 6462.1, seed: int = 7, n_prompt: i
     return out
 
 
+def prefill(iters: int = 0, peak_gbs: float = 6462.1, seed: int = 7, n_prompt: int = 32, n_predict: int = 256):
+    """Batched prefill. (1) muyo_cuda_mat_mul_f16 at the 0.5B layer's projection shapes for 128
+    positions: device time per call (CUDA graph of back-to-back calls), weight GB/s and tensor
+    TFLOP/s. (2) Prompt-only prefill (positions 0 .. P-2 of a P-id prompt, then the one decode step
+    that forms the first logits) against P decode steps, P = 32, 128, 512. (3) Config 4 end to end
+    (32 prompt + 256 generated ids) with and without batched prefill."""
+    import ctypes as C
+
+    from . import _abi, engine, synth
+
+    out = []
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    stream = torch.cuda.Stream()
+    n_calls = iters or 50
+    for N, K, T, what in [(1152, 896, 128, "QKV"), (896, 896, 128, "O"), (9728, 896, 128, "gate|up"),
+                          (896, 4864, 128, "down")]:
+        w = (torch.rand(N * K, generator=g, device="cuda") * 0.1 - 0.05).half()
+        x = torch.randn(T * K, generator=g, device="cuda")
+        y = torch.empty(T * N, device="cuda")
+        p = _abi.MatMulParams(K, N, T, 0, 0, 0)
+        wsb = int(_abi.lib().muyo_cuda_mat_mul_f16_workspace_size(C.byref(p)))
+        ws = torch.empty(wsb, dtype=torch.uint8, device="cuda")
+
+        def call():
+            _abi.call("muyo_cuda_mat_mul_f16", C.byref(p), C.c_void_p(w.data_ptr()), C.c_void_p(x.data_ptr()),
+                      C.c_void_p(y.data_ptr()), None, C.c_void_p(ws.data_ptr()), wsb, C.c_void_p(stream.cuda_stream))
+
+        with torch.cuda.stream(stream):
+            call()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream, capture_error_mode="thread_local"):
+            for _ in range(n_calls):
+                call()
+        gr.replay()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        gr.replay()
+        e.record()
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / n_calls
+        alg = N * K * 2 + T * K * 4 + T * N * 4
+        r = _result("k_pf_split + k_pf_gemm", f"{N}x{K}, {T} positions ({what})", alg, ms, peak_gbs,
+                    tflops=2 * N * K * T / (ms * 1e-3) / 1e12, mode="weights L2-resident between calls")
+        out.append(r)
+    cfg = synth.QWEN2_05B
+    t = synth.make_model(cfg, seed)
+    models = {}
+    for pf in (False, True):
+        models[pf] = engine.Qwen2Model(cfg, t, kv_dtype=_abi.KV_F16, engine=engine.Qwen2Model.ENGINE_GRAPH)
+        if pf:
+            _abi.call("muyo_model_set_option", models[pf]._m, b"prefill", 1)
+
+    def timed(m, prompt, n):
+        best = float("inf")
+        for _ in range(3):
+            m.reset()
+            torch.cuda.synchronize()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            m.generate(prompt, n)
+            e.record()
+            torch.cuda.synchronize()
+            best = min(best, s.elapsed_time(e))
+        return best
+
+    for P in (32, 128, 512):
+        prompt = [int(i) for i in synth.prompt_ids(seed, P, cfg.vocab)]
+        off, on = timed(models[False], prompt, 1), timed(models[True], prompt, 1)
+        out.append({"kernel": "prompt to first token", "shape": f"config 4 arch, {P}-id prompt",
+                    "ms_stepwise": off, "ms_prefill": on, "speedup": off / on,
+                    "prompt_tokens_per_s_prefill": P / (on * 1e-3), "mode": "prefill of P-1 positions + 1 step"})
+    prompt = [int(i) for i in synth.prompt_ids(seed, n_prompt, cfg.vocab)]
+    for pf in (False, True):
+        ms = timed(models[pf], prompt, n_predict)
+        out.append({"kernel": "generate", "shape": f"config 4 ({n_prompt} prompt + {n_predict} generated)",
+                    "batched_prefill": pf, "ms": ms, "tokens_per_s": (n_prompt + n_predict) / (ms * 1e-3)})
+    for m in models.values():
+        m.close()
+    return out
+
+
 SHARDED_SHAPES = [(151936, 896), (4096, 4096), (14336, 4096), (128256, 4096)]
 
 
