@@ -861,6 +861,8 @@ struct MuyoModel {
     bool prefill = false;           // generate: the prompt's positions but the last in one batched pass
     char* pf_buf = nullptr;         // batched-prefill activations for kPfCap positions
     float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_att = nullptr, *pf_gu = nullptr;
+    float* pf_part = nullptr;  // split-K partial sums
+    size_t pf_part_floats = 0;
     __half *pf_hi = nullptr, *pf_lo = nullptr;
     double* rope_cs = nullptr;      // [max_seq][head_dim] cos/sin table (float64)
     muyo::PLayer* d_layers = nullptr;
@@ -1572,6 +1574,7 @@ static int check_device_error(MuyoModel* m, cudaStream_t st)
 // ---- batched prefill ---------------------------------------------------------------------------------
 
 constexpr int kPfCap = 128;  // positions per prefill pass (longer prompts take several passes)
+constexpr int kPfMaxSplits = 16;
 
 static int pf_alloc(MuyoModel* m)
 {
@@ -1579,8 +1582,9 @@ static int pf_alloc(MuyoModel* m)
         return MUYO_OK;
     const Shape& s = m->s;
     const size_t wide = (size_t)std::max(std::max(s.hidden, s.q_dim), s.ffn);
-    const size_t f32 = (size_t)kPfCap * ((size_t)s.hidden + s.qkv_rows + 2 * (size_t)s.q_dim + 2 * (size_t)s.ffn);
-    const size_t bytes = f32 * sizeof(float) + 2 * (size_t)kPfCap * wide * sizeof(__half) + 256;
+    const size_t part = (size_t)kPfMaxSplits * kPfCap * std::max(s.qkv_rows, s.hidden);
+    const size_t f32 = (size_t)kPfCap * ((size_t)s.hidden + s.qkv_rows + 2 * (size_t)s.q_dim + 2 * (size_t)s.ffn) + part;
+    const size_t bytes = f32 * sizeof(float) + 2 * (size_t)kPfCap * wide * sizeof(__half) + 256 * 9;
     if (cudaMalloc(&m->pf_buf, bytes) != cudaSuccess) {
         cudaGetLastError();
         m->pf_buf = nullptr;
@@ -1600,7 +1604,9 @@ static int pf_alloc(MuyoModel* m)
     m->pf_gu = reinterpret_cast<float*>(take((size_t)kPfCap * 2 * s.ffn * 4));
     m->pf_hi = reinterpret_cast<__half*>(take((size_t)kPfCap * wide * 2));
     m->pf_lo = reinterpret_cast<__half*>(take((size_t)kPfCap * wide * 2));
-    if ((size_t)(p - m->pf_buf) > bytes + 256 * 8) {
+    m->pf_part = reinterpret_cast<float*>(take(part * 4));
+    m->pf_part_floats = part;
+    if ((size_t)(p - m->pf_buf) > bytes + 256 * 9) {
         set_error("prefill: buffer plan overflow");
         return MUYO_EINVAL;
     }
@@ -1609,13 +1615,32 @@ static int pf_alloc(MuyoModel* m)
     return MUYO_OK;
 }
 
+// K-range splits of a prefill GEMM: enough CTAs for two per SM, each range at least 4 stages long.
+static int pf_splits(int N, int K, int T)
+{
+    const int ctas = ((N + kPfBM - 1) / kPfBM) * ((T + kPfBN - 1) / kPfBN);
+    const int stages = (K + kPfBK - 1) / kPfBK;
+    int S = (2 * sm_count() + ctas - 1) / ctas;
+    S = std::min(S, std::max(1, stages / 4));
+    return std::max(1, std::min(S, kPfMaxSplits));
+}
+
+// part: S * T * N floats when pf_splits > 1 (the prefill workspace).
 template <int EPI>
 static int pf_gemm(const __half* w0, const __half* w1, int n_split, int N, int K, int T, const __half* xhi,
-                   const __half* xlo, int ldx, float* y, int ldy, const float* bias, cudaStream_t st)
+                   const __half* xlo, int ldx, float* y, int ldy, const float* bias, float* part, size_t part_floats,
+                   cudaStream_t st)
 {
     PfGemm g{w0, w1 ? w1 : w0, n_split, N, K, T, xhi, xlo, ldx, y, ldy, bias};
-    const dim3 grid((N + kPfBM - 1) / kPfBM, (T + kPfBN - 1) / kPfBN);
-    MUYO_CUDA_TRY(launch_kernel(k_pf_gemm<EPI>, grid, dim3(kPfThreads), kPfGemmSmem, st, true, g));
+    int S = pf_splits(N, K, T);
+    if ((size_t)S * T * N > part_floats)
+        S = 1;
+    const dim3 grid((N + kPfBM - 1) / kPfBM, (T + kPfBN - 1) / kPfBN, S);
+    MUYO_CUDA_TRY(launch_kernel(k_pf_gemm<EPI>, grid, dim3(kPfThreads), kPfGemmSmem, st, true, g, part));
+    if (S > 1) {
+        const int blocks = (int)std::min<size_t>(((size_t)T * N + 255) / 256, (size_t)sm_count() * 8);
+        MUYO_CUDA_TRY(launch_kernel(k_pf_reduce<EPI>, dim3(blocks), dim3(256), 0, st, true, g, (const float*)part, S));
+    }
     return MUYO_OK;
 }
 
@@ -1664,22 +1689,24 @@ static int prefill_run(MuyoModel* m, int p0, int n, cudaStream_t st)
             MUYO_CUDA_TRY(launch_kernel(k_pf_norm_split, dim3(T), dim3(256), 0, st, true, (const float*)m->pf_x, H,
                                         w.attn_norm, s.eps, H, m->pf_hi, m->pf_lo, ldh));
             if ((rc = pf_gemm<PF_BIAS>(w.wqkv, nullptr, s.qkv_rows, s.qkv_rows, H, T, m->pf_hi, m->pf_lo, ldh,
-                                       m->pf_qkv, s.qkv_rows, w.bqkv, st)))
+                                       m->pf_qkv, s.qkv_rows, w.bqkv, m->pf_part, m->pf_part_floats, st)))
                 return rc;
             if ((rc = pf_attention(s, m->pf_q, m->pf_att, m->pf_qkv, kc, vc, pos0, T, st)))
                 return rc;
             MUYO_CUDA_TRY(launch_kernel(k_pf_split, dim3(T), dim3(256), 0, st, true, (const float*)m->pf_att, QD, QD,
                                         m->pf_hi, m->pf_lo, ldh));
-            if ((rc = pf_gemm<PF_ADD>(w.wo, nullptr, H, H, QD, T, m->pf_hi, m->pf_lo, ldh, m->pf_x, H, nullptr, st)))
+            if ((rc = pf_gemm<PF_ADD>(w.wo, nullptr, H, H, QD, T, m->pf_hi, m->pf_lo, ldh, m->pf_x, H, nullptr, m->pf_part,
+                                      m->pf_part_floats, st)))
                 return rc;
             MUYO_CUDA_TRY(launch_kernel(k_pf_norm_split, dim3(T), dim3(256), 0, st, true, (const float*)m->pf_x, H,
                                         w.ffn_norm, s.eps, H, m->pf_hi, m->pf_lo, ldh));
             if ((rc = pf_gemm<PF_STORE>(w.wgate, w.wup, F, 2 * F, H, T, m->pf_hi, m->pf_lo, ldh, m->pf_gu, 2 * F,
-                                        nullptr, st)))
+                                        nullptr, m->pf_part, m->pf_part_floats, st)))
                 return rc;
             MUYO_CUDA_TRY(launch_kernel(k_pf_swiglu_split, dim3(T), dim3(256), 0, st, true, (const float*)m->pf_gu, F,
                                         m->pf_hi, m->pf_lo, ldh));
-            if ((rc = pf_gemm<PF_ADD>(w.wdown, nullptr, H, H, F, T, m->pf_hi, m->pf_lo, ldh, m->pf_x, H, nullptr, st)))
+            if ((rc = pf_gemm<PF_ADD>(w.wdown, nullptr, H, H, F, T, m->pf_hi, m->pf_lo, ldh, m->pf_x, H, nullptr, m->pf_part,
+                                      m->pf_part_floats, st)))
                 return rc;
         }
     }
@@ -1919,7 +1946,9 @@ extern "C" size_t muyo_cuda_mat_mul_f16_workspace_size(const MuyoMatMulParams* p
 {
     if (!p)
         return 0;
-    return 2 * (size_t)p->tokens * ((size_t)p->ncols + 7) / 8 * 8 * sizeof(__half) + 256;
+    const size_t halves = 2 * (size_t)p->tokens * (((size_t)p->ncols + 7) / 8 * 8);
+    const size_t part = (size_t)pf_splits((int)p->rows, (int)p->ncols, (int)p->tokens) * p->tokens * p->rows;
+    return halves * sizeof(__half) + 256 + part * sizeof(float);
 }
 
 extern "C" int muyo_cuda_mat_mul_f16(const MuyoMatMulParams* p, const void* a, const float* x, float* y,
@@ -1943,17 +1972,20 @@ extern "C" int muyo_cuda_mat_mul_f16(const MuyoMatMulParams* p, const void* a, c
     const int ldh = (K + 7) / 8 * 8;
     __half* hi = static_cast<__half*>(workspace);
     __half* lo = hi + (size_t)T * ldh;
+    const size_t part_off = ((size_t)2 * T * ldh * sizeof(__half) + 255) / 256 * 256;
+    float* part = reinterpret_cast<float*>(static_cast<char*>(workspace) + part_off);
+    const size_t part_floats = (workspace_bytes - part_off) / sizeof(float);
     for (auto k : {k_pf_gemm<PF_STORE>, k_pf_gemm<PF_BIAS>, k_pf_gemm<PF_ADD>})
         MUYO_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPfGemmSmem));
     MUYO_CUDA_TRY(launch_kernel(k_pf_split, dim3(T), dim3(256), 0, st, true, x, ldx, K, hi, lo, ldh));
     const __half* w = static_cast<const __half*>(a);
     int rc;
     if (p->flags & MUYO_MATMUL_BIAS)
-        rc = pf_gemm<PF_BIAS>(w, nullptr, N, N, K, T, hi, lo, ldh, y, ldy, bias, st);
+        rc = pf_gemm<PF_BIAS>(w, nullptr, N, N, K, T, hi, lo, ldh, y, ldy, bias, part, part_floats, st);
     else if (p->flags & MUYO_MATMUL_ACCUMULATE)
-        rc = pf_gemm<PF_ADD>(w, nullptr, N, N, K, T, hi, lo, ldh, y, ldy, nullptr, st);
+        rc = pf_gemm<PF_ADD>(w, nullptr, N, N, K, T, hi, lo, ldh, y, ldy, nullptr, part, part_floats, st);
     else
-        rc = pf_gemm<PF_STORE>(w, nullptr, N, N, K, T, hi, lo, ldh, y, ldy, nullptr, st);
+        rc = pf_gemm<PF_STORE>(w, nullptr, N, N, K, T, hi, lo, ldh, y, ldy, nullptr, part, part_floats, st);
     if (rc)
         return rc;
     MUYO_LAUNCH_CHECK();

@@ -85,38 +85,52 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], unsigned a0, unsigned a
 
 // One CTA: 64 feature rows x 64 positions. Warp w owns rows [16w, 16w + 16) of the tile and all 64
 // positions (8 accumulator fragments of 16 x 8). K advances 64 at a time through a 3-stage cp.async
-// ring; chunks past N, T or K are zero-filled (K is a multiple of 8).
+// ring; chunks past N, T or K are zero-filled (K is a multiple of 8). With gridDim.z = S > 1 the CTA
+// covers the z-th of S contiguous ranges of K stages and stores its raw sums to part[z][t][n]
+// (k_pf_reduce adds the S ranges in order and applies the epilogue).
 template <int EPI>
-__global__ void __launch_bounds__(kPfThreads) k_pf_gemm(PfGemm g)
+__global__ void __launch_bounds__(kPfThreads, 2) k_pf_gemm(PfGemm g, float* part)
 {
     extern __shared__ __align__(16) __half pf_smem[];
     pdl_wait();
     pdl_trigger();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int n0 = blockIdx.x * kPfBM, t0 = blockIdx.y * kPfBN;
-    const int nk = (g.K + kPfBK - 1) / kPfBK;
+    const int nk_all = (g.K + kPfBK - 1) / kPfBK, S = gridDim.z, z = blockIdx.z;
+    const int kt0 = (int)((long long)nk_all * z / S), kt1 = (int)((long long)nk_all * (z + 1) / S);
+    const int nk = kt1 - kt0;
     const unsigned sbase = (unsigned)__cvta_generic_to_shared(pf_smem);
 
+    // This thread's 12 chunks of a stage (3 tiles x 64 rows x 8 chunks over 128 threads): chunk
+    // c = tid + 128 i is tile i / 4, row (c >> 3) & 63, 16-byte column c & 7; its source row is fixed.
+    const __half* src_row[12];
+    bool row_ok[12];
+    unsigned dst_off[12];
+    int kcol[12];
+#pragma unroll
+    for (int i = 0; i < 12; ++i) {
+        const int c = tid + i * kPfThreads, tile = i >> 2, r = (c >> 3) & 63, ch = c & 7;
+        dst_off[i] = (unsigned)((tile * 64 * kPfLD + r * kPfLD + ch * 8) * 2);
+        kcol[i] = ch * 8;
+        if (tile == 0) {
+            const int n = n0 + r;
+            row_ok[i] = n < g.N;
+            src_row[i] = !row_ok[i] ? g.w0 : (n < g.n_split ? g.w0 + (size_t)n * g.K : g.w1 + (size_t)(n - g.n_split) * g.K);
+        } else {
+            const int t = t0 + r;
+            const __half* xb = tile == 1 ? g.xhi : g.xlo;
+            row_ok[i] = t < g.T;
+            src_row[i] = row_ok[i] ? xb + (size_t)t * g.ldx : xb;
+        }
+    }
     auto load_stage = [&](int buf, int kt) {
         const int k0 = kt * kPfBK;
         const unsigned st = sbase + (unsigned)(buf * kPfStageHalfs * 2);
-        for (int c = tid; c < 3 * 64 * 8; c += kPfThreads) {  // 3 tiles x 64 rows x 8 16-byte chunks
-            const int tile = c >> 9, r = (c >> 3) & 63, ch = c & 7;
-            const int k = k0 + ch * 8;
-            const unsigned dst = st + (unsigned)((tile * 64 * kPfLD + r * kPfLD + ch * 8) * 2);
-            if (tile == 0) {
-                const int n = n0 + r;
-                const bool ok = n < g.N && k < g.K;
-                const __half* src = g.w0;
-                if (ok)
-                    src = n < g.n_split ? g.w0 + (size_t)n * g.K + k : g.w1 + (size_t)(n - g.n_split) * g.K + k;
-                cp_async16(dst, src, ok);
-            } else {
-                const int t = t0 + r;
-                const bool ok = t < g.T && k < g.K;
-                const __half* xb = tile == 1 ? g.xhi : g.xlo;
-                cp_async16(dst, ok ? xb + (size_t)t * g.ldx + k : xb, ok);
-            }
+#pragma unroll
+        for (int i = 0; i < 12; ++i) {
+            const int k = k0 + kcol[i];
+            const bool ok = row_ok[i] && k < g.K;
+            cp_async16(st + dst_off[i], ok ? src_row[i] + k : src_row[i], ok);
         }
     };
 
@@ -129,20 +143,20 @@ __global__ void __launch_bounds__(kPfThreads) k_pf_gemm(PfGemm g)
 #pragma unroll
     for (int s = 0; s < kPfStages - 1; ++s) {
         if (s < nk)
-            load_stage(s, s);
+            load_stage(s, kt0 + s);
         cp_async_commit();
     }
     const int mat = lane >> 3;
-    for (int kt = 0; kt < nk; ++kt) {
+    for (int i = 0; i < nk; ++i) {
         cp_async_wait<kPfStages - 2>();
-        __syncthreads();  // stage kt is visible, and every warp is done with the buffer refilled next
+        __syncthreads();  // stage i is visible, and every warp is done with the buffer refilled next
         {
-            const int nxt = kt + kPfStages - 1;
+            const int nxt = i + kPfStages - 1;
             if (nxt < nk)
-                load_stage(nxt % kPfStages, nxt);
+                load_stage(nxt % kPfStages, kt0 + nxt);
             cp_async_commit();
         }
-        const unsigned ws = sbase + (unsigned)((kt % kPfStages) * kPfStageHalfs * 2);
+        const unsigned ws = sbase + (unsigned)((i % kPfStages) * kPfStageHalfs * 2);
         const unsigned xh = ws + 64 * kPfLD * 2, xl = ws + 2 * 64 * kPfLD * 2;
 #pragma unroll
         for (int kk = 0; kk < kPfBK; kk += 16) {
@@ -151,17 +165,22 @@ __global__ void __launch_bounds__(kPfThreads) k_pf_gemm(PfGemm g)
                 const int r = warp * 16 + (mat & 1) * 8 + (lane & 7), c = kk + (mat >> 1) * 8;
                 ldsm_x4(ws + (unsigned)((r * kPfLD + c) * 2), a0, a1, a2, a3);
             }
+            unsigned bh[8][2], bl[8][2];
 #pragma unroll
             for (int j2 = 0; j2 < 4; ++j2) {  // positions 16*j2 .. +15: two 8-wide fragments
                 const int r = j2 * 16 + (mat >> 1) * 8 + (lane & 7), c = kk + (mat & 1) * 8;
-                unsigned h0, h1, h2, h3, l0, l1, l2, l3;
-                ldsm_x4(xh + (unsigned)((r * kPfLD + c) * 2), h0, h1, h2, h3);
-                ldsm_x4(xl + (unsigned)((r * kPfLD + c) * 2), l0, l1, l2, l3);
-                mma_16816(acc[2 * j2], a0, a1, a2, a3, h0, h1);
-                mma_16816(acc[2 * j2], a0, a1, a2, a3, l0, l1);
-                mma_16816(acc[2 * j2 + 1], a0, a1, a2, a3, h2, h3);
-                mma_16816(acc[2 * j2 + 1], a0, a1, a2, a3, l2, l3);
+                ldsm_x4(xh + (unsigned)((r * kPfLD + c) * 2), bh[2 * j2][0], bh[2 * j2][1], bh[2 * j2 + 1][0],
+                        bh[2 * j2 + 1][1]);
+                ldsm_x4(xl + (unsigned)((r * kPfLD + c) * 2), bl[2 * j2][0], bl[2 * j2][1], bl[2 * j2 + 1][0],
+                        bl[2 * j2 + 1][1]);
             }
+            // eight independent accumulators between two products into the same one
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                mma_16816(acc[j], a0, a1, a2, a3, bh[j][0], bh[j][1]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                mma_16816(acc[j], a0, a1, a2, a3, bl[j][0], bl[j][1]);
         }
     }
     cp_async_wait<0>();
@@ -174,15 +193,40 @@ __global__ void __launch_bounds__(kPfThreads) k_pf_gemm(PfGemm g)
             const int n = n0 + warp * 16 + gr + (e >> 1) * 8;
             const int t = t0 + j * 8 + tq * 2 + (e & 1);
             if (n < g.N && t < g.T) {
-                float* yp = g.y + (size_t)t * g.ldy + n;
-                float v = acc[j][e];
-                if (EPI == PF_BIAS)
-                    v = v + g.bias[n];
-                if (EPI == PF_ADD)
-                    v = *yp + v;
-                *yp = v;
+                if (S > 1) {
+                    part[((size_t)z * g.T + t) * g.N + n] = acc[j][e];
+                } else {
+                    float* yp = g.y + (size_t)t * g.ldy + n;
+                    float v = acc[j][e];
+                    if (EPI == PF_BIAS)
+                        v = v + g.bias[n];
+                    if (EPI == PF_ADD)
+                        v = *yp + v;
+                    *yp = v;
+                }
             }
         }
+}
+
+// y[t][n] = epilogue(part[0][t][n] + part[1][t][n] + ... + part[S-1][t][n]), left to right.
+template <int EPI>
+__global__ void __launch_bounds__(256) k_pf_reduce(PfGemm g, const float* __restrict__ part, int S)
+{
+    pdl_wait();
+    pdl_trigger();
+    const size_t total = (size_t)g.T * g.N;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int t = (int)(i / g.N), n = (int)(i % g.N);
+        float v = part[i];
+        for (int z = 1; z < S; ++z)
+            v += part[(size_t)z * total + i];
+        float* yp = g.y + (size_t)t * g.ldy + n;
+        if (EPI == PF_BIAS)
+            v = v + g.bias[n];
+        if (EPI == PF_ADD)
+            v = *yp + v;
+        *yp = v;
+    }
 }
 
 __device__ __forceinline__ void split_store(__half* hi, __half* lo, float4 v)
