@@ -80,7 +80,45 @@ __device__ __forceinline__ void stage_x_split(float* xs, const float* x, int n, 
     }
 }
 
-template <int ROWS, int U, int KSPLIT>
+// warp_gemv_f16_range with x read from global memory (float4 pairs 2c, 2c + 1 of chunk c; L1-resident
+// after the first warp of the SM) instead of the staged copy; the same products in the same order.
+template <int ROWS, int U>
+__device__ __forceinline__ void warp_gemv_f16_range_xg(const GemvArgs<ROWS, U, 1>& a, int row0, int nvalid,
+                                                       const float* __restrict__ x, int c_begin, int c_end, int lane,
+                                                       float (&acc)[1][ROWS])
+{
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    const uint4* rowp[ROWS];
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r)
+        rowp[r] = reinterpret_cast<const uint4*>(a.w[0] + (size_t)(row0 + (r < nvalid ? r : 0)) * a.ldw);
+    for (int base = c_begin; base < c_end; base += WARP * U) {
+        uint4 wv[ROWS][U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int c = base + lane + WARP * u;
+#pragma unroll
+            for (int r = 0; r < ROWS; ++r)
+                wv[r][u] = c < c_end ? ld_stream16(rowp[r] + c) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int c = base + lane + WARP * u;
+            if (c < c_end) {
+                const float4 xa = __ldg(x4 + 2 * c);
+                const float4 xb = __ldg(x4 + 2 * c + 1);
+#pragma unroll
+                for (int r = 0; r < ROWS; ++r)
+                    acc[0][r] = dot_chunk(wv[r][u], xa, xb, acc[0][r]);
+            }
+        }
+    }
+}
+
+// XG: x is read from global memory (K a multiple of 8, x 16-byte aligned, one batch, small weights):
+// the first weight and x loads leave together, with no staging round trip and no block barrier
+// before them.
+template <int ROWS, int U, int KSPLIT, bool XG>
 __global__ void __launch_bounds__(kThreads) k_mat_vec_f16(MatVecDev p, const __half* __restrict__ A,
                                                           const float* __restrict__ B, float* __restrict__ D,
                                                           const float* __restrict__ f0, const float* __restrict__ f1)
@@ -103,8 +141,10 @@ __global__ void __launch_bounds__(kThreads) k_mat_vec_f16(MatVecDev p, const __h
                          min(block_rows, p.rows - (int)blockIdx.x * block_rows));
     pdl_wait();  // the L2 prefetch above is only a hint; every read of A, x or D comes after this wait
     pdl_trigger();
-    stage_x_split(xs, Bb, p.ncols, p.k8);
-    __syncthreads();
+    if (!XG) {
+        stage_x_split(xs, Bb, p.ncols, p.k8);
+        __syncthreads();
+    }
     const int c_begin = (int)((long long)p.k8 * ks / KSPLIT), c_end = (int)((long long)p.k8 * (ks + 1) / KSPLIT);
     GemvArgs<ROWS, U, 1> ga{{Ab}, (size_t)p.stride_a};
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {  // the same trip count in every warp
@@ -118,9 +158,13 @@ __global__ void __launch_bounds__(kThreads) k_mat_vec_f16(MatVecDev p, const __h
         for (int r = 0; r < ROWS; ++r)
             acc[0][r] = 0.0f;
         if (nvalid > 0) {
-            warp_gemv_f16_range<ROWS, U, 1>(ga, row0, nvalid, xs, p.k8, c_begin, c_end, lane, acc);
-            if (ks == KSPLIT - 1)  // columns past the last full chunk
-                warp_gemv_f16_tail<ROWS, 1>(ga.w, ga.ldw, row0, nvalid, xs, p.k8, p.ncols, lane, acc);
+            if (XG) {
+                warp_gemv_f16_range_xg<ROWS, U>(ga, row0, nvalid, Bb, c_begin, c_end, lane, acc);
+            } else {
+                warp_gemv_f16_range<ROWS, U, 1>(ga, row0, nvalid, xs, p.k8, c_begin, c_end, lane, acc);
+                if (ks == KSPLIT - 1)  // columns past the last full chunk
+                    warp_gemv_f16_tail<ROWS, 1>(ga.w, ga.ldw, row0, nvalid, xs, p.k8, p.ncols, lane, acc);
+            }
             warp_reduce_acc<ROWS, 1>(acc);
         }
         if (KSPLIT > 1) {
@@ -293,20 +337,35 @@ static int launch_mat_vec(bool f16, const MatVecDev& q, int batches, const void*
         // Loads in flight per lane grow with K so that a warp covers a long row in few round trips:
         // U chunks of 16 bytes per row per lane (each lane still adds its chunks in column order).
         const int lane_chunks = q.k8 / ksplit / 32;
-        auto k = k_mat_vec_f16<ROWS, 4, 1>;
-        if (ksplit == 4)
-            k = lane_chunks >= 8 ? k_mat_vec_f16<ROWS, 8, 4> : k_mat_vec_f16<ROWS, 4, 4>;
-        else if (ksplit == 2)
-            k = lane_chunks >= 8 ? k_mat_vec_f16<ROWS, 8, 2> : k_mat_vec_f16<ROWS, 4, 2>;
-        else if (lane_chunks >= 8)
-            k = k_mat_vec_f16<ROWS, 8, 1>;
-        MUYO_CUDA_TRY(set_smem(k, smem));
+        // Below 16 MB of weights a call is mostly its fixed chain, which reading x from global memory
+        // shortens (896x4864: 4.98 -> 4.05 us); for streaming shapes the x reads through L1 cost more
+        // than the staging round trip they save (4096x4096: 0.68 -> 0.54 of peak), so x is staged.
+        const bool xg = batches == 1 && q.ncols % 8 == 0 && aligned16(b) &&
+                        (size_t)q.rows * q.ncols * sizeof(__half) < ((size_t)16 << 20);
+        auto k = k_mat_vec_f16<ROWS, 4, 1, false>;
+        if (xg) {
+            if (ksplit == 4)
+                k = lane_chunks >= 8 ? k_mat_vec_f16<ROWS, 8, 4, true> : k_mat_vec_f16<ROWS, 4, 4, true>;
+            else if (ksplit == 2)
+                k = lane_chunks >= 8 ? k_mat_vec_f16<ROWS, 8, 2, true> : k_mat_vec_f16<ROWS, 4, 2, true>;
+            else
+                k = lane_chunks >= 8 ? k_mat_vec_f16<ROWS, 8, 1, true> : k_mat_vec_f16<ROWS, 4, 1, true>;
+        } else {
+            if (ksplit == 4)
+                k = lane_chunks >= 8 ? k_mat_vec_f16<ROWS, 8, 4, false> : k_mat_vec_f16<ROWS, 4, 4, false>;
+            else if (ksplit == 2)
+                k = lane_chunks >= 8 ? k_mat_vec_f16<ROWS, 8, 2, false> : k_mat_vec_f16<ROWS, 4, 2, false>;
+            else if (lane_chunks >= 8)
+                k = k_mat_vec_f16<ROWS, 8, 1, false>;
+        }
+        const size_t smem_k = xg ? 0 : smem;
+        MUYO_CUDA_TRY(set_smem(k, smem_k));
         // CTAs stride over the row tiles: the grid stops at what is resident at once
         int per_sm = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, smem) == cudaSuccess && per_sm > 0 &&
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, smem_k) == cudaSuccess && per_sm > 0 &&
             batches == 1 && grid.x > (unsigned)(per_sm * sm_count()))
             grid.x = per_sm * sm_count();
-        MUYO_CUDA_TRY(launch_kernel(k, dim3(grid), dim3(kThreads), smem, s, true, q, static_cast<const __half*>(a), b, d, f0, f1));
+        MUYO_CUDA_TRY(launch_kernel(k, dim3(grid), dim3(kThreads), smem_k, s, true, q, static_cast<const __half*>(a), b, d, f0, f1));
     } else {
         auto k = k_mat_vec_f32<ROWS, 4>;
         MUYO_CUDA_TRY(set_smem(k, smem));
