@@ -311,17 +311,22 @@ int muyo_model_set_option(MuyoModel* m, const char* key, int value);
  * attention kernel over the cache), writing the same KV cache; the decode step then runs from the
  * prompt's last position. The reference feeds a prompt one position at a time (src/FullModel.cpp:
  * 1174-1181): results agree to float rounding, not bit for bit (the projections sum in another
- * order). No logits are formed for the batched positions. */
+ * order). No logits are formed for the batched positions. Option "prefill_tc" = 1 runs the
+ * projections on the tcgen05 GEMM (see muyo_cuda_mat_mul_f16). */
 
 /* ---- batched F16 GEMM (the prefill projections) ---------------------------------------------------
  * y[t][n] = sum_k A[n][k] * x[t][k] for n < rows, t < tokens: ggml's mul_mm with src0 = A (F16,
  * [rows][ncols] row-major) and src1 = x (F32, tokens rows of stride_x), the batched counterpart of
  * muyo_cuda_mat_vec_f16 (the reference's shaders/llama/mul_mm.comp, which its engine never
  * dispatches). BIAS adds bias[n]; ACCUMULATE adds to y. x enters the tensor cores as two F16 halves
- * (hi = f16(x), lo = f16(x - hi)) with F32 accumulation. ncols a multiple of 8; a, x and the
- * workspace 16-byte aligned. */
+ * (hi = f16(x), lo = f16(x - hi)) with F32 accumulation: warp-level mma.sync on 64 x 64 tiles, or
+ * with MUYO_MATMUL_TCGEN05 tcgen05.mma (tensor-memory accumulator, 128 x 64 tiles; slower at the
+ * 0.5B layer's sizes while its tiles are fed by cp.async). ncols a multiple of 8; a, x and the
+ * workspace 16-byte aligned. The kernels' waits are bounded (2 s); one that expired leaves y
+ * unspecified (the model's prefill reports it as MUYO_ETIMEOUT). */
 #define MUYO_MATMUL_BIAS 0x1u
 #define MUYO_MATMUL_ACCUMULATE 0x2u
+#define MUYO_MATMUL_TCGEN05 0x4u /* the tcgen05 kernel instead of the warp-level mma.sync one (the default) */
 typedef struct MuyoMatMulParams {
     uint32_t ncols;    /* K */
     uint32_t rows;     /* N: output features */

@@ -19,7 +19,7 @@ MUYO_OK = 0
 ERRORS = {-1: "MUYO_EINVAL", -2: "MUYO_ECUDA", -3: "MUYO_ETIMEOUT", -4: "MUYO_ENOMEM", -5: "MUYO_EUNSUPPORTED",
           -6: "MUYO_ESTATE"}
 MATVEC_BIAS0, MATVEC_BIAS1, MATVEC_SCALE0, MATVEC_SCALE1 = 1, 2, 4, 8
-MATMUL_BIAS, MATMUL_ACCUMULATE = 1, 2
+MATMUL_BIAS, MATMUL_ACCUMULATE, MATMUL_TCGEN05 = 1, 2, 4
 GLU_HALVES, GLU_SWAPPED, GLU_SPLIT = 0, 1, 2
 ROPE_NORMAL, ROPE_NEOX = 0, 2
 KV_F32, KV_F16 = 0, 1

@@ -20,7 +20,6 @@
 
 #include "attention.cuh"
 #include "common.cuh"
-#include "prefill.cuh"
 
 // sampler.cu: parameter check and launch of the device sampler (gate = the model's {step,
 // prompt_end, total}, see k_sample).
@@ -48,6 +47,7 @@ static_assert(offsetof(Control, prompt_end) == 4 && offsetof(Control, total) == 
 }  // namespace muyo
 
 #include "decode_persistent.cuh"
+#include "prefill.cuh"  // after the mbarrier helpers it uses
 
 namespace muyo {
 
@@ -859,6 +859,7 @@ struct MuyoModel {
     MuyoSamplerParams sp{};         // its parameters (baked into the recorded graph)
     void* rng = nullptr;            // its mt19937_64 state, followed by the last sampled id (int32)
     bool prefill = false;           // generate: the prompt's positions but the last in one batched pass
+    bool pf_tc = false;             // prefill projections on tcgen05 (default: the warp-level mma.sync kernel)
     char* pf_buf = nullptr;         // batched-prefill activations for kPfCap positions
     float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_att = nullptr, *pf_gu = nullptr;
     float* pf_part = nullptr;  // split-K partial sums
@@ -1565,7 +1566,9 @@ static int check_device_error(MuyoModel* m, cudaStream_t st)
     MUYO_CUDA_TRY(cudaStreamSynchronize(st));
     if (e != 0) {
         MUYO_CUDA_TRY(cudaMemsetAsync(m->err, 0, sizeof(int), st));
-        set_error("decode: a bounded device wait expired (error word %d: 3 persistent kernel, 4 weight-tile copy)", e);
+        set_error("decode: a bounded device wait expired (error word %d: 3 persistent kernel, 4 weight-tile copy, "
+                  "6 prefill tensor-core pipeline)",
+                  e);
         return MUYO_ETIMEOUT;
     }
     return MUYO_OK;
@@ -1612,31 +1615,42 @@ static int pf_alloc(MuyoModel* m)
     }
     for (auto k : {k_pf_gemm<PF_STORE>, k_pf_gemm<PF_BIAS>, k_pf_gemm<PF_ADD>})
         MUYO_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPfGemmSmem));
+    for (auto k : {k_pf_gemm_tc<PF_STORE>, k_pf_gemm_tc<PF_BIAS>, k_pf_gemm_tc<PF_ADD>})
+        MUYO_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem));
     return MUYO_OK;
 }
 
 // K-range splits of a prefill GEMM: enough CTAs for two per SM, each range at least 4 stages long.
-static int pf_splits(int N, int K, int T)
+// tc: the tensor-core kernel's 128-row tiles (else the warp-MMA kernel's 64-row tiles).
+static int pf_splits(int N, int K, int T, bool tc = false)
 {
-    const int ctas = ((N + kPfBM - 1) / kPfBM) * ((T + kPfBN - 1) / kPfBN);
+    const int bm = tc ? kTcBM : kPfBM;
+    const int ctas = ((N + bm - 1) / bm) * ((T + kPfBN - 1) / kPfBN);
     const int stages = (K + kPfBK - 1) / kPfBK;
     int S = (2 * sm_count() + ctas - 1) / ctas;
     S = std::min(S, std::max(1, stages / 4));
     return std::max(1, std::min(S, kPfMaxSplits));
 }
 
-// part: S * T * N floats when pf_splits > 1 (the prefill workspace).
+// part: S * T * N floats when pf_splits > 1 (the prefill workspace). tc: the tcgen05 kernel, else the
+// warp-level mma.sync kernel (faster at these sizes while tcgen05's tiles are fed by cp.async from
+// every thread). err: the bounded waits' error word (may be null).
 template <int EPI>
 static int pf_gemm(const __half* w0, const __half* w1, int n_split, int N, int K, int T, const __half* xhi,
                    const __half* xlo, int ldx, float* y, int ldy, const float* bias, float* part, size_t part_floats,
-                   cudaStream_t st)
+                   cudaStream_t st, bool tc = false, int* err = nullptr)
 {
     PfGemm g{w0, w1 ? w1 : w0, n_split, N, K, T, xhi, xlo, ldx, y, ldy, bias};
-    int S = pf_splits(N, K, T);
+    int S = pf_splits(N, K, T, tc);
     if ((size_t)S * T * N > part_floats)
         S = 1;
-    const dim3 grid((N + kPfBM - 1) / kPfBM, (T + kPfBN - 1) / kPfBN, S);
-    MUYO_CUDA_TRY(launch_kernel(k_pf_gemm<EPI>, grid, dim3(kPfThreads), kPfGemmSmem, st, true, g, part));
+    if (tc) {
+        const dim3 grid((N + kTcBM - 1) / kTcBM, (T + kTcBN - 1) / kTcBN, S);
+        MUYO_CUDA_TRY(launch_kernel(k_pf_gemm_tc<EPI>, grid, dim3(kTcThreads), kTcSmem, st, true, g, part, err));
+    } else {
+        const dim3 grid((N + kPfBM - 1) / kPfBM, (T + kPfBN - 1) / kPfBN, S);
+        MUYO_CUDA_TRY(launch_kernel(k_pf_gemm<EPI>, grid, dim3(kPfThreads), kPfGemmSmem, st, true, g, part));
+    }
     if (S > 1) {
         const int blocks = (int)std::min<size_t>(((size_t)T * N + 255) / 256, (size_t)sm_count() * 8);
         MUYO_CUDA_TRY(launch_kernel(k_pf_reduce<EPI>, dim3(blocks), dim3(256), 0, st, true, g, (const float*)part, S));
@@ -1689,24 +1703,25 @@ static int prefill_run(MuyoModel* m, int p0, int n, cudaStream_t st)
             MUYO_CUDA_TRY(launch_kernel(k_pf_norm_split, dim3(T), dim3(256), 0, st, true, (const float*)m->pf_x, H,
                                         w.attn_norm, s.eps, H, m->pf_hi, m->pf_lo, ldh));
             if ((rc = pf_gemm<PF_BIAS>(w.wqkv, nullptr, s.qkv_rows, s.qkv_rows, H, T, m->pf_hi, m->pf_lo, ldh,
-                                       m->pf_qkv, s.qkv_rows, w.bqkv, m->pf_part, m->pf_part_floats, st)))
+                                       m->pf_qkv, s.qkv_rows, w.bqkv, m->pf_part, m->pf_part_floats, st, m->pf_tc,
+                                       m->err)))
                 return rc;
             if ((rc = pf_attention(s, m->pf_q, m->pf_att, m->pf_qkv, kc, vc, pos0, T, st)))
                 return rc;
             MUYO_CUDA_TRY(launch_kernel(k_pf_split, dim3(T), dim3(256), 0, st, true, (const float*)m->pf_att, QD, QD,
                                         m->pf_hi, m->pf_lo, ldh));
             if ((rc = pf_gemm<PF_ADD>(w.wo, nullptr, H, H, QD, T, m->pf_hi, m->pf_lo, ldh, m->pf_x, H, nullptr, m->pf_part,
-                                      m->pf_part_floats, st)))
+                                      m->pf_part_floats, st, m->pf_tc, m->err)))
                 return rc;
             MUYO_CUDA_TRY(launch_kernel(k_pf_norm_split, dim3(T), dim3(256), 0, st, true, (const float*)m->pf_x, H,
                                         w.ffn_norm, s.eps, H, m->pf_hi, m->pf_lo, ldh));
             if ((rc = pf_gemm<PF_STORE>(w.wgate, w.wup, F, 2 * F, H, T, m->pf_hi, m->pf_lo, ldh, m->pf_gu, 2 * F,
-                                        nullptr, m->pf_part, m->pf_part_floats, st)))
+                                        nullptr, m->pf_part, m->pf_part_floats, st, m->pf_tc, m->err)))
                 return rc;
             MUYO_CUDA_TRY(launch_kernel(k_pf_swiglu_split, dim3(T), dim3(256), 0, st, true, (const float*)m->pf_gu, F,
                                         m->pf_hi, m->pf_lo, ldh));
             if ((rc = pf_gemm<PF_ADD>(w.wdown, nullptr, H, H, F, T, m->pf_hi, m->pf_lo, ldh, m->pf_x, H, nullptr, m->pf_part,
-                                      m->pf_part_floats, st)))
+                                      m->pf_part_floats, st, m->pf_tc, m->err)))
                 return rc;
         }
     }
@@ -1930,6 +1945,11 @@ extern "C" int muyo_model_set_option(MuyoModel* m, const char* key, int value)
         m->prefill = value != 0;
         return MUYO_OK;
     }
+    if (k == "prefill_tc") {
+        MUYO_REQUIRE(value == 0 || value == 1, "set_option: prefill_tc must be 0 or 1");
+        m->pf_tc = value != 0;
+        return MUYO_OK;
+    }
     if (k == "pdl") {
         MUYO_REQUIRE(value == 0 || value == 1, "set_option: pdl must be 0 or 1");
         MUYO_REQUIRE(!m->exec, "set_option: pdl must be set before muyo_model_finalize");
@@ -1947,7 +1967,9 @@ extern "C" size_t muyo_cuda_mat_mul_f16_workspace_size(const MuyoMatMulParams* p
     if (!p)
         return 0;
     const size_t halves = 2 * (size_t)p->tokens * (((size_t)p->ncols + 7) / 8 * 8);
-    const size_t part = (size_t)pf_splits((int)p->rows, (int)p->ncols, (int)p->tokens) * p->tokens * p->rows;
+    const int S = std::max(pf_splits((int)p->rows, (int)p->ncols, (int)p->tokens, true),
+                           pf_splits((int)p->rows, (int)p->ncols, (int)p->tokens, false));
+    const size_t part = (size_t)S * p->tokens * p->rows;
     return halves * sizeof(__half) + 256 + part * sizeof(float);
 }
 
@@ -1961,7 +1983,7 @@ extern "C" int muyo_cuda_mat_mul_f16(const MuyoMatMulParams* p, const void* a, c
     MUYO_REQUIRE(K > 0 && N > 0 && T > 0, "mat_mul: ncols, rows and tokens must be positive");
     MUYO_REQUIRE(K % 8 == 0, "mat_mul: ncols %d must be a multiple of 8", K);
     MUYO_REQUIRE(ldx >= K && ldx % 4 == 0 && ldy >= N, "mat_mul: strides too small or x stride not a multiple of 4");
-    MUYO_REQUIRE((p->flags & ~(MUYO_MATMUL_BIAS | MUYO_MATMUL_ACCUMULATE)) == 0 &&
+    MUYO_REQUIRE((p->flags & ~(MUYO_MATMUL_BIAS | MUYO_MATMUL_ACCUMULATE | MUYO_MATMUL_TCGEN05)) == 0 &&
                      (p->flags & (MUYO_MATMUL_BIAS | MUYO_MATMUL_ACCUMULATE)) != (MUYO_MATMUL_BIAS | MUYO_MATMUL_ACCUMULATE),
                  "mat_mul: flags are BIAS or ACCUMULATE");
     MUYO_REQUIRE(!(p->flags & MUYO_MATMUL_BIAS) || bias, "mat_mul: BIAS without a bias vector");
@@ -1977,15 +1999,18 @@ extern "C" int muyo_cuda_mat_mul_f16(const MuyoMatMulParams* p, const void* a, c
     const size_t part_floats = (workspace_bytes - part_off) / sizeof(float);
     for (auto k : {k_pf_gemm<PF_STORE>, k_pf_gemm<PF_BIAS>, k_pf_gemm<PF_ADD>})
         MUYO_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPfGemmSmem));
+    for (auto k : {k_pf_gemm_tc<PF_STORE>, k_pf_gemm_tc<PF_BIAS>, k_pf_gemm_tc<PF_ADD>})
+        MUYO_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem));
     MUYO_CUDA_TRY(launch_kernel(k_pf_split, dim3(T), dim3(256), 0, st, true, x, ldx, K, hi, lo, ldh));
     const __half* w = static_cast<const __half*>(a);
+    const bool tc = (p->flags & MUYO_MATMUL_TCGEN05) != 0;
     int rc;
     if (p->flags & MUYO_MATMUL_BIAS)
-        rc = pf_gemm<PF_BIAS>(w, nullptr, N, N, K, T, hi, lo, ldh, y, ldy, bias, part, part_floats, st);
+        rc = pf_gemm<PF_BIAS>(w, nullptr, N, N, K, T, hi, lo, ldh, y, ldy, bias, part, part_floats, st, tc);
     else if (p->flags & MUYO_MATMUL_ACCUMULATE)
-        rc = pf_gemm<PF_ADD>(w, nullptr, N, N, K, T, hi, lo, ldh, y, ldy, nullptr, part, part_floats, st);
+        rc = pf_gemm<PF_ADD>(w, nullptr, N, N, K, T, hi, lo, ldh, y, ldy, nullptr, part, part_floats, st, tc);
     else
-        rc = pf_gemm<PF_STORE>(w, nullptr, N, N, K, T, hi, lo, ldh, y, ldy, nullptr, part, part_floats, st);
+        rc = pf_gemm<PF_STORE>(w, nullptr, N, N, K, T, hi, lo, ldh, y, ldy, nullptr, part, part_floats, st, tc);
     if (rc)
         return rc;
     MUYO_LAUNCH_CHECK();

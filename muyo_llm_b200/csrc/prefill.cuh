@@ -16,9 +16,10 @@
 //   k_pf_gemm<ADD>    the MLP
 //
 // The GEMM is weight-read bound for prompts of up to a few hundred positions (2 flops per weight
-// byte per position), so it uses the warp-level mma.sync m16n8k16 (F16 x F16 -> F32) on tiles
-// staged by cp.async: an activation x enters as hi = f16(x) and lo = f16(x - hi), two products into
-// one F32 accumulator, which keeps the product error near F32's (2^-22 relative to |x|).
+// byte per position), so by default it uses the warp-level mma.sync m16n8k16 (F16 x F16 -> F32) on
+// tiles staged by cp.async; k_pf_gemm_tc is the same GEMM on tcgen05 (tensor-memory accumulator).
+// An activation x enters as hi = f16(x) and lo = f16(x - hi), two products into one F32
+// accumulator, which keeps the product error near F32's (2^-22 relative to |x|).
 #pragma once
 
 #include <cuda_fp16.h>
@@ -226,6 +227,222 @@ __global__ void __launch_bounds__(256) k_pf_reduce(PfGemm g, const float* __rest
         if (EPI == PF_ADD)
             v = *yp + v;
         *yp = v;
+    }
+}
+
+// ---- the same GEMM on the 5th-generation tensor cores (tcgen05) -----------------------------------
+// One CTA: 128 feature rows (the UMMA M) x 64 positions (N). Operands are K-major and unswizzled in
+// shared memory: 16-byte row pieces of 8 halves, core matrices of 8 rows x 16 bytes (128 bytes),
+// piece (row, chunk) of an R-row tile at chunk * (R * 16) + (row / 8) * 128 + (row % 8) * 16, so the
+// descriptor's leading-byte offset (between the two K halves of a 16-deep step) is R * 16 and its
+// stride-byte offset (between 8-row groups) is 128. All 128 threads fill a 3-stage ring by cp.async;
+// one thread issues per stage 4 K-steps x 2 MMAs (x-hi and x-lo) into a 64-column F32 accumulator in
+// tensor memory and commits them to the stage's mbarrier, which the stage's refill waits for. After
+// the last commit each warp reads its 32 accumulator lanes (tcgen05.ld 32x32b) for the epilogue.
+// Every wait is bounded (2 s): on expiry the error word gets 6 and the CTA still releases its TMEM.
+constexpr int kTcBM = 128, kTcBN = 64, kTcBK = 64, kTcStages = 3, kTcThreads = 128;
+constexpr int kTcWBytes = kTcBM * kTcBK * 2;               // 16 KB
+constexpr int kTcXBytes = kTcBN * kTcBK * 2;               // 8 KB
+constexpr int kTcStageBytes = kTcWBytes + 2 * kTcXBytes;   // 32 KB
+constexpr size_t kTcSmem = (size_t)kTcStages * kTcStageBytes + 1024;  // + alignment slack
+constexpr int kTcTmemCols = 64;
+
+// UMMA shared-memory descriptor: start >> 4 in [0,14), leading-byte offset >> 4 in [16,30),
+// stride-byte offset >> 4 in [32,46), version 1 in [46,48), no swizzle (layout 0 in [61,64)).
+__device__ __forceinline__ uint64_t umma_desc(unsigned saddr, unsigned lbo, unsigned sbo)
+{
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+
+// Instruction descriptor, kind::f16: F32 accumulator (bits [4,6) = 1), A and B F16 (0), both
+// K-major, N >> 3 in [17,23), M >> 4 in [24,29).
+constexpr uint32_t kTcIdesc = (1u << 4) | ((uint32_t)(kTcBN >> 3) << 17) | ((uint32_t)(kTcBM >> 4) << 24);
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem, uint64_t da, uint64_t db, uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem),
+        "l"(da), "l"(db), "r"(kTcIdesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+// 32 consecutive accumulator columns of this warp's 32 lanes: thread l of warp w gets row 32w + l.
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t (&r)[32])
+{
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+
+// Bounded wait for `parity` of `bar`; false (error word 6) on expiry.
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, unsigned parity, int* err)
+{
+    if (mbar_try_wait(bar, parity))
+        return true;
+    const unsigned long long t0 = now_ns();
+    while (!mbar_try_wait(bar, parity))
+        if (now_ns() - t0 > kWaitLimitNs) {
+            if (err)
+                atomicMax(err, 6);
+            return false;
+        }
+    return true;
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kTcThreads, 1) k_pf_gemm_tc(PfGemm g, float* part, int* err)
+{
+    extern __shared__ unsigned char tc_raw[];
+    __shared__ __align__(8) uint64_t stage_bar[kTcStages];
+    __shared__ __align__(8) uint64_t done_bar;
+    __shared__ uint32_t tmem_base;
+    pdl_wait();
+    pdl_trigger();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const unsigned sraw = smem_u32(tc_raw);
+    const unsigned sbase = (sraw + 1023u) & ~1023u;  // 1 KB-aligned ring
+    const int n0 = blockIdx.x * kTcBM, t0 = blockIdx.y * kTcBN;
+    const int nk_all = (g.K + kTcBK - 1) / kTcBK, S = gridDim.z, z = blockIdx.z;
+    const int kt0 = (int)((long long)nk_all * z / S), kt1 = (int)((long long)nk_all * (z + 1) / S);
+    const int nk = kt1 - kt0;
+
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
+                     "r"(kTcTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == 0) {
+        for (int s = 0; s < kTcStages; ++s)
+            mbar_init(&stage_bar[s], 1);
+        mbar_init(&done_bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base;
+
+    // This thread's pieces of a stage: 8 of the W tile (row p >> 3, chunk p & 7 for p = tid + 128 j)
+    // and 4 of each x tile.
+    auto load_stage = [&](int buf, int kt) {
+        const int k0 = kt * kTcBK;
+        const unsigned st = sbase + (unsigned)(buf * kTcStageBytes);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int pc = tid + kTcThreads * j, row = pc >> 3, ch = pc & 7, n = n0 + row, k = k0 + ch * 8;
+            const bool ok = n < g.N && k < g.K;
+            const __half* src = g.w0;
+            if (ok)
+                src = (n < g.n_split ? g.w0 + (size_t)n * g.K : g.w1 + (size_t)(n - g.n_split) * g.K) + k;
+            cp_async16(st + (unsigned)(ch * (kTcBM * 16) + (row >> 3) * 128 + (row & 7) * 16), src, ok);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int pc = tid + kTcThreads * (j & 3), row = pc >> 3, ch = pc & 7, t = t0 + row, k = k0 + ch * 8;
+            const bool ok = t < g.T && k < g.K;
+            const __half* xb = j < 4 ? g.xhi : g.xlo;
+            const unsigned tile = st + (unsigned)(kTcWBytes + (j < 4 ? 0 : kTcXBytes));
+            cp_async16(tile + (unsigned)(ch * (kTcBN * 16) + (row >> 3) * 128 + (row & 7) * 16),
+                       ok ? xb + (size_t)t * g.ldx + k : xb, ok);
+        }
+    };
+
+#pragma unroll
+    for (int s = 0; s < kTcStages - 1; ++s) {
+        if (s < nk)
+            load_stage(s, kt0 + s);
+        cp_async_commit();
+    }
+    bool failed = false;  // this thread's last bounded wait expired
+    for (int i = 0; i < nk; ++i) {
+        const int buf = i % kTcStages;
+        cp_async_wait<kTcStages - 2>();
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the copies, to the tensor cores
+        if (__syncthreads_or(failed))  // every thread leaves together
+            break;
+        if (tid == 0) {
+            tc_fence_after();
+            const unsigned st = sbase + (unsigned)(buf * kTcStageBytes);
+#pragma unroll
+            for (int s = 0; s < kTcBK / 16; ++s) {  // K-step s: chunks 2s, 2s + 1
+                const uint64_t da = umma_desc(st + (unsigned)(2 * s * kTcBM * 16), kTcBM * 16, 128);
+                const uint64_t dh = umma_desc(st + (unsigned)(kTcWBytes + 2 * s * kTcBN * 16), kTcBN * 16, 128);
+                const uint64_t dl =
+                    umma_desc(st + (unsigned)(kTcWBytes + kTcXBytes + 2 * s * kTcBN * 16), kTcBN * 16, 128);
+                tc_mma(tmem, da, dh, (i > 0 || s > 0) ? 1u : 0u);
+                tc_mma(tmem, da, dl, 1u);
+            }
+            tc_commit(&stage_bar[buf]);
+        }
+        const int nxt = i + kTcStages - 1;
+        if (nxt < nk) {
+            // the buffer refilled now last held stage i - 1: its MMAs must be complete
+            if (i >= 1 && !tc_wait(&stage_bar[nxt % kTcStages], (unsigned)(((i - 1) / kTcStages) & 1), err))
+                failed = true;
+            if (!failed)
+                load_stage(nxt % kTcStages, kt0 + nxt);
+        }
+        cp_async_commit();
+    }
+    cp_async_wait<0>();
+    if (tid == 0)
+        tc_commit(&done_bar);  // arrives when every MMA this thread issued is complete
+    __syncthreads();
+    const bool ok = __syncthreads_and(tc_wait(&done_bar, 0, err) && !failed);  // uniform over the CTA
+    tc_fence_after();
+    if (ok) {
+        // thread l of warp w: feature row n0 + 32w + l, accumulator columns = positions t0 .. t0 + 63
+        const int n = n0 + warp * 32 + lane;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            uint32_t r[32];
+            tc_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(half * 32), r);
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            if (n < g.N) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int t = t0 + half * 32 + j;
+                    if (t < g.T) {
+                        const float v0 = __uint_as_float(r[j]);
+                        if (S > 1) {
+                            part[((size_t)z * g.T + t) * g.N + n] = v0;
+                        } else {
+                            float* yp = g.y + (size_t)t * g.ldy + n;
+                            float v = v0;
+                            if (EPI == PF_BIAS)
+                                v = v + g.bias[n];
+                            if (EPI == PF_ADD)
+                                v = *yp + v;
+                            *yp = v;
+                        }
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcTmemCols) : "memory");
     }
 }
 

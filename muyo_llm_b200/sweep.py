@@ -222,12 +222,14 @@ def prefill(iters: int = 0, peak_gbs: float = 6462.1, seed: int = 7, n_prompt: i
     g.manual_seed(seed)
     stream = torch.cuda.Stream()
     n_calls = iters or 50
-    for N, K, T, what in [(1152, 896, 128, "QKV"), (896, 896, 128, "O"), (9728, 896, 128, "gate|up"),
-                          (896, 4864, 128, "down")]:
+    for N, K, T, what, kern in [(n, k, t, w_, kk) for (n, k, t, w_) in
+                                [(1152, 896, 128, "QKV"), (896, 896, 128, "O"), (9728, 896, 128, "gate|up"),
+                                 (896, 4864, 128, "down"), (9728, 896, 512, "gate|up")]
+                                for kk in ("mma_sync", "tcgen05")]:
         w = (torch.rand(N * K, generator=g, device="cuda") * 0.1 - 0.05).half()
         x = torch.randn(T * K, generator=g, device="cuda")
         y = torch.empty(T * N, device="cuda")
-        p = _abi.MatMulParams(K, N, T, 0, 0, 0)
+        p = _abi.MatMulParams(K, N, T, 0, 0, _abi.MATMUL_TCGEN05 if kern == "tcgen05" else 0)
         wsb = int(_abi.lib().muyo_cuda_mat_mul_f16_workspace_size(C.byref(p)))
         ws = torch.empty(wsb, dtype=torch.uint8, device="cuda")
 
@@ -251,16 +253,19 @@ def prefill(iters: int = 0, peak_gbs: float = 6462.1, seed: int = 7, n_prompt: i
         torch.cuda.synchronize()
         ms = s.elapsed_time(e) / n_calls
         alg = N * K * 2 + T * K * 4 + T * N * 4
-        r = _result("k_pf_split + k_pf_gemm", f"{N}x{K}, {T} positions ({what})", alg, ms, peak_gbs,
+        r = _result("k_pf_split + " + ("k_pf_gemm_tc" if kern == "tcgen05" else "k_pf_gemm"),
+                    f"{N}x{K}, {T} positions ({what})", alg, ms, peak_gbs, tensor=kern,
                     tflops=2 * N * K * T / (ms * 1e-3) / 1e12, mode="weights L2-resident between calls")
         out.append(r)
     cfg = synth.QWEN2_05B
     t = synth.make_model(cfg, seed)
     models = {}
-    for pf in (False, True):
+    for pf in (False, True, "tcgen05"):
         models[pf] = engine.Qwen2Model(cfg, t, kv_dtype=_abi.KV_F16, engine=engine.Qwen2Model.ENGINE_GRAPH)
         if pf:
             _abi.call("muyo_model_set_option", models[pf]._m, b"prefill", 1)
+        if pf == "tcgen05":
+            _abi.call("muyo_model_set_option", models[pf]._m, b"prefill_tc", 1)
 
     def timed(m, prompt, n):
         best = float("inf")
@@ -278,8 +283,9 @@ def prefill(iters: int = 0, peak_gbs: float = 6462.1, seed: int = 7, n_prompt: i
     for P in (32, 128, 512):
         prompt = [int(i) for i in synth.prompt_ids(seed, P, cfg.vocab)]
         off, on = timed(models[False], prompt, 1), timed(models[True], prompt, 1)
+        on_tc = timed(models["tcgen05"], prompt, 1)
         out.append({"kernel": "prompt to first token", "shape": f"config 4 arch, {P}-id prompt",
-                    "ms_stepwise": off, "ms_prefill": on, "speedup": off / on,
+                    "ms_stepwise": off, "ms_prefill": on, "ms_prefill_tcgen05": on_tc, "speedup": off / on,
                     "prompt_tokens_per_s_prefill": P / (on * 1e-3), "mode": "prefill of P-1 positions + 1 step"})
     prompt = [int(i) for i in synth.prompt_ids(seed, n_prompt, cfg.vocab)]
     for pf in (False, True):

@@ -41,27 +41,32 @@ def _mat_mul(w, x, flags=0, bias=None, y0=None):
     return yd.cpu().numpy()
 
 
-@pytest.mark.parametrize("N,K,T", [(128, 256, 1), (1152, 896, 32), (897, 904, 65), (64, 4864, 128), (200, 8, 3)])
-def test_mat_mul_f16_against_float64(cuda, N, K, T):
+@pytest.mark.parametrize("kernel", ["mma_sync", "tcgen05"])
+@pytest.mark.parametrize("N,K,T", [(128, 256, 1), (1152, 896, 32), (897, 904, 65), (64, 4864, 128), (200, 8, 3),
+                                   (896, 4864, 100)])
+def test_mat_mul_f16_against_float64(cuda, N, K, T, kernel):
     rng = np.random.default_rng(N * 7 + K + T)
     w = (rng.uniform(-1, 1, (N, K)) * 0.05).astype(np.float16)
     x = rng.standard_normal((T, K)).astype(np.float32)
     exact = x.astype(np.float64) @ w.astype(np.float64).T
     bound = 1e-5 * (np.abs(x).astype(np.float64) @ np.abs(w.astype(np.float64)).T) + 1e-6
-    y = _mat_mul(w, x)
+    f = _abi.MATMUL_TCGEN05 if kernel == "tcgen05" else 0
+    y = _mat_mul(w, x, f)
     assert np.all(np.abs(y - exact) <= bound)
     b = rng.standard_normal(N).astype(np.float32)
-    yb = _mat_mul(w, x, _abi.MATMUL_BIAS, bias=b)
+    yb = _mat_mul(w, x, f | _abi.MATMUL_BIAS, bias=b)
     assert np.all(np.abs(yb - (exact + b)) <= bound + 1e-6 * np.abs(b))
     y0 = rng.standard_normal((T, N)).astype(np.float32)
-    ya = _mat_mul(w, x, _abi.MATMUL_ACCUMULATE, y0=y0)
+    ya = _mat_mul(w, x, f | _abi.MATMUL_ACCUMULATE, y0=y0)
     assert np.all(np.abs(ya - (exact + y0)) <= bound + 1e-6 * np.abs(y0))
 
 
-def _model(cfg, t, kv, prefill):
+def _model(cfg, t, kv, prefill, tc=False):
     m = engine.Qwen2Model(cfg, t, kv_dtype=kv, engine=engine.Qwen2Model.ENGINE_GRAPH)
     if prefill:
         _abi.call("muyo_model_set_option", m._m, b"prefill", 1)
+    if tc:
+        _abi.call("muyo_model_set_option", m._m, b"prefill_tc", 1)
     return m
 
 
@@ -104,11 +109,13 @@ FULL = os.path.join(GOLDEN, "qwen2_05b_greedy.json")
 
 
 @pytest.mark.skipif(not os.path.exists(FULL), reason="0.5B golden fixture not generated")
-def test_prefill_05b_greedy_bit_identical_to_reference(cuda):
+@pytest.mark.parametrize("tc", [False, True])
+def test_prefill_05b_greedy_bit_identical_to_reference(cuda, tc):
+    """With either GEMM kernel (mma.sync, tcgen05) behind the prefill projections."""
     g = json.load(open(FULL))
     cfg = synth.QWEN2_05B
     t = synth.make_model(cfg, int(g["seed"]))
-    m = _model(cfg, t, _abi.KV_F32, True)
+    m = _model(cfg, t, _abi.KV_F32, True, tc)
     ids = list(m.generate([int(i) for i in g["prompt"]], len(g["generated"])))
     m.close()
     assert ids == [int(i) for i in g["generated"]]
