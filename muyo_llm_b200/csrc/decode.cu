@@ -14,6 +14,7 @@
 #include <cstddef>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <new>
 #include <string>
 #include <vector>
@@ -860,6 +861,7 @@ struct MuyoModel {
     void* rng = nullptr;            // its mt19937_64 state, followed by the last sampled id (int32)
     bool prefill = false;           // generate: the prompt's positions but the last in one batched pass
     bool pf_tc = false;             // prefill projections on tcgen05 (default: the warp-level mma.sync kernel)
+    std::vector<CUtensorMap> pf_maps;  // tcgen05 prefill: 5 weight maps per layer, then the activation halves
     char* pf_buf = nullptr;         // batched-prefill activations for kPfCap positions
     float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_att = nullptr, *pf_gu = nullptr;
     float* pf_part = nullptr;  // split-K partial sums
@@ -1579,6 +1581,56 @@ static int check_device_error(MuyoModel* m, cudaStream_t st)
 constexpr int kPfCap = 128;  // positions per prefill pass (longer prompts take several passes)
 constexpr int kPfMaxSplits = 16;
 
+// TMA descriptors of one tcgen05 prefill GEMM: the W rows (two matrices for gate | up) and the
+// activation halves.
+struct PfMaps {
+    CUtensorMap w0, w1, xhi, xlo;
+};
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against the driver).
+static EncodeTiledFn encode_tiled()
+{
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(f);
+        else
+            cudaGetLastError();
+    });
+    return fn;
+}
+
+// F16 matrix [rows][cols] with row stride ld halves, read in boxes of 8 halves x box_rows rows
+// (unswizzled; outside the matrix the box is zero-filled). cols, ld multiples of 8; base 16-byte aligned.
+static int make_map(CUtensorMap* map, const void* base, int cols, int rows, int ld, int box_rows)
+{
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) {
+        set_error("prefill: cuTensorMapEncodeTiled is not available from the driver");
+        return MUYO_EUNSUPPORTED;
+    }
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    const cuuint32_t box[2] = {8, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("prefill: cuTensorMapEncodeTiled failed (%d) for a %d x %d matrix", (int)r, rows, cols);
+        return MUYO_ECUDA;
+    }
+    return MUYO_OK;
+}
+
 static int pf_alloc(MuyoModel* m)
 {
     if (m->pf_buf)
@@ -1632,21 +1684,22 @@ static int pf_splits(int N, int K, int T, bool tc = false)
     return std::max(1, std::min(S, kPfMaxSplits));
 }
 
-// part: S * T * N floats when pf_splits > 1 (the prefill workspace). tc: the tcgen05 kernel, else the
-// warp-level mma.sync kernel (faster at these sizes while tcgen05's tiles are fed by cp.async from
-// every thread). err: the bounded waits' error word (may be null).
+// part: S * T * N floats when pf_splits > 1 (the prefill workspace). tc: the tensor maps of the
+// tcgen05 kernel (its W rows: n_split a multiple of 128), else the warp-level mma.sync kernel runs.
+// err: the bounded waits' error word (may be null).
 template <int EPI>
 static int pf_gemm(const __half* w0, const __half* w1, int n_split, int N, int K, int T, const __half* xhi,
                    const __half* xlo, int ldx, float* y, int ldy, const float* bias, float* part, size_t part_floats,
-                   cudaStream_t st, bool tc = false, int* err = nullptr)
+                   cudaStream_t st, const PfMaps* tc = nullptr, int* err = nullptr)
 {
     PfGemm g{w0, w1 ? w1 : w0, n_split, N, K, T, xhi, xlo, ldx, y, ldy, bias};
-    int S = pf_splits(N, K, T, tc);
+    int S = pf_splits(N, K, T, tc != nullptr);
     if ((size_t)S * T * N > part_floats)
         S = 1;
     if (tc) {
         const dim3 grid((N + kTcBM - 1) / kTcBM, (T + kTcBN - 1) / kTcBN, S);
-        MUYO_CUDA_TRY(launch_kernel(k_pf_gemm_tc<EPI>, grid, dim3(kTcThreads), kTcSmem, st, true, g, part, err));
+        MUYO_CUDA_TRY(launch_kernel(k_pf_gemm_tc<EPI>, grid, dim3(kTcThreads), kTcSmem, st, true, g, part, err,
+                                    tc->w0, tc->w1, tc->xhi, tc->xlo));
     } else {
         const dim3 grid((N + kPfBM - 1) / kPfBM, (T + kPfBN - 1) / kPfBN, S);
         MUYO_CUDA_TRY(launch_kernel(k_pf_gemm<EPI>, grid, dim3(kPfThreads), kPfGemmSmem, st, true, g, part));
@@ -1684,6 +1737,32 @@ static int pf_attention(const Shape& s, float* q, float* out, const float* qkv, 
 #undef MUYO_PF_ATTN
 }
 
+// The tcgen05 prefill's tensor maps: per layer qkv, o, gate, up, down (W row tiles of 128), then the
+// activation halves as K = hidden, q_dim and ffn wide (position tiles of 64).
+static int pf_make_maps(MuyoModel* m)
+{
+    const Shape& s = m->s;
+    const int H = s.hidden, QD = s.q_dim, F = s.ffn, ldh = std::max(std::max(H, QD), F);
+    std::vector<CUtensorMap> maps((size_t)5 * s.layers + 6);
+    int rc;
+    for (int l = 0; l < s.layers; ++l) {
+        const LayerPtrs w = layer_ptrs(m, l);
+        CUtensorMap* lm = maps.data() + (size_t)5 * l;
+        if ((rc = make_map(&lm[0], w.wqkv, H, s.qkv_rows, H, kTcBM)) || (rc = make_map(&lm[1], w.wo, QD, H, QD, kTcBM)) ||
+            (rc = make_map(&lm[2], w.wgate, H, F, H, kTcBM)) || (rc = make_map(&lm[3], w.wup, H, F, H, kTcBM)) ||
+            (rc = make_map(&lm[4], w.wdown, F, H, F, kTcBM)))
+            return rc;
+    }
+    CUtensorMap* xm = maps.data() + (size_t)5 * s.layers;
+    const int ks[3] = {H, QD, F};
+    for (int i = 0; i < 3; ++i)
+        if ((rc = make_map(&xm[2 * i], m->pf_hi, ks[i], kPfCap, ldh, kTcBN)) ||
+            (rc = make_map(&xm[2 * i + 1], m->pf_lo, ks[i], kPfCap, ldh, kTcBN)))
+            return rc;
+    m->pf_maps.swap(maps);
+    return MUYO_OK;
+}
+
 // Positions [p0, p0 + n) of m->tokens through every layer: their keys and values go to the cache.
 // No logits are formed (the decode step at position p0 + n forms the next ones).
 static int prefill_run(MuyoModel* m, int p0, int n, cudaStream_t st)
@@ -1692,6 +1771,19 @@ static int prefill_run(MuyoModel* m, int p0, int n, cudaStream_t st)
     const int H = s.hidden, QD = s.q_dim, F = s.ffn;
     const int ldh = std::max(std::max(H, QD), F);
     int rc;
+    if (m->pf_tc && m->pf_maps.empty() && (rc = pf_make_maps(m)))
+        return rc;
+    // tcgen05 GEMM of layer l: weight maps a and b of the layer (b for rows past the split) and the
+    // activation halves of K index xk (hidden, q_dim, ffn); null selects the mma.sync kernel.
+    PfMaps pm;
+    auto tc = [&](int l, int a, int b, int xk) -> const PfMaps* {
+        if (!m->pf_tc || (a != b && F % kTcBM != 0))
+            return nullptr;
+        const CUtensorMap* lm = m->pf_maps.data() + (size_t)5 * l;
+        const CUtensorMap* xm = m->pf_maps.data() + (size_t)5 * s.layers + 2 * xk;
+        pm = PfMaps{lm[a], lm[b], xm[0], xm[1]};
+        return &pm;
+    };
     for (int c0 = 0; c0 < n; c0 += kPfCap) {
         const int T = std::min(kPfCap, n - c0), pos0 = p0 + c0;
         MUYO_CUDA_TRY(launch_kernel(k_pf_embed, dim3(T), dim3(256), 0, st, true, W(m, "token_embd.weight"),
@@ -1703,7 +1795,7 @@ static int prefill_run(MuyoModel* m, int p0, int n, cudaStream_t st)
             MUYO_CUDA_TRY(launch_kernel(k_pf_norm_split, dim3(T), dim3(256), 0, st, true, (const float*)m->pf_x, H,
                                         w.attn_norm, s.eps, H, m->pf_hi, m->pf_lo, ldh));
             if ((rc = pf_gemm<PF_BIAS>(w.wqkv, nullptr, s.qkv_rows, s.qkv_rows, H, T, m->pf_hi, m->pf_lo, ldh,
-                                       m->pf_qkv, s.qkv_rows, w.bqkv, m->pf_part, m->pf_part_floats, st, m->pf_tc,
+                                       m->pf_qkv, s.qkv_rows, w.bqkv, m->pf_part, m->pf_part_floats, st, tc(l, 0, 0, 0),
                                        m->err)))
                 return rc;
             if ((rc = pf_attention(s, m->pf_q, m->pf_att, m->pf_qkv, kc, vc, pos0, T, st)))
@@ -1711,17 +1803,17 @@ static int prefill_run(MuyoModel* m, int p0, int n, cudaStream_t st)
             MUYO_CUDA_TRY(launch_kernel(k_pf_split, dim3(T), dim3(256), 0, st, true, (const float*)m->pf_att, QD, QD,
                                         m->pf_hi, m->pf_lo, ldh));
             if ((rc = pf_gemm<PF_ADD>(w.wo, nullptr, H, H, QD, T, m->pf_hi, m->pf_lo, ldh, m->pf_x, H, nullptr, m->pf_part,
-                                      m->pf_part_floats, st, m->pf_tc, m->err)))
+                                      m->pf_part_floats, st, tc(l, 1, 1, 1), m->err)))
                 return rc;
             MUYO_CUDA_TRY(launch_kernel(k_pf_norm_split, dim3(T), dim3(256), 0, st, true, (const float*)m->pf_x, H,
                                         w.ffn_norm, s.eps, H, m->pf_hi, m->pf_lo, ldh));
             if ((rc = pf_gemm<PF_STORE>(w.wgate, w.wup, F, 2 * F, H, T, m->pf_hi, m->pf_lo, ldh, m->pf_gu, 2 * F,
-                                        nullptr, m->pf_part, m->pf_part_floats, st, m->pf_tc, m->err)))
+                                        nullptr, m->pf_part, m->pf_part_floats, st, tc(l, 2, 3, 0), m->err)))
                 return rc;
             MUYO_CUDA_TRY(launch_kernel(k_pf_swiglu_split, dim3(T), dim3(256), 0, st, true, (const float*)m->pf_gu, F,
                                         m->pf_hi, m->pf_lo, ldh));
             if ((rc = pf_gemm<PF_ADD>(w.wdown, nullptr, H, H, F, T, m->pf_hi, m->pf_lo, ldh, m->pf_x, H, nullptr, m->pf_part,
-                                      m->pf_part_floats, st, m->pf_tc, m->err)))
+                                      m->pf_part_floats, st, tc(l, 4, 4, 2), m->err)))
                 return rc;
         }
     }
@@ -2003,8 +2095,16 @@ extern "C" int muyo_cuda_mat_mul_f16(const MuyoMatMulParams* p, const void* a, c
         MUYO_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem));
     MUYO_CUDA_TRY(launch_kernel(k_pf_split, dim3(T), dim3(256), 0, st, true, x, ldx, K, hi, lo, ldh));
     const __half* w = static_cast<const __half*>(a);
-    const bool tc = (p->flags & MUYO_MATMUL_TCGEN05) != 0;
+    PfMaps maps;
+    const PfMaps* tc = nullptr;
     int rc;
+    if (p->flags & MUYO_MATMUL_TCGEN05) {
+        if ((rc = make_map(&maps.w0, w, K, N, K, kTcBM)) || (rc = make_map(&maps.xhi, hi, K, T, ldh, kTcBN)) ||
+            (rc = make_map(&maps.xlo, lo, K, T, ldh, kTcBN)))
+            return rc;
+        maps.w1 = maps.w0;
+        tc = &maps;
+    }
     if (p->flags & MUYO_MATMUL_BIAS)
         rc = pf_gemm<PF_BIAS>(w, nullptr, N, N, K, T, hi, lo, ldh, y, ldy, bias, part, part_floats, st, tc);
     else if (p->flags & MUYO_MATMUL_ACCUMULATE)

@@ -22,6 +22,7 @@
 // accumulator, which keeps the product error near F32's (2^-22 relative to |x|).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 
 #include "attention.cuh"
@@ -230,17 +231,21 @@ __global__ void __launch_bounds__(256) k_pf_reduce(PfGemm g, const float* __rest
     }
 }
 
-// ---- the same GEMM on the 5th-generation tensor cores (tcgen05) -----------------------------------
-// One CTA: 128 feature rows (the UMMA M) x 64 positions (N). Operands are K-major and unswizzled in
-// shared memory: 16-byte row pieces of 8 halves, core matrices of 8 rows x 16 bytes (128 bytes),
-// piece (row, chunk) of an R-row tile at chunk * (R * 16) + (row / 8) * 128 + (row % 8) * 16, so the
-// descriptor's leading-byte offset (between the two K halves of a 16-deep step) is R * 16 and its
-// stride-byte offset (between 8-row groups) is 128. All 128 threads fill a 3-stage ring by cp.async;
-// one thread issues per stage 4 K-steps x 2 MMAs (x-hi and x-lo) into a 64-column F32 accumulator in
-// tensor memory and commits them to the stage's mbarrier, which the stage's refill waits for. After
-// the last commit each warp reads its 32 accumulator lanes (tcgen05.ld 32x32b) for the epilogue.
-// Every wait is bounded (2 s): on expiry the error word gets 6 and the CTA still releases its TMEM.
-constexpr int kTcBM = 128, kTcBN = 64, kTcBK = 64, kTcStages = 3, kTcThreads = 128;
+// ---- the same GEMM on the 5th-generation tensor cores (tcgen05), fed by TMA -------------------------
+// One CTA: 128 feature rows (the UMMA M) x 64 positions (N), warp-specialised:
+//   warp 0, one lane: the producer. Per 64-deep K stage it arms the stage's `full` mbarrier with the
+//     stage's 32 KB and issues 24 two-dimensional TMA tile loads (8 K-chunks of 8 halves for each of
+//     W, x-hi and x-lo), after waiting on the stage's `empty` barrier once the 4-stage ring wraps;
+//   warp 1, one lane: the MMA issuer. It waits on `full`, issues 4 K-steps x 2 MMAs (x-hi, x-lo) into
+//     a 64-column F32 accumulator in tensor memory, and commits them to `empty`; the last commit goes
+//     to `done`;
+//   all four warps: the epilogue, each reading its 32 accumulator lanes (tcgen05.ld 32x32b).
+// A TMA box of 8 halves x R rows lands as R rows x 16 bytes, one column of 8x16-byte core matrices:
+// K-chunk c of an R-row tile sits at c * R * 16, so the UMMA descriptors are K-major and unswizzled
+// with a leading-byte offset of R * 16 (the two K halves of a 16-deep step) and a stride-byte offset
+// of 128 (8-row groups). Rows and columns outside the tensors are zero-filled by the TMA. Every wait is
+// bounded (2 s): on expiry the error word gets 6, the roles stop, and the CTA still frees its TMEM.
+constexpr int kTcBM = 128, kTcBN = 64, kTcBK = 64, kTcStages = 4, kTcThreads = 128;
 constexpr int kTcWBytes = kTcBM * kTcBK * 2;               // 16 KB
 constexpr int kTcXBytes = kTcBN * kTcBK * 2;               // 8 KB
 constexpr int kTcStageBytes = kTcWBytes + 2 * kTcXBytes;   // 32 KB
@@ -306,23 +311,29 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, unsigned parity, int* err
     return true;
 }
 
+// 2-D TMA tile load into this CTA's shared memory, completing on `bar` (no multicast).
+__device__ __forceinline__ void tma_load_2d(unsigned dst, const void* map, int x, int y, uint64_t* bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// The tile's W rows come from tw0 (rows n0 .. ) or, past n_split (a multiple of 128), from tw1.
 template <int EPI>
-__global__ void __launch_bounds__(kTcThreads, 1) k_pf_gemm_tc(PfGemm g, float* part, int* err)
+__global__ void __launch_bounds__(kTcThreads, 1)
+    k_pf_gemm_tc(PfGemm g, float* part, int* err, const __grid_constant__ CUtensorMap tw0,
+                 const __grid_constant__ CUtensorMap tw1, const __grid_constant__ CUtensorMap txh,
+                 const __grid_constant__ CUtensorMap txl)
 {
     extern __shared__ unsigned char tc_raw[];
-    __shared__ __align__(8) uint64_t stage_bar[kTcStages];
+    __shared__ __align__(8) uint64_t full_bar[kTcStages];
+    __shared__ __align__(8) uint64_t empty_bar[kTcStages];
     __shared__ __align__(8) uint64_t done_bar;
     __shared__ uint32_t tmem_base;
-    pdl_wait();
-    pdl_trigger();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const unsigned sraw = smem_u32(tc_raw);
-    const unsigned sbase = (sraw + 1023u) & ~1023u;  // 1 KB-aligned ring
-    const int n0 = blockIdx.x * kTcBM, t0 = blockIdx.y * kTcBN;
-    const int nk_all = (g.K + kTcBK - 1) / kTcBK, S = gridDim.z, z = blockIdx.z;
-    const int kt0 = (int)((long long)nk_all * z / S), kt1 = (int)((long long)nk_all * (z + 1) / S);
-    const int nk = kt1 - kt0;
-
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
                      "r"(kTcTmemCols)
@@ -330,83 +341,67 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_pf_gemm_tc(PfGemm g, float* p
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     if (tid == 0) {
-        for (int s = 0; s < kTcStages; ++s)
-            mbar_init(&stage_bar[s], 1);
+        for (int s = 0; s < kTcStages; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
         mbar_init(&done_bar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tw0)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&txh)) : "memory");
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_base;
+    pdl_wait();  // x comes from the previous kernel: no TMA load before this point
+    pdl_trigger();
+    const unsigned sbase = (smem_u32(tc_raw) + 1023u) & ~1023u;  // 1 KB-aligned ring
+    const int n0 = blockIdx.x * kTcBM, t0 = blockIdx.y * kTcBN;
+    const int nk_all = (g.K + kTcBK - 1) / kTcBK, S = gridDim.z, z = blockIdx.z;
+    const int kt0 = (int)((long long)nk_all * z / S), kt1 = (int)((long long)nk_all * (z + 1) / S);
+    const int nk = kt1 - kt0;
 
-    // This thread's pieces of a stage: 8 of the W tile (row p >> 3, chunk p & 7 for p = tid + 128 j)
-    // and 4 of each x tile.
-    auto load_stage = [&](int buf, int kt) {
-        const int k0 = kt * kTcBK;
-        const unsigned st = sbase + (unsigned)(buf * kTcStageBytes);
+    if (warp == 0 && lane == 0) {  // producer
+        const CUtensorMap* tw = n0 < g.n_split ? &tw0 : &tw1;
+        const int wrow = n0 < g.n_split ? n0 : n0 - g.n_split;
+        for (int i = 0; i < nk; ++i) {
+            const int s = i % kTcStages;
+            if (i >= kTcStages && !tc_wait(&empty_bar[s], (unsigned)(((i / kTcStages) - 1) & 1), err))
+                break;
+            mbar_expect_tx(&full_bar[s], (unsigned)kTcStageBytes);
+            const unsigned st = sbase + (unsigned)(s * kTcStageBytes);
+            const int k0 = (kt0 + i) * kTcBK;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int pc = tid + kTcThreads * j, row = pc >> 3, ch = pc & 7, n = n0 + row, k = k0 + ch * 8;
-            const bool ok = n < g.N && k < g.K;
-            const __half* src = g.w0;
-            if (ok)
-                src = (n < g.n_split ? g.w0 + (size_t)n * g.K : g.w1 + (size_t)(n - g.n_split) * g.K) + k;
-            cp_async16(st + (unsigned)(ch * (kTcBM * 16) + (row >> 3) * 128 + (row & 7) * 16), src, ok);
+            for (int c = 0; c < kTcBK / 8; ++c) {
+                tma_load_2d(st + (unsigned)(c * kTcBM * 16), tw, k0 + 8 * c, wrow, &full_bar[s]);
+                tma_load_2d(st + (unsigned)(kTcWBytes + c * kTcBN * 16), &txh, k0 + 8 * c, t0, &full_bar[s]);
+                tma_load_2d(st + (unsigned)(kTcWBytes + kTcXBytes + c * kTcBN * 16), &txl, k0 + 8 * c, t0,
+                            &full_bar[s]);
+            }
         }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int pc = tid + kTcThreads * (j & 3), row = pc >> 3, ch = pc & 7, t = t0 + row, k = k0 + ch * 8;
-            const bool ok = t < g.T && k < g.K;
-            const __half* xb = j < 4 ? g.xhi : g.xlo;
-            const unsigned tile = st + (unsigned)(kTcWBytes + (j < 4 ? 0 : kTcXBytes));
-            cp_async16(tile + (unsigned)(ch * (kTcBN * 16) + (row >> 3) * 128 + (row & 7) * 16),
-                       ok ? xb + (size_t)t * g.ldx + k : xb, ok);
-        }
-    };
-
-#pragma unroll
-    for (int s = 0; s < kTcStages - 1; ++s) {
-        if (s < nk)
-            load_stage(s, kt0 + s);
-        cp_async_commit();
-    }
-    bool failed = false;  // this thread's last bounded wait expired
-    for (int i = 0; i < nk; ++i) {
-        const int buf = i % kTcStages;
-        cp_async_wait<kTcStages - 2>();
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the copies, to the tensor cores
-        if (__syncthreads_or(failed))  // every thread leaves together
-            break;
-        if (tid == 0) {
+    } else if (warp == 1 && lane == 0) {  // MMA issuer
+        for (int i = 0; i < nk; ++i) {
+            const int s = i % kTcStages;
+            if (!tc_wait(&full_bar[s], (unsigned)((i / kTcStages) & 1), err))
+                break;
             tc_fence_after();
-            const unsigned st = sbase + (unsigned)(buf * kTcStageBytes);
+            const unsigned st = sbase + (unsigned)(s * kTcStageBytes);
 #pragma unroll
-            for (int s = 0; s < kTcBK / 16; ++s) {  // K-step s: chunks 2s, 2s + 1
-                const uint64_t da = umma_desc(st + (unsigned)(2 * s * kTcBM * 16), kTcBM * 16, 128);
-                const uint64_t dh = umma_desc(st + (unsigned)(kTcWBytes + 2 * s * kTcBN * 16), kTcBN * 16, 128);
+            for (int k = 0; k < kTcBK / 16; ++k) {  // K-step k: chunks 2k, 2k + 1
+                const uint64_t da = umma_desc(st + (unsigned)(2 * k * kTcBM * 16), kTcBM * 16, 128);
+                const uint64_t dh = umma_desc(st + (unsigned)(kTcWBytes + 2 * k * kTcBN * 16), kTcBN * 16, 128);
                 const uint64_t dl =
-                    umma_desc(st + (unsigned)(kTcWBytes + kTcXBytes + 2 * s * kTcBN * 16), kTcBN * 16, 128);
-                tc_mma(tmem, da, dh, (i > 0 || s > 0) ? 1u : 0u);
+                    umma_desc(st + (unsigned)(kTcWBytes + kTcXBytes + 2 * k * kTcBN * 16), kTcBN * 16, 128);
+                tc_mma(tmem, da, dh, (i > 0 || k > 0) ? 1u : 0u);
                 tc_mma(tmem, da, dl, 1u);
             }
-            tc_commit(&stage_bar[buf]);
+            tc_commit(&empty_bar[s]);
         }
-        const int nxt = i + kTcStages - 1;
-        if (nxt < nk) {
-            // the buffer refilled now last held stage i - 1: its MMAs must be complete
-            if (i >= 1 && !tc_wait(&stage_bar[nxt % kTcStages], (unsigned)(((i - 1) / kTcStages) & 1), err))
-                failed = true;
-            if (!failed)
-                load_stage(nxt % kTcStages, kt0 + nxt);
-        }
-        cp_async_commit();
+        tc_commit(&done_bar);  // arrives when every MMA issued above is complete
     }
-    cp_async_wait<0>();
-    if (tid == 0)
-        tc_commit(&done_bar);  // arrives when every MMA this thread issued is complete
-    __syncthreads();
-    const bool ok = __syncthreads_and(tc_wait(&done_bar, 0, err) && !failed);  // uniform over the CTA
+    __syncwarp();
+    const bool ok = __syncthreads_and(nk > 0 && tc_wait(&done_bar, 0, err));  // uniform over the CTA
     tc_fence_after();
     if (ok) {
         // thread l of warp w: feature row n0 + 32w + l, accumulator columns = positions t0 .. t0 + 63
