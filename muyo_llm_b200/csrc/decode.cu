@@ -1674,13 +1674,14 @@ static int pf_alloc(MuyoModel* m)
 
 // K-range splits of a prefill GEMM: enough CTAs for two per SM, each range at least 4 stages long.
 // tc: the tensor-core kernel's 128-row tiles (else the warp-MMA kernel's 64-row tiles).
+// (tc: the persistent kernel's work items, enough for every SM.)
 static int pf_splits(int N, int K, int T, bool tc = false)
 {
-    const int bm = tc ? kTcBM : kPfBM;
-    const int ctas = ((N + bm - 1) / bm) * ((T + kPfBN - 1) / kPfBN);
+    const int bm = tc ? kTcBM : kPfBM, bn = tc ? kTcBN : kPfBN;
+    const int ctas = ((N + bm - 1) / bm) * ((T + bn - 1) / bn);
     const int stages = (K + kPfBK - 1) / kPfBK;
     int S = (2 * sm_count() + ctas - 1) / ctas;
-    S = std::min(S, std::max(1, stages / 4));
+    S = std::min(S, std::max(1, stages / (tc ? 2 : 4)));  // the persistent kernel ramps once per CTA
     return std::max(1, std::min(S, kPfMaxSplits));
 }
 
@@ -1696,10 +1697,10 @@ static int pf_gemm(const __half* w0, const __half* w1, int n_split, int N, int K
     int S = pf_splits(N, K, T, tc != nullptr);
     if ((size_t)S * T * N > part_floats)
         S = 1;
-    if (tc) {
-        const dim3 grid((N + kTcBM - 1) / kTcBM, (T + kTcBN - 1) / kTcBN, S);
-        MUYO_CUDA_TRY(launch_kernel(k_pf_gemm_tc<EPI>, grid, dim3(kTcThreads), kTcSmem, st, true, g, part, err,
-                                    tc->w0, tc->w1, tc->xhi, tc->xlo));
+    if (tc) {  // persistent: one CTA per SM at most, striding over (feature tile, position tile, K range)
+        const int items = ((N + kTcBM - 1) / kTcBM) * ((T + kTcBN - 1) / kTcBN) * S;
+        MUYO_CUDA_TRY(launch_kernel(k_pf_gemm_tc<EPI>, dim3(std::min(items, sm_count())), dim3(kTcThreads), kTcSmem, st,
+                                    true, g, part, err, S, tc->w0, tc->w1, tc->xhi, tc->xlo));
     } else {
         const dim3 grid((N + kPfBM - 1) / kPfBM, (T + kPfBN - 1) / kPfBN, S);
         MUYO_CUDA_TRY(launch_kernel(k_pf_gemm<EPI>, grid, dim3(kPfThreads), kPfGemmSmem, st, true, g, part));

@@ -232,25 +232,29 @@ __global__ void __launch_bounds__(256) k_pf_reduce(PfGemm g, const float* __rest
 }
 
 // ---- the same GEMM on the 5th-generation tensor cores (tcgen05), fed by TMA -------------------------
-// One CTA: 128 feature rows (the UMMA M) x 64 positions (N), warp-specialised:
-//   warp 0, one lane: the producer. Per 64-deep K stage it arms the stage's `full` mbarrier with the
-//     stage's 32 KB and issues 24 two-dimensional TMA tile loads (8 K-chunks of 8 halves for each of
-//     W, x-hi and x-lo), after waiting on the stage's `empty` barrier once the 4-stage ring wraps;
-//   warp 1, one lane: the MMA issuer. It waits on `full`, issues 4 K-steps x 2 MMAs (x-hi, x-lo) into
-//     a 64-column F32 accumulator in tensor memory, and commits them to `empty`; the last commit goes
-//     to `done`;
-//   all four warps: the epilogue, each reading its 32 accumulator lanes (tcgen05.ld 32x32b).
-// A TMA box of 8 halves x R rows lands as R rows x 16 bytes, one column of 8x16-byte core matrices:
-// K-chunk c of an R-row tile sits at c * R * 16, so the UMMA descriptors are K-major and unswizzled
-// with a leading-byte offset of R * 16 (the two K halves of a 16-deep step) and a stride-byte offset
-// of 128 (8-row groups). Rows and columns outside the tensors are zero-filled by the TMA. Every wait is
+// Persistent CTAs (one per SM) over work items = (128-feature tile, 128-position tile, K range);
+// 6 warps with fixed roles:
+//   warp 4, one lane: the producer. Per 64-deep K stage it arms the stage's `full` mbarrier with the
+//     stage's 48 KB and issues 24 two-dimensional TMA tile loads (8 K-chunks of 8 halves for each of
+//     W, x-hi and x-lo), waiting on the stage's `empty` barrier once the 4-stage ring wraps; it runs
+//     ahead across work items;
+//   warp 5: allocates 256 tensor-memory columns (two 128-column F32 accumulators); its lane 0 is the
+//     MMA issuer: it waits on `full`, issues 4 K-steps x 2 MMAs (x-hi, x-lo) of 128 x 128 x 16, and
+//     commits each stage to `empty`; at the end of a work item it commits the accumulator to
+//     `acc_full` (after waiting on `acc_empty` before reusing a buffer);
+//   warps 0-3: the epilogue. Warp w reads accumulator lanes 32w .. 32w + 31 (tcgen05.ld 32x32b),
+//     stores, and arrives on `acc_empty`; the MMA issuer meanwhile fills the other accumulator.
+// A TMA box of 8 halves x 128 rows lands as 128 rows x 16 bytes, one column of 8x16-byte core matrices:
+// K-chunk c of a tile sits at c * 2048, so the UMMA descriptors are K-major and unswizzled with a
+// leading-byte offset of 2048 (the two K halves of a 16-deep step) and a stride-byte offset of 128
+// (8-row groups). Rows and columns outside the tensors are zero-filled by the TMA. Every wait is
 // bounded (2 s): on expiry the error word gets 6, the roles stop, and the CTA still frees its TMEM.
-constexpr int kTcBM = 128, kTcBN = 64, kTcBK = 64, kTcStages = 4, kTcThreads = 128;
+constexpr int kTcBM = 128, kTcBN = 128, kTcBK = 64, kTcStages = 4, kTcThreads = 192;
 constexpr int kTcWBytes = kTcBM * kTcBK * 2;               // 16 KB
-constexpr int kTcXBytes = kTcBN * kTcBK * 2;               // 8 KB
-constexpr int kTcStageBytes = kTcWBytes + 2 * kTcXBytes;   // 32 KB
+constexpr int kTcXBytes = kTcBN * kTcBK * 2;               // 16 KB
+constexpr int kTcStageBytes = kTcWBytes + 2 * kTcXBytes;   // 48 KB
 constexpr size_t kTcSmem = (size_t)kTcStages * kTcStageBytes + 1024;  // + alignment slack
-constexpr int kTcTmemCols = 64;
+constexpr int kTcTmemCols = 2 * kTcBN;                     // two accumulators
 
 // UMMA shared-memory descriptor: start >> 4 in [0,14), leading-byte offset >> 4 in [16,30),
 // stride-byte offset >> 4 in [32,46), version 1 in [46,48), no swizzle (layout 0 in [61,64)).
@@ -321,20 +325,21 @@ __device__ __forceinline__ void tma_load_2d(unsigned dst, const void* map, int x
         : "memory");
 }
 
-// The tile's W rows come from tw0 (rows n0 .. ) or, past n_split (a multiple of 128), from tw1.
+// The tile's W rows come from tw0 or, past n_split (a multiple of 128), from tw1 (row n - n_split).
 template <int EPI>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    k_pf_gemm_tc(PfGemm g, float* part, int* err, const __grid_constant__ CUtensorMap tw0,
+    k_pf_gemm_tc(PfGemm g, float* part, int* err, int S, const __grid_constant__ CUtensorMap tw0,
                  const __grid_constant__ CUtensorMap tw1, const __grid_constant__ CUtensorMap txh,
                  const __grid_constant__ CUtensorMap txl)
 {
     extern __shared__ unsigned char tc_raw[];
     __shared__ __align__(8) uint64_t full_bar[kTcStages];
     __shared__ __align__(8) uint64_t empty_bar[kTcStages];
-    __shared__ __align__(8) uint64_t done_bar;
+    __shared__ __align__(8) uint64_t acc_full[2];
+    __shared__ __align__(8) uint64_t acc_empty[2];
     __shared__ uint32_t tmem_base;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    if (warp == 0) {
+    if (warp == 5) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
                      "r"(kTcTmemCols)
                      : "memory");
@@ -345,10 +350,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_init(&full_bar[s], 1);
             mbar_init(&empty_bar[s], 1);
         }
-        mbar_init(&done_bar, 1);
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&acc_full[a], 1);
+            mbar_init(&acc_empty[a], 128);  // every epilogue thread arrives
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tw0)) : "memory");
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&txh)) : "memory");
     }
     tc_fence_before();
     __syncthreads();
@@ -357,85 +363,128 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     pdl_wait();  // x comes from the previous kernel: no TMA load before this point
     pdl_trigger();
     const unsigned sbase = (smem_u32(tc_raw) + 1023u) & ~1023u;  // 1 KB-aligned ring
-    const int n0 = blockIdx.x * kTcBM, t0 = blockIdx.y * kTcBN;
-    const int nk_all = (g.K + kTcBK - 1) / kTcBK, S = gridDim.z, z = blockIdx.z;
-    const int kt0 = (int)((long long)nk_all * z / S), kt1 = (int)((long long)nk_all * (z + 1) / S);
-    const int nk = kt1 - kt0;
+    const int ntn = (g.N + kTcBM - 1) / kTcBM, ntt = (g.T + kTcBN - 1) / kTcBN;  // S: K ranges
+    const int nk_all = (g.K + kTcBK - 1) / kTcBK, items = ntn * ntt * S;
+    // work item -> (feature tile, position tile, K range [kt0, kt1))
+    auto item_geom = [&](int it, int& n0, int& t0, int& z, int& kt0, int& kt1) {
+        n0 = (it % ntn) * kTcBM;
+        t0 = ((it / ntn) % ntt) * kTcBN;
+        z = it / (ntn * ntt);
+        kt0 = (int)((long long)nk_all * z / S);
+        kt1 = (int)((long long)nk_all * (z + 1) / S);
+    };
 
-    if (warp == 0 && lane == 0) {  // producer
-        const CUtensorMap* tw = n0 < g.n_split ? &tw0 : &tw1;
-        const int wrow = n0 < g.n_split ? n0 : n0 - g.n_split;
-        for (int i = 0; i < nk; ++i) {
-            const int s = i % kTcStages;
-            if (i >= kTcStages && !tc_wait(&empty_bar[s], (unsigned)(((i / kTcStages) - 1) & 1), err))
-                break;
-            mbar_expect_tx(&full_bar[s], (unsigned)kTcStageBytes);
-            const unsigned st = sbase + (unsigned)(s * kTcStageBytes);
-            const int k0 = (kt0 + i) * kTcBK;
+    if (warp == 4) {
+        if (lane == 0) {  // producer
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tw0)) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&txh)) : "memory");
+            int gs = 0;  // stages issued by this CTA
+            bool stop = false;
+            for (int it = blockIdx.x; it < items && !stop; it += gridDim.x) {
+                int n0, t0, z, kt0, kt1;
+                item_geom(it, n0, t0, z, kt0, kt1);
+                const CUtensorMap* tw = n0 < g.n_split ? &tw0 : &tw1;
+                const int wrow = n0 < g.n_split ? n0 : n0 - g.n_split;
+                for (int kt = kt0; kt < kt1; ++kt, ++gs) {
+                    const int s = gs % kTcStages;
+                    if (gs >= kTcStages && !tc_wait(&empty_bar[s], (unsigned)(((gs / kTcStages) - 1) & 1), err)) {
+                        stop = true;
+                        break;
+                    }
+                    mbar_expect_tx(&full_bar[s], (unsigned)kTcStageBytes);
+                    const unsigned st = sbase + (unsigned)(s * kTcStageBytes);
+                    const int k0 = kt * kTcBK;
 #pragma unroll
-            for (int c = 0; c < kTcBK / 8; ++c) {
-                tma_load_2d(st + (unsigned)(c * kTcBM * 16), tw, k0 + 8 * c, wrow, &full_bar[s]);
-                tma_load_2d(st + (unsigned)(kTcWBytes + c * kTcBN * 16), &txh, k0 + 8 * c, t0, &full_bar[s]);
-                tma_load_2d(st + (unsigned)(kTcWBytes + kTcXBytes + c * kTcBN * 16), &txl, k0 + 8 * c, t0,
-                            &full_bar[s]);
-            }
-        }
-    } else if (warp == 1 && lane == 0) {  // MMA issuer
-        for (int i = 0; i < nk; ++i) {
-            const int s = i % kTcStages;
-            if (!tc_wait(&full_bar[s], (unsigned)((i / kTcStages) & 1), err))
-                break;
-            tc_fence_after();
-            const unsigned st = sbase + (unsigned)(s * kTcStageBytes);
-#pragma unroll
-            for (int k = 0; k < kTcBK / 16; ++k) {  // K-step k: chunks 2k, 2k + 1
-                const uint64_t da = umma_desc(st + (unsigned)(2 * k * kTcBM * 16), kTcBM * 16, 128);
-                const uint64_t dh = umma_desc(st + (unsigned)(kTcWBytes + 2 * k * kTcBN * 16), kTcBN * 16, 128);
-                const uint64_t dl =
-                    umma_desc(st + (unsigned)(kTcWBytes + kTcXBytes + 2 * k * kTcBN * 16), kTcBN * 16, 128);
-                tc_mma(tmem, da, dh, (i > 0 || k > 0) ? 1u : 0u);
-                tc_mma(tmem, da, dl, 1u);
-            }
-            tc_commit(&empty_bar[s]);
-        }
-        tc_commit(&done_bar);  // arrives when every MMA issued above is complete
-    }
-    __syncwarp();
-    const bool ok = __syncthreads_and(nk > 0 && tc_wait(&done_bar, 0, err));  // uniform over the CTA
-    tc_fence_after();
-    if (ok) {
-        // thread l of warp w: feature row n0 + 32w + l, accumulator columns = positions t0 .. t0 + 63
-        const int n = n0 + warp * 32 + lane;
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-            uint32_t r[32];
-            tc_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(half * 32), r);
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            if (n < g.N) {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int t = t0 + half * 32 + j;
-                    if (t < g.T) {
-                        const float v0 = __uint_as_float(r[j]);
-                        if (S > 1) {
-                            part[((size_t)z * g.T + t) * g.N + n] = v0;
-                        } else {
-                            float* yp = g.y + (size_t)t * g.ldy + n;
-                            float v = v0;
-                            if (EPI == PF_BIAS)
-                                v = v + g.bias[n];
-                            if (EPI == PF_ADD)
-                                v = *yp + v;
-                            *yp = v;
-                        }
+                    for (int c = 0; c < kTcBK / 8; ++c) {
+                        tma_load_2d(st + (unsigned)(c * kTcBM * 16), tw, k0 + 8 * c, wrow, &full_bar[s]);
+                        tma_load_2d(st + (unsigned)(kTcWBytes + c * kTcBN * 16), &txh, k0 + 8 * c, t0, &full_bar[s]);
+                        tma_load_2d(st + (unsigned)(kTcWBytes + kTcXBytes + c * kTcBN * 16), &txl, k0 + 8 * c, t0,
+                                    &full_bar[s]);
                     }
                 }
             }
         }
+    } else if (warp == 5) {
+        if (lane == 0) {  // MMA issuer
+            int gs = 0, j = 0;  // stages consumed, work items done by this CTA
+            bool stop = false;
+            for (int it = blockIdx.x; it < items && !stop; it += gridDim.x, ++j) {
+                int n0, t0, z, kt0, kt1;
+                item_geom(it, n0, t0, z, kt0, kt1);
+                const int a = j & 1;
+                if (j >= 2 && !tc_wait(&acc_empty[a], (unsigned)(((j >> 1) - 1) & 1), err))
+                    break;
+                tc_fence_after();
+                const uint32_t acc = tmem + (uint32_t)(a * kTcBN);
+                for (int kt = kt0; kt < kt1; ++kt, ++gs) {
+                    const int s = gs % kTcStages;
+                    if (!tc_wait(&full_bar[s], (unsigned)((gs / kTcStages) & 1), err)) {
+                        stop = true;
+                        break;
+                    }
+                    tc_fence_after();
+                    const unsigned st = sbase + (unsigned)(s * kTcStageBytes);
+#pragma unroll
+                    for (int k = 0; k < kTcBK / 16; ++k) {  // K-step k: chunks 2k, 2k + 1
+                        const uint64_t da = umma_desc(st + (unsigned)(2 * k * kTcBM * 16), kTcBM * 16, 128);
+                        const uint64_t dh = umma_desc(st + (unsigned)(kTcWBytes + 2 * k * kTcBN * 16), kTcBN * 16, 128);
+                        const uint64_t dl =
+                            umma_desc(st + (unsigned)(kTcWBytes + kTcXBytes + 2 * k * kTcBN * 16), kTcBN * 16, 128);
+                        tc_mma(acc, da, dh, (kt > kt0 || k > 0) ? 1u : 0u);
+                        tc_mma(acc, da, dl, 1u);
+                    }
+                    tc_commit(&empty_bar[s]);
+                }
+                tc_commit(&acc_full[a]);  // the item's accumulator is complete once its MMAs are
+            }
+        }
+    } else {  // epilogue: warps 0-3, warp w owns accumulator lanes (feature rows) 32w .. 32w + 31
+        int j = 0;
+        for (int it = blockIdx.x; it < items; it += gridDim.x, ++j) {
+            int n0, t0, z, kt0, kt1;
+            item_geom(it, n0, t0, z, kt0, kt1);
+            const int a = j & 1;
+            bool ok = true;
+            if (lane == 0)
+                ok = tc_wait(&acc_full[a], (unsigned)((j >> 1) & 1), err);
+            ok = __shfl_sync(0xffffffffu, ok, 0);  // one decision per warp (tcgen05.ld is warp-wide)
+            if (!ok)
+                break;
+            tc_fence_after();
+            const int n = n0 + warp * 32 + lane;
+#pragma unroll 1
+            for (int q = 0; q < kTcBN / 32; ++q) {
+                uint32_t r[32];
+                tc_ld32(tmem + (uint32_t)(a * kTcBN) + ((uint32_t)(warp * 32) << 16) + (uint32_t)(q * 32), r);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (n < g.N) {
+#pragma unroll
+                    for (int c = 0; c < 32; ++c) {
+                        const int t = t0 + q * 32 + c;
+                        if (t < g.T) {
+                            const float v0 = __uint_as_float(r[c]);
+                            if (S > 1) {
+                                part[((size_t)z * g.T + t) * g.N + n] = v0;
+                            } else {
+                                float* yp = g.y + (size_t)t * g.ldy + n;
+                                float v = v0;
+                                if (EPI == PF_BIAS)
+                                    v = v + g.bias[n];
+                                if (EPI == PF_ADD)
+                                    v = *yp + v;
+                                *yp = v;
+                            }
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&acc_empty[a]);
+        }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) {
+    if (warp == 5) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcTmemCols) : "memory");
     }
