@@ -23,7 +23,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CU_SOURCES = ["runtime.cu", "ops.cu", "decode.cu", "sampler.cu"]
 CPP_SOURCES = ["gguf_loader.cpp"]
 HOST = os.path.join(PKG, "host")
-HOST_SOURCES = ["checks.cpp", "forward.cpp", "main.cpp"]
+HOST_SOURCES = ["checks.cpp", "forward.cpp", "main.cpp", "gguf_meta.cpp", "tokenizer.cpp"]
 HOST_BIN = os.path.join(LIBDIR, "muyo-llm")  # the C++ command line over the library
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 
@@ -73,7 +73,8 @@ def build_host() -> str:
     """The muyo-llm command line (host/): g++ against include/ and libmuyo_cuda.so (found beside it
     through $ORIGIN), with the CUDA runtime for its own device buffers."""
     srcs = [os.path.join(HOST, f) for f in HOST_SOURCES]
-    deps = srcs + [os.path.join(HOST, "host.h"), os.path.join(INCLUDE, "muyo_cuda.h"), LIB]
+    deps = srcs + [os.path.join(HOST, f) for f in ("host.h", "gguf_meta.h", "tokenizer.h", "unicode_classes.inc")]
+    deps += [os.path.join(INCLUDE, "muyo_cuda.h"), LIB]
     if _newer(HOST_BIN, deps):
         cxx = shutil.which("g++") or "g++"
         cmd = [cxx, "-O2", "-std=c++17", "-Wall", "-I", INCLUDE, "-I", HOST, "-I", os.path.join(CUDA_HOME, "include")]

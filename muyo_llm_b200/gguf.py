@@ -37,6 +37,9 @@ def _w_kv(f: BinaryIO, key: str, value) -> None:
         f.write(struct.pack("<If", _F32, value))
     elif isinstance(value, int):
         f.write(struct.pack("<II", _U32, value))
+    elif isinstance(value, list) and value and all(isinstance(v, int) for v in value):
+        f.write(struct.pack("<IIQ", _ARR, _I32, len(value)))  # e.g. tokenizer.ggml.token_type
+        f.write(np.asarray(value, dtype="<i4").tobytes())
     elif isinstance(value, list):
         f.write(struct.pack("<IIQ", _ARR, _STR, len(value)))
         for s in value:
@@ -96,9 +99,80 @@ def write_gguf(path: str, metadata: dict, tensors: dict[str, np.ndarray]) -> Non
             f.write(b"\0" * ((-len(b)) % _ALIGN))
 
 
-def write_synthetic_qwen2(path: str, cfg: Qwen2Config, seed: int) -> None:
-    """Write the seeded random-init model of ``synth.make_model`` as a Qwen2 GGUF."""
-    write_gguf(path, qwen2_metadata(cfg), make_model(cfg, seed))
+def gpt2_byte_symbols() -> tuple[list[str], dict[int, str]]:
+    """GPT-2's byte -> code point map as the 256 one-symbol tokens, in the order byte-level BPE
+    vocabularies list them: the bytes that stand for themselves ('!'..'~', 0xA1..0xAC, 0xAE..0xFF),
+    then the other 68 bytes as U+0100.. (so token 0 is "!", as in the Qwen2 and GPT-2 vocabularies)."""
+    own = [b for b in range(256) if 0x21 <= b <= 0x7E or 0xA1 <= b <= 0xAC or b >= 0xAE]
+    rest = [b for b in range(256) if b not in own]
+    cp = {b: b for b in own} | {b: 256 + i for i, b in enumerate(rest)}
+    return [chr(cp[b]) for b in own + rest], {b: chr(cp[b]) for b in range(256)}
+
+
+SPECIALS = ["<|endoftext|>", "<|im_start|>", "<|im_end|>"]
+
+
+def bpe_tokenizer(vocab: int, corpus: str, pre: str = "qwen2") -> dict:
+    """A byte-level BPE vocabulary of exactly ``vocab`` tokens trained on ``corpus``: the 256 byte
+    symbols, ``vocab - 259`` merges (most frequent adjacent pair first, words split at spaces with
+    the space kept in front) and the three Qwen2 special tokens (CONTROL, token type 3) at the end.
+    Returns the tokenizer.ggml.* metadata, with eos = <|im_end|> and bos = <|endoftext|> as in the
+    Qwen2.5 files."""
+    symbols, enc = gpt2_byte_symbols()
+    n_merges = vocab - 256 - len(SPECIALS)
+    assert n_merges >= 0, vocab
+    words: dict[tuple[str, ...], int] = {}
+    for i, w in enumerate(corpus.split(" ")):
+        piece = (" " if i else "") + w
+        key = tuple(enc[b] for b in piece.encode())
+        if key:
+            words[key] = words.get(key, 0) + 1
+    tokens, merges = list(symbols), []
+    while len(merges) < n_merges:
+        pairs: dict[tuple[str, str], int] = {}
+        for w, c in words.items():
+            for a, b in zip(w, w[1:]):
+                pairs[(a, b)] = pairs.get((a, b), 0) + c
+        if not pairs:
+            break
+        best = min(pairs, key=lambda p: (-pairs[p], p))
+        merges.append(f"{best[0]} {best[1]}")
+        tokens.append(best[0] + best[1])
+        merged = {}
+        for w, c in words.items():
+            out, i = [], 0
+            while i < len(w):
+                if i + 1 < len(w) and (w[i], w[i + 1]) == best:
+                    out.append(w[i] + w[i + 1])
+                    i += 2
+                else:
+                    out.append(w[i])
+                    i += 1
+            merged[tuple(out)] = merged.get(tuple(out), 0) + c
+        words = merged
+    while len(tokens) < vocab - len(SPECIALS):  # a corpus too small for the merges asked
+        tokens.append(f"<unused{len(tokens)}>")
+    tokens += SPECIALS
+    types = [1] * (vocab - len(SPECIALS)) + [3] * len(SPECIALS)
+    return {
+        "tokenizer.ggml.model": "gpt2",
+        "tokenizer.ggml.pre": pre,
+        "tokenizer.ggml.tokens": tokens,
+        "tokenizer.ggml.token_type": types,
+        "tokenizer.ggml.merges": merges,
+        "tokenizer.ggml.bos_token_id": vocab - 3,
+        "tokenizer.ggml.eos_token_id": vocab - 1,
+    }
+
+
+def write_synthetic_qwen2(path: str, cfg: Qwen2Config, seed: int, tokenizer: dict | None = None) -> None:
+    """Write the seeded random-init model of ``synth.make_model`` as a Qwen2 GGUF; ``tokenizer``
+    (tokenizer.ggml.* keys, e.g. from ``bpe_tokenizer``) replaces the placeholder vocabulary."""
+    meta = qwen2_metadata(cfg)
+    if tokenizer is not None:
+        assert len(tokenizer["tokenizer.ggml.tokens"]) == cfg.vocab
+        meta.update(tokenizer)
+    write_gguf(path, meta, make_model(cfg, seed))
 
 
 def read_gguf(path: str) -> tuple[dict, dict[str, tuple[int, tuple[int, ...], int]], int]:

@@ -25,8 +25,9 @@ struct SamplerParams
     uint64_t seed = 0;
 };
 
-/// src/FullModel.h:12-21. Text prompts, chat framing and interactive turns need the tokenizer,
-/// which is outside this build: RunFullModel takes token ids.
+/// src/FullModel.h:12-21: a text prompt (run through the GGUF's tokenizer) or ids, the generation
+/// budget, the sampler and the chat controls (--chat frames the prompt as a ChatML turn; interactive
+/// reads further user turns from stdin).
 struct ForwardOptions
 {
     std::vector<int32_t> tokens;
@@ -50,8 +51,13 @@ int RunAttention();
 int RunKvCache();
 int RunTransformerLayer();
 
-/// Loads a Qwen2 GGUF (F16/F32 tensors), feeds options.tokens one position at a time and greedily
-/// generates options.nPredict ids, printed to stdout as a comma-separated list.
-/// @return 0 on success, 1 on a load or device failure, 2 for options this build does not support.
+/// Loads a Qwen2 GGUF (F16/F32 tensors and its tokenizer), feeds the prompt and generates up to
+/// options.nPredict ids, stopping after tokenizer.ggml.eos_token_id: the reply's text goes to stdout,
+/// its ids to stderr ("[forward] generated N tokens: ...").
+/// @return 0 on success, 1 on a load, tokenizer or device failure.
 int RunFullModel(const std::string& ggufPath, const ForwardOptions& options);
+
+/// src/Tokenize.cpp:12-48: prints the ids of `text`, checks that they decode back to it exactly and,
+/// when token 0 is "!", that "!" encodes to {0}. No device. @return 0 when both hold, else 1.
+int RunTokenize(const std::string& ggufPath, const std::string& text);
 }  // namespace muyo_llm

@@ -1,6 +1,6 @@
 // muyo-llm command line (src/main.cpp:186-431): the same mode flags and exit codes (0 ok, 1 check
-// failed or error, 2 usage) for the decode-step modes, run on the B200 kernels. The modes of the
-// reference that are not part of the decode step (--smoke, --gguf, --model, --tokenize, --embed)
+// failed or error, 2 usage) for the decode-step modes and --tokenize, run on the B200 kernels. The
+// modes of the reference that are not part of the decode step (--smoke, --gguf, --model, --embed)
 // exit with 2 and say so.
 #include <cstdio>
 #include <cstdlib>
@@ -31,8 +31,9 @@ void Usage(const char* argv0)
 {
     std::fprintf(stderr,
                  "usage: %s --add | --matvec | --rmsnorm | --rope | --swiglu | --getrows | --argmax | --softmax |\n"
-                 "       --attention | --kvcache | --layer | --forward <gguf> --tokens id,id [-n N] [--temp T] [--top-k K]\n"
-                 "       [--top-p P] [--repeat-penalty R] [--repeat-last-n N] [--seed S]\n",
+                 "       --attention | --kvcache | --layer | --tokenize <gguf> <text> |\n"
+                 "       --forward <gguf> [-p TEXT | --tokens id,id] [--chat] [-i] [--system TEXT] [-n N] [--temp T]\n"
+                 "       [--top-k K] [--top-p P] [--repeat-penalty R] [--repeat-last-n N] [--seed S]\n",
                  argv0);
 }
 }  // namespace
@@ -40,11 +41,24 @@ void Usage(const char* argv0)
 int main(int argc, char** argv)
 {
     const std::string mode = argc > 1 ? argv[1] : "";
-    for (const char* other : {"--smoke", "--gguf", "--model", "--tokenize", "--embed"})
+    for (const char* other : {"--smoke", "--gguf", "--model", "--embed"})
         if (mode == other) {
             std::fprintf(stderr, "%s is not part of this build (the decode-step kernels only)\n", other);
             return 2;
         }
+    // --tokenize reads the GGUF's tokenizer; it needs no device (src/main.cpp:209-226).
+    if (mode == "--tokenize") {
+        if (argc < 4) {
+            std::fprintf(stderr, "usage: %s --tokenize <gguf> <text>\n", argv[0]);
+            return 2;
+        }
+        try {
+            return muyo_llm::RunTokenize(argv[2], argv[3]);
+        } catch (const std::exception& e) {
+            std::fprintf(stderr, "[fail] %s\n", e.what());
+            return 1;
+        }
+    }
     try {
         if (mode == "--add")
             return muyo_llm::RunElementwiseAdd();
@@ -74,6 +88,7 @@ int main(int argc, char** argv)
                 return 2;
             }
             muyo_llm::ForwardOptions options;
+            bool chosePrompt = false;
             for (int i = 3; i < argc; ++i) {
                 const std::string arg = argv[i];
                 auto value = [&](const char* name) -> std::string {
@@ -81,10 +96,15 @@ int main(int argc, char** argv)
                         throw std::invalid_argument(std::string(name) + " needs a value");
                     return argv[++i];
                 };
-                if (arg == "-p" || arg == "--prompt")
+                if (arg == "-p" || arg == "--prompt") {
                     options.prompt = value("--prompt");
-                else if (arg == "--tokens")
+                    options.tokens.clear();
+                    chosePrompt = true;
+                } else if (arg == "--tokens") {
                     options.tokens = ParseTokens(value("--tokens"));
+                    options.prompt.clear();
+                    chosePrompt = true;
+                }
                 else if (arg == "-n" || arg == "--n-predict")
                     options.nPredict = (uint32_t)std::stoul(value("--n-predict"));
                 else if (arg == "--temp" || arg == "--temperature")
@@ -102,13 +122,18 @@ int main(int argc, char** argv)
                 else if (arg == "--chat")
                     options.chat = true;
                 else if (arg == "-i" || arg == "--interactive")
-                    options.interactive = true;
+                    options.chat = options.interactive = true;
                 else if (arg == "--system")
                     options.system = value("--system");
                 else {
                     std::fprintf(stderr, "unknown --forward option: %s\n", arg.c_str());
                     return 2;
                 }
+            }
+            if (!chosePrompt && !options.chat) {
+                // A completion needs a prompt; in chat mode an empty prompt means "no initial turn".
+                options.prompt = "Hello world";
+                std::fprintf(stderr, "[forward] no -p/--tokens given, using -p \"%s\"\n", options.prompt.c_str());
             }
             return muyo_llm::RunFullModel(argv[2], options);
         }

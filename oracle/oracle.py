@@ -265,8 +265,12 @@ class Sampler:
 REF_SAMPLER = os.path.join(HERE, "_ref", "libsampler_ref.so")
 
 
+REF_TOKENIZER = os.path.join(HERE, "_ref", "libtokenizer_ref.so")
+
+
 def build_ref() -> str | None:
-    """Compile the reference's own sampler into oracle/_ref (needs the reference tree); None if absent."""
+    """Compile the reference's own sampler and tokenizer into oracle/_ref (needs the reference tree);
+    returns the sampler's path, None if neither the tree nor a built copy is there."""
     if not os.path.exists(os.path.join("/root/reference", "src", "Sampler.cpp")):
         return REF_SAMPLER if os.path.exists(REF_SAMPLER) else None
     subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
@@ -293,5 +297,52 @@ class RefSampler:
     def __del__(self):
         try:
             self.L.ref_sampler_destroy(self.h)
+        except Exception:
+            pass
+
+
+class RefTokenizer:
+    """The reference's Tokenizer itself (oracle/_ref/libtokenizer_ref.so, built from src/Tokenizer.cpp,
+    src/Gguf.cpp and the vendored llama.cpp unicode code) over a GGUF file."""
+
+    def __init__(self, path: str):
+        L = C.CDLL(REF_TOKENIZER)
+        L.ref_tok_open.restype = C.c_void_p
+        L.ref_tok_open.argtypes = [C.c_char_p]
+        L.ref_tok_close.argtypes = [C.c_void_p]
+        L.ref_tok_encode.restype = C.c_long
+        L.ref_tok_encode.argtypes = [C.c_void_p, C.c_char_p, C.c_long, C.c_int, C.POINTER(C.c_int), C.c_long]
+        L.ref_tok_decode.restype = C.c_long
+        L.ref_tok_decode.argtypes = [C.c_void_p, C.POINTER(C.c_int), C.c_long, C.c_char_p, C.c_long]
+        L.ref_unicode_flags.argtypes = [C.c_uint, C.c_uint, C.POINTER(C.c_ushort)]
+        self.L = L
+        self.h = L.ref_tok_open(path.encode())
+        if not self.h:
+            raise RuntimeError(f"reference tokenizer could not open {path}")
+
+    def encode(self, text: bytes, parse_special: bool = True) -> list[int]:
+        buf = (C.c_int * (4 * len(text) + 8))()
+        n = self.L.ref_tok_encode(self.h, text, len(text), int(parse_special), buf, len(buf))
+        return list(buf[:n])
+
+    def decode(self, ids) -> bytes:
+        arr = (C.c_int * max(1, len(ids)))(*ids)
+        cap = 64 * len(ids) + 16
+        out = C.create_string_buffer(cap)
+        n = self.L.ref_tok_decode(self.h, arr, len(ids), out, cap)
+        return out.raw[:n]
+
+    @staticmethod
+    def unicode_flags() -> np.ndarray:
+        """llama.cpp's 16-bit flags of every code point (0x4 letter, 0x2 number, 0x100 white space)."""
+        L = C.CDLL(REF_TOKENIZER)
+        L.ref_unicode_flags.argtypes = [C.c_uint, C.c_uint, C.POINTER(C.c_ushort)]
+        f = np.zeros(0x110000, np.uint16)
+        L.ref_unicode_flags(0, f.size, f.ctypes.data_as(C.POINTER(C.c_ushort)))
+        return f
+
+    def __del__(self):
+        try:
+            self.L.ref_tok_close(self.h)
         except Exception:
             pass
