@@ -1608,8 +1608,9 @@ static EncodeTiledFn encode_tiled()
     return fn;
 }
 
-// F16 matrix [rows][cols] with row stride ld halves, read in boxes of 8 halves x box_rows rows
-// (unswizzled; outside the matrix the box is zero-filled). cols, ld multiples of 8; base 16-byte aligned.
+// F16 matrix [rows][cols] with row stride ld halves, read in boxes of 64 halves x box_rows rows with
+// the 128-byte swizzle (the tcgen05 GEMM's operand layout; outside the matrix the box is zero-filled).
+// cols, ld multiples of 8; base 16-byte aligned.
 static int make_map(CUtensorMap* map, const void* base, int cols, int rows, int ld, int box_rows)
 {
     EncodeTiledFn fn = encode_tiled();
@@ -1619,10 +1620,10 @@ static int make_map(CUtensorMap* map, const void* base, int cols, int rows, int 
     }
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
-    const cuuint32_t box[2] = {8, (cuuint32_t)box_rows};
+    const cuuint32_t box[2] = {(cuuint32_t)kTcBK, (cuuint32_t)box_rows};  // 128-byte rows, swizzled
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         set_error("prefill: cuTensorMapEncodeTiled failed (%d) for a %d x %d matrix", (int)r, rows, cols);

@@ -244,11 +244,13 @@ __global__ void __launch_bounds__(256) k_pf_reduce(PfGemm g, const float* __rest
 //     `acc_full` (after waiting on `acc_empty` before reusing a buffer);
 //   warps 0-3: the epilogue. Warp w reads accumulator lanes 32w .. 32w + 31 (tcgen05.ld 32x32b),
 //     stores, and arrives on `acc_empty`; the MMA issuer meanwhile fills the other accumulator.
-// A TMA box of 8 halves x 128 rows lands as 128 rows x 16 bytes, one column of 8x16-byte core matrices:
-// K-chunk c of a tile sits at c * 2048, so the UMMA descriptors are K-major and unswizzled with a
-// leading-byte offset of 2048 (the two K halves of a 16-deep step) and a stride-byte offset of 128
-// (8-row groups). Rows and columns outside the tensors are zero-filled by the TMA. Every wait is
-// bounded (2 s): on expiry the error word gets 6, the roles stop, and the CTA still frees its TMEM.
+// Each operand tile of a stage is ONE TMA box of 64 halves x 128 rows (16 KB) with the 128-byte
+// swizzle: row r's 128 bytes sit at r * 128 with their 16-byte chunks permuted by r mod 8, the
+// canonical K-major SWIZZLE_128B layout. The UMMA descriptors name that layout (stride-byte offset
+// 1024 between 8-row groups); K-step k of the 64-deep stage starts 32 * k bytes into the tile, and
+// the hardware applies the same permutation to the advanced address (tiles are 1 KB-aligned). Rows
+// and columns outside the tensors are zero-filled by the TMA. Every wait is bounded (2 s): on expiry
+// the error word gets 6, the roles stop, and the CTA still frees its TMEM.
 constexpr int kTcBM = 128, kTcBN = 128, kTcBK = 64, kTcStages = 4, kTcThreads = 192;
 constexpr int kTcWBytes = kTcBM * kTcBK * 2;               // 16 KB
 constexpr int kTcXBytes = kTcBN * kTcBK * 2;               // 16 KB
@@ -256,12 +258,14 @@ constexpr int kTcStageBytes = kTcWBytes + 2 * kTcXBytes;   // 48 KB
 constexpr size_t kTcSmem = (size_t)kTcStages * kTcStageBytes + 1024;  // + alignment slack
 constexpr int kTcTmemCols = 2 * kTcBN;                     // two accumulators
 
-// UMMA shared-memory descriptor: start >> 4 in [0,14), leading-byte offset >> 4 in [16,30),
-// stride-byte offset >> 4 in [32,46), version 1 in [46,48), no swizzle (layout 0 in [61,64)).
-__device__ __forceinline__ uint64_t umma_desc(unsigned saddr, unsigned lbo, unsigned sbo)
+// UMMA shared-memory descriptor of a K-major SWIZZLE_128B tile: start >> 4 in [0,14), leading-byte
+// offset in [16,30) (unused by swizzled K-major layouts; 1), stride-byte offset 1024 >> 4 in
+// [32,46), version 1 in [46,48), base offset 0 in [49,52) (1 KB-aligned tiles), layout 2 (128-byte
+// swizzle) in [61,64).
+__device__ __forceinline__ uint64_t umma_desc_sw128(unsigned saddr)
 {
-    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
-           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
+           (2ull << 61);
 }
 
 // Instruction descriptor, kind::f16: F32 accumulator (bits [4,6) = 1), A and B F16 (0), both
@@ -394,13 +398,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     mbar_expect_tx(&full_bar[s], (unsigned)kTcStageBytes);
                     const unsigned st = sbase + (unsigned)(s * kTcStageBytes);
                     const int k0 = kt * kTcBK;
-#pragma unroll
-                    for (int c = 0; c < kTcBK / 8; ++c) {
-                        tma_load_2d(st + (unsigned)(c * kTcBM * 16), tw, k0 + 8 * c, wrow, &full_bar[s]);
-                        tma_load_2d(st + (unsigned)(kTcWBytes + c * kTcBN * 16), &txh, k0 + 8 * c, t0, &full_bar[s]);
-                        tma_load_2d(st + (unsigned)(kTcWBytes + kTcXBytes + c * kTcBN * 16), &txl, k0 + 8 * c, t0,
-                                    &full_bar[s]);
-                    }
+                    tma_load_2d(st, tw, k0, wrow, &full_bar[s]);
+                    tma_load_2d(st + (unsigned)kTcWBytes, &txh, k0, t0, &full_bar[s]);
+                    tma_load_2d(st + (unsigned)(kTcWBytes + kTcXBytes), &txl, k0, t0, &full_bar[s]);
                 }
             }
         }
@@ -425,11 +425,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     tc_fence_after();
                     const unsigned st = sbase + (unsigned)(s * kTcStageBytes);
 #pragma unroll
-                    for (int k = 0; k < kTcBK / 16; ++k) {  // K-step k: chunks 2k, 2k + 1
-                        const uint64_t da = umma_desc(st + (unsigned)(2 * k * kTcBM * 16), kTcBM * 16, 128);
-                        const uint64_t dh = umma_desc(st + (unsigned)(kTcWBytes + 2 * k * kTcBN * 16), kTcBN * 16, 128);
-                        const uint64_t dl =
-                            umma_desc(st + (unsigned)(kTcWBytes + kTcXBytes + 2 * k * kTcBN * 16), kTcBN * 16, 128);
+                    for (int k = 0; k < kTcBK / 16; ++k) {  // K-step k: bytes 32k .. 32k + 31 of each row
+                        const uint64_t da = umma_desc_sw128(st + (unsigned)(32 * k));
+                        const uint64_t dh = umma_desc_sw128(st + (unsigned)(kTcWBytes + 32 * k));
+                        const uint64_t dl = umma_desc_sw128(st + (unsigned)(kTcWBytes + kTcXBytes + 32 * k));
                         tc_mma(acc, da, dh, (kt > kt0 || k > 0) ? 1u : 0u);
                         tc_mma(acc, da, dl, 1u);
                     }

@@ -394,15 +394,31 @@ std::vector<int32_t> Tokenizer::Encode(const std::string& text, bool parseSpecia
 {
     std::vector<int32_t> ids;
     const ByteMap& bm = Bytes();
+    constexpr size_t kCacheEntries = 1 << 16;
     auto plain = [&](size_t b, size_t e) {
         if (e <= b)
             return;
         std::string enc;
+        std::vector<int32_t> merged;
         for (const std::string& piece : PreTokenize(text.substr(b, e - b))) {
+            {
+                std::lock_guard<std::mutex> lock(m_cacheMutex);
+                const auto it = m_pieceCache.find(piece);
+                if (it != m_pieceCache.end()) {
+                    ids.insert(ids.end(), it->second.begin(), it->second.end());
+                    continue;
+                }
+            }
             enc.clear();
             for (unsigned char c : piece)
                 enc += bm.encoded[c];
-            MergePiece(enc, ids);
+            merged.clear();
+            MergePiece(enc, merged);
+            ids.insert(ids.end(), merged.begin(), merged.end());
+            std::lock_guard<std::mutex> lock(m_cacheMutex);
+            if (m_pieceCache.size() >= kCacheEntries)
+                m_pieceCache.clear();
+            m_pieceCache.emplace(piece, merged);
         }
     };
     size_t runStart = 0, i = 0;

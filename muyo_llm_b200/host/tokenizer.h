@@ -4,6 +4,7 @@
 #pragma once
 
 #include <cstdint>
+#include <mutex>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -48,6 +49,9 @@ private:
     // Special tokens by first byte, longest text first (then lowest id).
     std::vector<std::vector<std::pair<std::string, int32_t>>> m_specialByByte;
     bool m_qwen2Split = false;                // tokenizer.ggml.pre selects the Qwen2 split, else GPT-2's
+    // Ids of pieces already merged (a word recurs often in a text); bounded, emptied when full.
+    mutable std::mutex m_cacheMutex;
+    mutable std::unordered_map<std::string, std::vector<int32_t>> m_pieceCache;
 };
 
 /// Qwen2.5's ChatML framing (src/ChatTemplate.h:14-30).

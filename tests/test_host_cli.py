@@ -9,8 +9,10 @@ engine's ids over the tokenizer's prompt ids, cut after the end-of-sequence id, 
 """
 from __future__ import annotations
 
+import dataclasses
 import importlib
 import os
+import re
 import subprocess
 
 import numpy as np
@@ -49,8 +51,9 @@ def test_forward_option_errors_before_any_device_work(tmp_path):
 
 def _generated(stderr: str) -> list[int]:
     """The ids of "[forward] generated N tokens: a b c" (src/FullModel.cpp:1273-1278)."""
-    line = [ln for ln in stderr.splitlines() if ln.startswith("[forward] generated ")][-1]
-    return [int(v) for v in line.split(":", 1)[1].split()]
+    # The last such line; an interactive session's "[chat] you> " prompt precedes it on its line.
+    line = re.findall(r"\[forward\] generated \d+ tokens:([ 0-9]*)", stderr)[-1]
+    return [int(v) for v in line.split()]
 
 
 @pytest.mark.gpu
@@ -154,7 +157,10 @@ def _cut(ids, eos):
 
 
 def _engine(path):
-    return engine.Qwen2Model(synth.QWEN2_TINY, gguf_path=path, kv_dtype=_abi.KV_F32)
+    # The tiny file says 64 positions; a ChatML turn in its small vocabulary is longer, so the engine
+    # gets the CLI's room (results do not depend on the cache capacity).
+    cfg = dataclasses.replace(synth.QWEN2_TINY, max_seq=512)
+    return engine.Qwen2Model(cfg, gguf_path=path, kv_dtype=_abi.KV_F32)
 
 
 @pytest.mark.gpu
@@ -166,13 +172,16 @@ def test_forward_text_prompt_stops_at_eos(cuda, tmp_path):
     m = _engine(path)
     full = [int(v) for v in m.generate(prompt, 12)]
     m.close()
-    k = next(i for i in range(1, len(full)) if full[i] not in full[:i])
-    path2, tok2 = _tok_model(tmp_path, eos=full[k])
-    rc, out, err = _run_bytes("--forward", path2, "-p", "the lazy dog", "-n", "12")
-    assert rc == 0, err
-    assert "[forward] prompt tokens: " + " ".join(map(str, prompt)) in err
-    assert _generated(err) == full[:k + 1]
-    assert out == _stdout(tok2, [full[:k + 1]])
+    # An end id the run never reaches: all 12 ids. The last id that is new in the run: cut there.
+    absent = next(i for i in range(synth.QWEN2_TINY.vocab - 1, -1, -1) if i not in full)
+    k = max(i for i in range(len(full)) if full[i] not in full[:i])
+    for eos, want in ((absent, full), (full[k], full[:k + 1])):
+        path2, tok2 = _tok_model(tmp_path, eos=eos)
+        rc, out, err = _run_bytes("--forward", path2, "-p", "the lazy dog", "-n", "12")
+        assert rc == 0, err
+        assert "[forward] prompt tokens: " + " ".join(map(str, prompt)) in err
+        assert _generated(err) == want
+        assert out == _stdout(tok2, [want])
 
 
 @pytest.mark.gpu
