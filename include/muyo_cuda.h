@@ -312,7 +312,9 @@ int muyo_model_set_option(MuyoModel* m, const char* key, int value);
  * prompt's last position. The reference feeds a prompt one position at a time (src/FullModel.cpp:
  * 1174-1181): results agree to float rounding, not bit for bit (the projections sum in another
  * order). No logits are formed for the batched positions. Option "prefill_tc" = 1 runs the
- * projections on the tcgen05 GEMM (see muyo_cuda_mat_mul_f16). */
+ * projections on the tcgen05 GEMM (see muyo_cuda_mat_mul_f16). Option "prefill_positions" (a
+ * multiple of 128 up to 1024, default 128; set before "prefill") is the number of positions per
+ * pass: long prompts run fastest in passes of 512 on the tcgen05 GEMM. */
 
 /* ---- batched F16 GEMM (the prefill projections) ---------------------------------------------------
  * y[t][n] = sum_k A[n][k] * x[t][k] for n < rows, t < tokens: ggml's mul_mm with src0 = A (F16,

@@ -862,7 +862,8 @@ struct MuyoModel {
     bool prefill = false;           // generate: the prompt's positions but the last in one batched pass
     bool pf_tc = false;             // prefill projections on tcgen05 (default: the warp-level mma.sync kernel)
     std::vector<CUtensorMap> pf_maps;  // tcgen05 prefill: 5 weight maps per layer, then the activation halves
-    char* pf_buf = nullptr;         // batched-prefill activations for kPfCap positions
+    char* pf_buf = nullptr;         // batched-prefill activations for pf_cap positions
+    int pf_cap = 128;               // positions per prefill pass (option "prefill_positions")
     float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_att = nullptr, *pf_gu = nullptr;
     float* pf_part = nullptr;  // split-K partial sums
     size_t pf_part_floats = 0;
@@ -1578,7 +1579,7 @@ static int check_device_error(MuyoModel* m, cudaStream_t st)
 
 // ---- batched prefill ---------------------------------------------------------------------------------
 
-constexpr int kPfCap = 128;  // positions per prefill pass (longer prompts take several passes)
+constexpr int kPfCapMax = 1024;  // largest "prefill_positions" (longer prompts take several passes)
 constexpr int kPfMaxSplits = 16;
 
 // TMA descriptors of one tcgen05 prefill GEMM: the W rows (two matrices for gate | up) and the
@@ -1638,9 +1639,9 @@ static int pf_alloc(MuyoModel* m)
         return MUYO_OK;
     const Shape& s = m->s;
     const size_t wide = (size_t)std::max(std::max(s.hidden, s.q_dim), s.ffn);
-    const size_t part = (size_t)kPfMaxSplits * kPfCap * std::max(s.qkv_rows, s.hidden);
-    const size_t f32 = (size_t)kPfCap * ((size_t)s.hidden + s.qkv_rows + 2 * (size_t)s.q_dim + 2 * (size_t)s.ffn) + part;
-    const size_t bytes = f32 * sizeof(float) + 2 * (size_t)kPfCap * wide * sizeof(__half) + 256 * 9;
+    const size_t part = (size_t)kPfMaxSplits * (size_t)m->pf_cap * std::max(s.qkv_rows, s.hidden);
+    const size_t f32 = (size_t)m->pf_cap * ((size_t)s.hidden + s.qkv_rows + 2 * (size_t)s.q_dim + 2 * (size_t)s.ffn) + part;
+    const size_t bytes = f32 * sizeof(float) + 2 * (size_t)m->pf_cap * wide * sizeof(__half) + 256 * 9;
     if (cudaMalloc(&m->pf_buf, bytes) != cudaSuccess) {
         cudaGetLastError();
         m->pf_buf = nullptr;
@@ -1653,13 +1654,13 @@ static int pf_alloc(MuyoModel* m)
         p += (n + 255) / 256 * 256;
         return r;
     };
-    m->pf_x = reinterpret_cast<float*>(take((size_t)kPfCap * s.hidden * 4));
-    m->pf_qkv = reinterpret_cast<float*>(take((size_t)kPfCap * s.qkv_rows * 4));
-    m->pf_q = reinterpret_cast<float*>(take((size_t)kPfCap * s.q_dim * 4));
-    m->pf_att = reinterpret_cast<float*>(take((size_t)kPfCap * s.q_dim * 4));
-    m->pf_gu = reinterpret_cast<float*>(take((size_t)kPfCap * 2 * s.ffn * 4));
-    m->pf_hi = reinterpret_cast<__half*>(take((size_t)kPfCap * wide * 2));
-    m->pf_lo = reinterpret_cast<__half*>(take((size_t)kPfCap * wide * 2));
+    m->pf_x = reinterpret_cast<float*>(take((size_t)m->pf_cap * s.hidden * 4));
+    m->pf_qkv = reinterpret_cast<float*>(take((size_t)m->pf_cap * s.qkv_rows * 4));
+    m->pf_q = reinterpret_cast<float*>(take((size_t)m->pf_cap * s.q_dim * 4));
+    m->pf_att = reinterpret_cast<float*>(take((size_t)m->pf_cap * s.q_dim * 4));
+    m->pf_gu = reinterpret_cast<float*>(take((size_t)m->pf_cap * 2 * s.ffn * 4));
+    m->pf_hi = reinterpret_cast<__half*>(take((size_t)m->pf_cap * wide * 2));
+    m->pf_lo = reinterpret_cast<__half*>(take((size_t)m->pf_cap * wide * 2));
     m->pf_part = reinterpret_cast<float*>(take(part * 4));
     m->pf_part_floats = part;
     if ((size_t)(p - m->pf_buf) > bytes + 256 * 9) {
@@ -1758,8 +1759,8 @@ static int pf_make_maps(MuyoModel* m)
     CUtensorMap* xm = maps.data() + (size_t)5 * s.layers;
     const int ks[3] = {H, QD, F};
     for (int i = 0; i < 3; ++i)
-        if ((rc = make_map(&xm[2 * i], m->pf_hi, ks[i], kPfCap, ldh, kTcBN)) ||
-            (rc = make_map(&xm[2 * i + 1], m->pf_lo, ks[i], kPfCap, ldh, kTcBN)))
+        if ((rc = make_map(&xm[2 * i], m->pf_hi, ks[i], m->pf_cap, ldh, kTcBN)) ||
+            (rc = make_map(&xm[2 * i + 1], m->pf_lo, ks[i], m->pf_cap, ldh, kTcBN)))
             return rc;
     m->pf_maps.swap(maps);
     return MUYO_OK;
@@ -1786,8 +1787,8 @@ static int prefill_run(MuyoModel* m, int p0, int n, cudaStream_t st)
         pm = PfMaps{lm[a], lm[b], xm[0], xm[1]};
         return &pm;
     };
-    for (int c0 = 0; c0 < n; c0 += kPfCap) {
-        const int T = std::min(kPfCap, n - c0), pos0 = p0 + c0;
+    for (int c0 = 0; c0 < n; c0 += m->pf_cap) {
+        const int T = std::min(m->pf_cap, n - c0), pos0 = p0 + c0;
         MUYO_CUDA_TRY(launch_kernel(k_pf_embed, dim3(T), dim3(256), 0, st, true, W(m, "token_embd.weight"),
                                     (const int32_t*)(m->tokens + pos0), s.vocab, H, m->pf_x));
         for (int l = 0; l < s.layers; ++l) {
@@ -2037,6 +2038,16 @@ extern "C" int muyo_model_set_option(MuyoModel* m, const char* key, int value)
                 return rc;
         }
         m->prefill = value != 0;
+        return MUYO_OK;
+    }
+    if (k == "prefill_positions") {
+        MUYO_REQUIRE(value >= 128 && value <= kPfCapMax && value % 128 == 0,
+                     "set_option: prefill_positions must be a multiple of 128 in [128, %d]", kPfCapMax);
+        if (m->pf_buf) {
+            set_error("set_option: prefill_positions must be set before prefill is enabled");
+            return MUYO_ESTATE;
+        }
+        m->pf_cap = value;
         return MUYO_OK;
     }
     if (k == "prefill_tc") {

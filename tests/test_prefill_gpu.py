@@ -61,8 +61,10 @@ def test_mat_mul_f16_against_float64(cuda, N, K, T, kernel):
     assert np.all(np.abs(ya - (exact + y0)) <= bound + 1e-6 * np.abs(y0))
 
 
-def _model(cfg, t, kv, prefill, tc=False):
+def _model(cfg, t, kv, prefill, tc=False, positions=None):
     m = engine.Qwen2Model(cfg, t, kv_dtype=kv, engine=engine.Qwen2Model.ENGINE_GRAPH)
+    if positions:
+        _abi.call("muyo_model_set_option", m._m, b"prefill_positions", positions)
     if prefill:
         _abi.call("muyo_model_set_option", m._m, b"prefill", 1)
     if tc:
@@ -103,6 +105,36 @@ def test_prefill_multi_pass_05b_arch(cuda):
         m.close()
     assert out[0][0] == out[1][0]
     assert_rel_close(out[1][1], out[0][1], 1e-3, "logits after a 300-position prompt")
+
+
+@pytest.mark.parametrize("tc", [False, True])
+def test_prefill_512_position_passes_05b_arch(cuda, tc):
+    """Option "prefill_positions" = 512: a 700-position prompt in two passes (512 + 187), on either
+    GEMM kernel, against one decode step per position."""
+    cfg = synth.QWEN2_05B
+    t = synth.make_model(cfg, 33)
+    prompt = [int(i) for i in synth.prompt_ids(33, 700, cfg.vocab)]
+    out = []
+    for prefill in (False, True):
+        m = _model(cfg, t, _abi.KV_F16, prefill, tc and prefill, 512 if prefill else None)
+        ids = list(m.generate(prompt, 8))
+        _, logits = m.step(ids[-1])
+        out.append((ids, logits))
+        m.close()
+    assert out[0][0] == out[1][0]
+    assert_rel_close(out[1][1], out[0][1], 1e-3, "logits after a 700-position prompt")
+
+
+def test_prefill_positions_option_checks(cuda):
+    cfg = synth.QWEN2_TINY
+    m = engine.Qwen2Model(cfg, synth.make_model(cfg, 1), kv_dtype=_abi.KV_F32)
+    for bad in (0, 64, 200, 2048):
+        with pytest.raises(_abi.MuyoError):
+            _abi.call("muyo_model_set_option", m._m, b"prefill_positions", bad)
+    _abi.call("muyo_model_set_option", m._m, b"prefill", 1)
+    with pytest.raises(_abi.MuyoError):  # after the activations are allocated
+        _abi.call("muyo_model_set_option", m._m, b"prefill_positions", 256)
+    m.close()
 
 
 FULL = os.path.join(GOLDEN, "qwen2_05b_greedy.json")
