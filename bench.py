@@ -318,7 +318,8 @@ def run_suite(args):
             shapes = [tuple(int(v) for v in s.split("x")) for s in args.shapes.split(",") if s] or None
             res = sweep.gemv(shapes, args.iters, peak)
         elif args.suite == "prefill":
-            res = sweep.prefill(args.iters, peak, n_prompt=args.n_prompt, n_predict=args.n_predict)
+            res = sweep.prefill(args.iters, peak, n_prompt=args.n_prompt, n_predict=args.n_predict,
+                                gemm_only=args.shapes == "gemm")
         elif args.suite == "sampler":
             res = sweep.sampler(args.iters, peak, n_prompt=args.n_prompt, n_predict=args.n_predict)
         else:
@@ -340,7 +341,8 @@ def main():
     ap.add_argument("--suite", default="decode", choices=["decode", "gemv", "ops", "gemv_sharded", "sampler", "prefill"],
                     help="decode: the config-4 headline line (default); gemv / ops: kernel sweeps, one JSON line "
                          "per case (1 GPU)")
-    ap.add_argument("--shapes", default="", help="gemv suite: comma-separated ROWSxCOLS list (default: all)")
+    ap.add_argument("--shapes", default="", help="gemv suite: comma-separated ROWSxCOLS list (default: all); "
+                    "prefill suite: 'gemm' times the GEMM cases only")
     ap.add_argument("--iters", type=int, default=0, help="gemv / ops suite: calls timed per case (0: automatic)")
     ap.add_argument("--n-prompt", type=int, default=N_PROMPT,
                     help="decode suite: prompt ids per sequence (config 4: 32; smaller only for profiling)")

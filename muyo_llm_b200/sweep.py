@@ -207,7 +207,8 @@ def sampler(iters: int = 0, peak_gbs: float = 6462.1, seed: int = 7, n_prompt: i
     return out
 
 
-def prefill(iters: int = 0, peak_gbs: float = 6462.1, seed: int = 7, n_prompt: int = 32, n_predict: int = 256):
+def prefill(iters: int = 0, peak_gbs: float = 6462.1, seed: int = 7, n_prompt: int = 32, n_predict: int = 256,
+            gemm_only: bool = False):
     """Batched prefill. (1) muyo_cuda_mat_mul_f16 at the 0.5B layer's projection shapes for 128
     positions: device time per call (CUDA graph of back-to-back calls), weight GB/s and tensor
     TFLOP/s. (2) Prompt-only prefill (positions 0 .. P-2 of a P-id prompt, then the one decode step
@@ -257,6 +258,8 @@ def prefill(iters: int = 0, peak_gbs: float = 6462.1, seed: int = 7, n_prompt: i
                     f"{N}x{K}, {T} positions ({what})", alg, ms, peak_gbs, tensor=kern,
                     tflops=2 * N * K * T / (ms * 1e-3) / 1e12, mode="weights L2-resident between calls")
         out.append(r)
+    if gemm_only:  # a short program for profiling the GEMM kernels
+        return out
     cfg = synth.QWEN2_05B
     t = synth.make_model(cfg, seed)
     models = {}
