@@ -1722,6 +1722,16 @@ static int pf_attention_t(const Shape& s, float* q, float* out, const float* qkv
     MUYO_CUDA_TRY(launch_kernel(k_pf_rope_append<KV, HD>, dim3(T, s.heads + s.kv_heads), dim3(HD), 0, st, true, r,
                                 reinterpret_cast<KV*>(kc), reinterpret_cast<KV*>(vc)));
     PfAttn a{q, out, p0, s.heads, s.kv_heads, s.gqa, s.max_seq, 1.0f / sqrtf((float)s.head_dim)};
+    if constexpr (std::is_same<KV, __half>::value && (HD == 64 || HD == 128)) {
+        // F16 cache: the tensor-core kernel, one CTA per (64-position query tile, query head).
+        constexpr size_t fsmem = pf_flash_smem<HD>();
+        if (fsmem > 48 * 1024)
+            MUYO_CUDA_TRY(cudaFuncSetAttribute(k_pf_flash<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsmem));
+        MUYO_CUDA_TRY(launch_kernel(k_pf_flash<HD>, dim3((T + kPfFlashRows - 1) / kPfFlashRows, s.heads),
+                                    dim3(kPfFlashThreads), fsmem, st, true, a, T, reinterpret_cast<const __half*>(kc),
+                                    reinterpret_cast<const __half*>(vc)));
+        return MUYO_OK;
+    }
     const size_t smem = pf_attn_smem(HD, s.gqa);
     if (smem > 48 * 1024)
         MUYO_CUDA_TRY(cudaFuncSetAttribute(k_pf_attention<KV, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

@@ -9,7 +9,8 @@
 //                     layout, so each row's value is bit-identical), written as two F16 halves
 //   k_pf_gemm<BIAS>   QKV projection + bias
 //   k_pf_rope_append  RoPE (float64 angles, as the decode step) on q and k; k and v into the cache
-//   k_pf_attention    causal GQA over the cache, one CTA per (kv head, position)
+//   k_pf_attention    causal GQA over the cache, one CTA per (kv head, position) (F32 cache)
+//   k_pf_flash        the same on the tensor cores for an F16 cache (flash attention, mma.sync)
 //   k_pf_split        attention rows -> two F16 halves
 //   k_pf_gemm<ADD>    O projection added to the residual
 //   k_pf_norm_split, k_pf_gemm<STORE> (gate | up, two matrices in one launch), k_pf_swiglu_split,
@@ -721,6 +722,210 @@ __global__ void __launch_bounds__(kPfAttnThreads) k_pf_attention(PfAttn a, const
     for (int e = tid; e < G * HD; e += nt) {
         const int gq = e / HD;
         a.out[(size_t)t * a.heads * HD + (size_t)kh * G * HD + e] = __fdiv_rn(Os[e], Ls[gq]);
+    }
+}
+
+// ---- causal GQA attention for an F16 cache on the tensor cores (flash attention) -------------------
+//
+// CTA (64-position query tile, query head h): 4 warps, warp w owns query rows [16w, 16w + 16). Keys
+// and values stream through shared memory 64 positions at a time (a 2-stage cp.async ring, rows
+// padded to HD + 8 halves so the fragment reads are conflict-free); only the tiles at or below the
+// tile's last position are read (causal). Per key tile:
+//   S = Q.K^T   mma.sync m16n8k16 with Q as hi + lo F16 halves (q - f32(hi) in lo), so the scores
+//               keep F32-level accuracy against the cache's exact F16 keys;
+//   online softmax in registers (row max and sum across the quad of lanes that share a row);
+//   O += P.V    P (exp of the scaled scores) again as hi + lo halves, V read with ldmatrix.trans.
+// Out-of-order keys and query rows past T are masked to exp(-inf) = 0. Output: O / l in F32.
+constexpr int kPfFlashRows = 64, kPfFlashKeys = 64, kPfFlashThreads = 128;
+
+__device__ __forceinline__ void ldsm_x4_t(unsigned addr, unsigned& r0, unsigned& r1, unsigned& r2, unsigned& r3)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+// hi = f16(x), lo = f16(x - hi), packed as (element 0, element 1) half2 words.
+__device__ __forceinline__ void split2(float x0, float x1, unsigned& hi, unsigned& lo)
+{
+    const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
+    const __half l0 = __float2half_rn(x0 - __half2float(h0)), l1 = __float2half_rn(x1 - __half2float(h1));
+    hi = (unsigned)__half_as_ushort(h0) | ((unsigned)__half_as_ushort(h1) << 16);
+    lo = (unsigned)__half_as_ushort(l0) | ((unsigned)__half_as_ushort(l1) << 16);
+}
+
+template <int HD>
+constexpr size_t pf_flash_smem()
+{
+    return (size_t)2 * 2 * kPfFlashKeys * (HD + 8) * sizeof(__half);  // 2 stages x (K, V)
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kPfFlashThreads) k_pf_flash(PfAttn a, int T, const __half* __restrict__ kc,
+                                                              const __half* __restrict__ vc)
+{
+    constexpr int LDS = HD + 8;            // halves per shared-memory row (16-byte multiple)
+    constexpr int KS = HD / 16;            // k-steps of Q.K^T
+    constexpr int ND = HD / 8;             // 8-wide output column tiles
+    constexpr int NT = kPfFlashKeys / 8;   // 8-key score tiles
+    constexpr int CH = HD / 8;             // 16-byte chunks per row
+    extern __shared__ __align__(16) __half pf_flash_smem_buf[];
+    pdl_wait();
+    pdl_trigger();
+    const int tile = blockIdx.x, h = blockIdx.y, kh = h / a.gqa;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, qr = lane >> 2, qc = (lane & 3) * 2;
+    const int t0 = tile * kPfFlashRows;
+    const int t_last = min(t0 + kPfFlashRows, T) - 1;
+    const int n_keys = a.p0 + t_last + 1;  // keys 0 .. p0 + t_last
+    const size_t head_base = (size_t)kh * a.max_seq * HD;
+    const unsigned sbase = smem_u32(pf_flash_smem_buf);
+    constexpr unsigned kStage = 2u * kPfFlashKeys * LDS * 2u;  // bytes of one stage (K then V)
+
+    auto load_tile = [&](int j0, int stage) {
+        const unsigned kb = sbase + (unsigned)stage * kStage, vb = kb + (unsigned)(kPfFlashKeys * LDS * 2);
+        for (int c = tid; c < kPfFlashKeys * CH; c += kPfFlashThreads) {
+            const int r = c / CH, ch = c % CH, key = j0 + r;
+            const bool ok = key < n_keys;
+            const size_t off = head_base + (size_t)(ok ? key : 0) * HD + ch * 8;
+            const unsigned so = (unsigned)((r * LDS + ch * 8) * 2);
+            cp_async16(kb + so, kc + off, ok);
+            cp_async16(vb + so, vc + off, ok);
+        }
+        cp_async_commit();
+    };
+    load_tile(0, 0);
+
+    // Q fragments (rows r0 = t0 + 16w + qr and r0 + 8), pre-split into F16 halves.
+    unsigned qh[KS][4], ql[KS][4];
+    {
+        const int ra = t0 + warp * 16 + qr, rb = ra + 8;
+        const float* qa = a.q + (size_t)ra * a.heads * HD + (size_t)h * HD;
+        const float* qb = a.q + (size_t)rb * a.heads * HD + (size_t)h * HD;
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+            const int c = ks * 16 + qc;
+            const float2 x0 = ra < T ? *reinterpret_cast<const float2*>(qa + c) : make_float2(0.f, 0.f);
+            const float2 x1 = rb < T ? *reinterpret_cast<const float2*>(qb + c) : make_float2(0.f, 0.f);
+            const float2 x2 = ra < T ? *reinterpret_cast<const float2*>(qa + c + 8) : make_float2(0.f, 0.f);
+            const float2 x3 = rb < T ? *reinterpret_cast<const float2*>(qb + c + 8) : make_float2(0.f, 0.f);
+            split2(x0.x, x0.y, qh[ks][0], ql[ks][0]);
+            split2(x1.x, x1.y, qh[ks][1], ql[ks][1]);
+            split2(x2.x, x2.y, qh[ks][2], ql[ks][2]);
+            split2(x3.x, x3.y, qh[ks][3], ql[ks][3]);
+        }
+    }
+    const int pos_a = a.p0 + t0 + warp * 16 + qr, pos_b = pos_a + 8;  // query positions of this lane's rows
+    float o[ND][4];
+#pragma unroll
+    for (int nd = 0; nd < ND; ++nd)
+        o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.0f;
+    float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.0f, l_b = 0.0f;
+
+    const int n_tiles = (n_keys + kPfFlashKeys - 1) / kPfFlashKeys;
+    for (int jt = 0; jt < n_tiles; ++jt) {
+        const int j0 = jt * kPfFlashKeys, stage = jt & 1;
+        if (jt + 1 < n_tiles) {
+            load_tile(j0 + kPfFlashKeys, stage ^ 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        const unsigned kb = sbase + (unsigned)stage * kStage, vb = kb + (unsigned)(kPfFlashKeys * LDS * 2);
+        const __half* ks_ptr = pf_flash_smem_buf + (size_t)stage * (kStage / 2);
+
+        float sc[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
+            const __half* krow = ks_ptr + (nt * 8 + qr) * LDS + qc;
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+                const unsigned b0 = *reinterpret_cast<const unsigned*>(krow + ks * 16);
+                const unsigned b1 = *reinterpret_cast<const unsigned*>(krow + ks * 16 + 8);
+                mma_16816(sc[nt], qh[ks][0], qh[ks][1], qh[ks][2], qh[ks][3], b0, b1);
+                mma_16816(sc[nt], ql[ks][0], ql[ks][1], ql[ks][2], ql[ks][3], b0, b1);
+            }
+        }
+        // Scale, mask (key > query position), row maxima.
+        float mx_a = -INFINITY, mx_b = -INFINITY;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const int key = j0 + nt * 8 + qc;
+            sc[nt][0] = key <= pos_a ? sc[nt][0] * a.scale : -INFINITY;
+            sc[nt][1] = key + 1 <= pos_a ? sc[nt][1] * a.scale : -INFINITY;
+            sc[nt][2] = key <= pos_b ? sc[nt][2] * a.scale : -INFINITY;
+            sc[nt][3] = key + 1 <= pos_b ? sc[nt][3] * a.scale : -INFINITY;
+            mx_a = fmaxf(mx_a, fmaxf(sc[nt][0], sc[nt][1]));
+            mx_b = fmaxf(mx_b, fmaxf(sc[nt][2], sc[nt][3]));
+        }
+        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
+        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
+        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
+        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
+        const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+        // A row with every key so far masked keeps m = -inf; its exponentials are 0 (no NaN).
+        const float base_a = mn_a == -INFINITY ? 0.0f : mn_a, base_b = mn_b == -INFINITY ? 0.0f : mn_b;
+        const float al_a = expf(m_a - base_a), al_b = expf(m_b - base_b);
+        m_a = mn_a, m_b = mn_b;
+        float rs_a = 0.0f, rs_b = 0.0f;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            sc[nt][0] = expf(sc[nt][0] - base_a);
+            sc[nt][1] = expf(sc[nt][1] - base_a);
+            sc[nt][2] = expf(sc[nt][2] - base_b);
+            sc[nt][3] = expf(sc[nt][3] - base_b);
+            rs_a += sc[nt][0] + sc[nt][1];
+            rs_b += sc[nt][2] + sc[nt][3];
+        }
+        rs_a += __shfl_xor_sync(0xffffffffu, rs_a, 1);
+        rs_a += __shfl_xor_sync(0xffffffffu, rs_a, 2);
+        rs_b += __shfl_xor_sync(0xffffffffu, rs_b, 1);
+        rs_b += __shfl_xor_sync(0xffffffffu, rs_b, 2);
+        l_a = l_a * al_a + rs_a;
+        l_b = l_b * al_b + rs_b;
+#pragma unroll
+        for (int nd = 0; nd < ND; ++nd) {
+            o[nd][0] *= al_a, o[nd][1] *= al_a;
+            o[nd][2] *= al_b, o[nd][3] *= al_b;
+        }
+        // O += P.V: key step kk covers score tiles 2kk, 2kk + 1.
+#pragma unroll
+        for (int kk = 0; kk < kPfFlashKeys / 16; ++kk) {
+            unsigned ph[4], pl[4];
+            split2(sc[2 * kk][0], sc[2 * kk][1], ph[0], pl[0]);
+            split2(sc[2 * kk][2], sc[2 * kk][3], ph[1], pl[1]);
+            split2(sc[2 * kk + 1][0], sc[2 * kk + 1][1], ph[2], pl[2]);
+            split2(sc[2 * kk + 1][2], sc[2 * kk + 1][3], ph[3], pl[3]);
+            // ldmatrix.trans rows: thread t gives key kk*16 + (t / 8 % 2) * 8 + t % 8, columns
+            // (pair * 2 + t / 16) * 8: matrices 0-1 are b0/b1 of column tile 2*pair, 2-3 of 2*pair + 1.
+            const int vkey = kk * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
+#pragma unroll
+            for (int pair = 0; pair < ND / 2; ++pair) {
+                unsigned b0, b1, b2, b3;
+                ldsm_x4_t(vb + (unsigned)((vkey * LDS + (pair * 2 + (lane >> 4)) * 8) * 2), b0, b1, b2, b3);
+                mma_16816(o[2 * pair], ph[0], ph[1], ph[2], ph[3], b0, b1);
+                mma_16816(o[2 * pair], pl[0], pl[1], pl[2], pl[3], b0, b1);
+                mma_16816(o[2 * pair + 1], ph[0], ph[1], ph[2], ph[3], b2, b3);
+                mma_16816(o[2 * pair + 1], pl[0], pl[1], pl[2], pl[3], b2, b3);
+            }
+        }
+        __syncthreads();  // the stage is refilled by the next iteration's load
+    }
+    const int ra = t0 + warp * 16 + qr, rb = ra + 8;
+#pragma unroll
+    for (int nd = 0; nd < ND; ++nd) {
+        const int c = h * HD + nd * 8 + qc;
+        if (ra < T) {
+            float* dst = a.out + (size_t)ra * a.heads * HD + c;
+            dst[0] = __fdiv_rn(o[nd][0], l_a);
+            dst[1] = __fdiv_rn(o[nd][1], l_a);
+        }
+        if (rb < T) {
+            float* dst = a.out + (size_t)rb * a.heads * HD + c;
+            dst[0] = __fdiv_rn(o[nd][2], l_b);
+            dst[1] = __fdiv_rn(o[nd][3], l_b);
+        }
     }
 }
 
