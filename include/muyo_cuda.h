@@ -305,16 +305,17 @@ int muyo_model_destroy(MuyoModel* m);
  * L2; "smem_weights" = 1 (default) has the per-layer GEMV kernels copy their weight tile into shared
  * memory before waiting for the previous kernel (bounded wait; MUYO_ETIMEOUT if it expires). */
 int muyo_model_set_option(MuyoModel* m, const char* key, int value);
-/* Option "prefill" = 1 (default 0; allocates activations for 128 positions on first use): in
- * muyo_model_generate(_device), every prompt position but the last goes through the layers in one
- * batched pass per 128 positions (muyo_cuda_mat_mul_f16's GEMM for the projections, a causal
- * attention kernel over the cache), writing the same KV cache; the decode step then runs from the
+/* Option "prefill" = 1 (default 0; allocates activations for one pass on first use): in
+ * muyo_model_generate(_device), every prompt position but the last goes through the layers in
+ * batched passes (muyo_cuda_mat_mul_f16's GEMM for the projections, a causal attention kernel
+ * over the cache, on the tensor cores for an F16 cache), writing the same KV cache; the decode step then runs from the
  * prompt's last position. The reference feeds a prompt one position at a time (src/FullModel.cpp:
  * 1174-1181): results agree to float rounding, not bit for bit (the projections sum in another
- * order). No logits are formed for the batched positions. Option "prefill_tc" = 1 runs the
- * projections on the tcgen05 GEMM (see muyo_cuda_mat_mul_f16). Option "prefill_positions" (a
- * multiple of 128 up to 1024, default 128; set before "prefill") is the number of positions per
- * pass: long prompts run fastest in passes of 512 on the tcgen05 GEMM. */
+ * order). No logits are formed for the batched positions. Option "prefill_tc" picks the projections'
+ * GEMM (see muyo_cuda_mat_mul_f16): 0 the mma.sync kernel, 1 the tcgen05 kernel, 2 (default) per
+ * GEMM: tcgen05 from 256 positions or for matrices of 4M weights and more. Option
+ * "prefill_positions" (a multiple of 128 up to 1024, default 512; set before "prefill") is the
+ * number of positions per pass; longer prompts take several passes. */
 
 /* ---- batched F16 GEMM (the prefill projections) ---------------------------------------------------
  * y[t][n] = sum_k A[n][k] * x[t][k] for n < rows, t < tokens: ggml's mul_mm with src0 = A (F16,

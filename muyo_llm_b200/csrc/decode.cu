@@ -860,10 +860,10 @@ struct MuyoModel {
     MuyoSamplerParams sp{};         // its parameters (baked into the recorded graph)
     void* rng = nullptr;            // its mt19937_64 state, followed by the last sampled id (int32)
     bool prefill = false;           // generate: the prompt's positions but the last in one batched pass
-    bool pf_tc = false;             // prefill projections on tcgen05 (default: the warp-level mma.sync kernel)
+    int pf_tc = 2;                  // prefill projections: 0 mma.sync, 1 tcgen05, 2 per GEMM (option "prefill_tc")
     std::vector<CUtensorMap> pf_maps;  // tcgen05 prefill: 5 weight maps per layer, then the activation halves
     char* pf_buf = nullptr;         // batched-prefill activations for pf_cap positions
-    int pf_cap = 128;               // positions per prefill pass (option "prefill_positions")
+    int pf_cap = 512;               // positions per prefill pass (option "prefill_positions")
     float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_att = nullptr, *pf_gu = nullptr;
     float* pf_part = nullptr;  // split-K partial sums
     size_t pf_part_floats = 0;
@@ -1682,8 +1682,11 @@ static int pf_splits(int N, int K, int T, bool tc = false)
     const int bm = tc ? kTcBM : kPfBM, bn = tc ? kTcBN : kPfBN;
     const int ctas = ((N + bm - 1) / bm) * ((T + bn - 1) / bn);
     const int stages = (K + kPfBK - 1) / kPfBK;
-    int S = (2 * sm_count() + ctas - 1) / ctas;
-    S = std::min(S, std::max(1, stages / (tc ? 2 : 4)));  // the persistent kernel ramps once per CTA
+    // mma.sync: enough CTAs for two per SM. tcgen05 (persistent, one CTA per SM): the most splits
+    // that still fit one wave, so long passes do not pay a second partial wave and a larger
+    // reduction (fewer K stages per item than 2 would not amortise the pipeline ramp).
+    int S = tc ? std::max(1, sm_count() / ctas) : (2 * sm_count() + ctas - 1) / ctas;
+    S = std::min(S, std::max(1, stages / (tc ? 2 : 4)));
     return std::max(1, std::min(S, kPfMaxSplits));
 }
 
@@ -1787,10 +1790,13 @@ static int prefill_run(MuyoModel* m, int p0, int n, cudaStream_t st)
     if (m->pf_tc && m->pf_maps.empty() && (rc = pf_make_maps(m)))
         return rc;
     // tcgen05 GEMM of layer l: weight maps a and b of the layer (b for rows past the split) and the
-    // activation halves of K index xk (hidden, q_dim, ffn); null selects the mma.sync kernel.
+    // activation halves of K index xk (hidden, q_dim, ffn); null selects the mma.sync kernel. Per
+    // GEMM (pf_tc 2): tcgen05 from 256 positions, or for matrices of 4M weights and more, where it
+    // measured faster; below that the mma.sync kernel's shorter set-up wins.
     PfMaps pm;
-    auto tc = [&](int l, int a, int b, int xk) -> const PfMaps* {
-        if (!m->pf_tc || (a != b && F % kTcBM != 0))
+    auto tc = [&](int l, int a, int b, int xk, int N, int K, int T) -> const PfMaps* {
+        const bool use = m->pf_tc == 1 || (m->pf_tc == 2 && (T >= 256 || (size_t)N * K >= ((size_t)4 << 20)));
+        if (!use || (a != b && F % kTcBM != 0))
             return nullptr;
         const CUtensorMap* lm = m->pf_maps.data() + (size_t)5 * l;
         const CUtensorMap* xm = m->pf_maps.data() + (size_t)5 * s.layers + 2 * xk;
@@ -1808,7 +1814,7 @@ static int prefill_run(MuyoModel* m, int p0, int n, cudaStream_t st)
             MUYO_CUDA_TRY(launch_kernel(k_pf_norm_split, dim3(T), dim3(256), 0, st, true, (const float*)m->pf_x, H,
                                         w.attn_norm, s.eps, H, m->pf_hi, m->pf_lo, ldh));
             if ((rc = pf_gemm<PF_BIAS>(w.wqkv, nullptr, s.qkv_rows, s.qkv_rows, H, T, m->pf_hi, m->pf_lo, ldh,
-                                       m->pf_qkv, s.qkv_rows, w.bqkv, m->pf_part, m->pf_part_floats, st, tc(l, 0, 0, 0),
+                                       m->pf_qkv, s.qkv_rows, w.bqkv, m->pf_part, m->pf_part_floats, st, tc(l, 0, 0, 0, s.qkv_rows, H, T),
                                        m->err)))
                 return rc;
             if ((rc = pf_attention(s, m->pf_q, m->pf_att, m->pf_qkv, kc, vc, pos0, T, st)))
@@ -1816,17 +1822,17 @@ static int prefill_run(MuyoModel* m, int p0, int n, cudaStream_t st)
             MUYO_CUDA_TRY(launch_kernel(k_pf_split, dim3(T), dim3(256), 0, st, true, (const float*)m->pf_att, QD, QD,
                                         m->pf_hi, m->pf_lo, ldh));
             if ((rc = pf_gemm<PF_ADD>(w.wo, nullptr, H, H, QD, T, m->pf_hi, m->pf_lo, ldh, m->pf_x, H, nullptr, m->pf_part,
-                                      m->pf_part_floats, st, tc(l, 1, 1, 1), m->err)))
+                                      m->pf_part_floats, st, tc(l, 1, 1, 1, H, QD, T), m->err)))
                 return rc;
             MUYO_CUDA_TRY(launch_kernel(k_pf_norm_split, dim3(T), dim3(256), 0, st, true, (const float*)m->pf_x, H,
                                         w.ffn_norm, s.eps, H, m->pf_hi, m->pf_lo, ldh));
             if ((rc = pf_gemm<PF_STORE>(w.wgate, w.wup, F, 2 * F, H, T, m->pf_hi, m->pf_lo, ldh, m->pf_gu, 2 * F,
-                                        nullptr, m->pf_part, m->pf_part_floats, st, tc(l, 2, 3, 0), m->err)))
+                                        nullptr, m->pf_part, m->pf_part_floats, st, tc(l, 2, 3, 0, 2 * F, H, T), m->err)))
                 return rc;
             MUYO_CUDA_TRY(launch_kernel(k_pf_swiglu_split, dim3(T), dim3(256), 0, st, true, (const float*)m->pf_gu, F,
                                         m->pf_hi, m->pf_lo, ldh));
             if ((rc = pf_gemm<PF_ADD>(w.wdown, nullptr, H, H, F, T, m->pf_hi, m->pf_lo, ldh, m->pf_x, H, nullptr, m->pf_part,
-                                      m->pf_part_floats, st, tc(l, 4, 4, 2), m->err)))
+                                      m->pf_part_floats, st, tc(l, 4, 4, 2, H, F, T), m->err)))
                 return rc;
         }
     }
@@ -2061,8 +2067,8 @@ extern "C" int muyo_model_set_option(MuyoModel* m, const char* key, int value)
         return MUYO_OK;
     }
     if (k == "prefill_tc") {
-        MUYO_REQUIRE(value == 0 || value == 1, "set_option: prefill_tc must be 0 or 1");
-        m->pf_tc = value != 0;
+        MUYO_REQUIRE(value >= 0 && value <= 2, "set_option: prefill_tc must be 0, 1 or 2");
+        m->pf_tc = value;
         return MUYO_OK;
     }
     if (k == "pdl") {

@@ -67,8 +67,8 @@ def _model(cfg, t, kv, prefill, tc=False, positions=None):
         _abi.call("muyo_model_set_option", m._m, b"prefill_positions", positions)
     if prefill:
         _abi.call("muyo_model_set_option", m._m, b"prefill", 1)
-    if tc:
-        _abi.call("muyo_model_set_option", m._m, b"prefill_tc", 1)
+    # 0: the mma.sync kernel for every projection, 1: tcgen05 for every one, 2 (default): per GEMM
+    _abi.call("muyo_model_set_option", m._m, b"prefill_tc", 1 if tc is True else 2 if tc == "auto" else 0)
     return m
 
 
@@ -98,7 +98,7 @@ def test_prefill_multi_pass_05b_arch(cuda):
     prompt = [int(i) for i in synth.prompt_ids(31, 300, cfg.vocab)]
     out = []
     for prefill in (False, True):
-        m = _model(cfg, t, _abi.KV_F16, prefill)
+        m = _model(cfg, t, _abi.KV_F16, prefill, positions=128 if prefill else None)
         ids = list(m.generate(prompt, 12))
         _, logits = m.step(ids[-1])
         out.append((ids, logits))
@@ -107,7 +107,7 @@ def test_prefill_multi_pass_05b_arch(cuda):
     assert_rel_close(out[1][1], out[0][1], 1e-3, "logits after a 300-position prompt")
 
 
-@pytest.mark.parametrize("tc", [False, True])
+@pytest.mark.parametrize("tc", [False, True, "auto"])
 def test_prefill_512_position_passes_05b_arch(cuda, tc):
     """Option "prefill_positions" = 512: a 700-position prompt in two passes (512 + 187), on either
     GEMM kernel, against one decode step per position."""
@@ -141,9 +141,10 @@ FULL = os.path.join(GOLDEN, "qwen2_05b_greedy.json")
 
 
 @pytest.mark.skipif(not os.path.exists(FULL), reason="0.5B golden fixture not generated")
-@pytest.mark.parametrize("tc", [False, True])
+@pytest.mark.parametrize("tc", [False, True, "auto"])
 def test_prefill_05b_greedy_bit_identical_to_reference(cuda, tc):
-    """With either GEMM kernel (mma.sync, tcgen05) behind the prefill projections."""
+    """With either GEMM kernel (mma.sync, tcgen05) behind the prefill projections, or the default
+    choice per GEMM."""
     g = json.load(open(FULL))
     cfg = synth.QWEN2_05B
     t = synth.make_model(cfg, int(g["seed"]))
