@@ -735,7 +735,8 @@ __global__ void __launch_bounds__(kPfAttnThreads) k_pf_attention(PfAttn a, const
 //               keep F32-level accuracy against the cache's exact F16 keys;
 //   online softmax in registers (row max and sum across the quad of lanes that share a row);
 //   O += P.V    P (exp of the scaled scores) again as hi + lo halves, V read with ldmatrix.trans.
-// Out-of-order keys and query rows past T are masked to exp(-inf) = 0. Output: O / l in F32.
+// Keys after a query's position get exp(-inf) = 0; rows past T are computed but not stored.
+// Output: O / l in F32.
 constexpr int kPfFlashRows = 64, kPfFlashKeys = 64, kPfFlashThreads = 128;
 
 __device__ __forceinline__ void ldsm_x4_t(unsigned addr, unsigned& r0, unsigned& r1, unsigned& r2, unsigned& r3)
