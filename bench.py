@@ -250,7 +250,7 @@ def run_b200(args, rank, world, local_rank):
         kernel = "decode step (CUDA graph of 5*layers+1 kernels); algorithmic bytes per token / time per token"
         launches = (5 * cfg.layers + 1 + 1) * steps_per_seq * args.steps  # + the control kernel per sequence
     else:
-        kernel = ("k_decode_persistent: one launch per sequence runs all 288 decode steps; algorithmic bytes "
+        kernel = ("k_decode_stream: one launch per sequence runs all 288 decode steps; algorithmic bytes "
                   "of the 288 steps / sequence time")
         launches = 2 * args.steps  # control kernel + persistent kernel per sequence
     traffic = step_traffic(cfg, pos_avg) if args.engine == "graph" else None

@@ -295,9 +295,13 @@ int muyo_model_buffer(MuyoModel* m, const char* name, void** ptr, size_t* bytes)
 int muyo_model_destroy(MuyoModel* m);
 /* Engine options: "engine" = 1 (the default) replays the per-phase kernels of muyo_cuda_layer_step
  * as a CUDA graph per decode step; 0 runs every decode step of a generate call in one persistent
- * cooperative kernel (a producer warp streams weight tiles into shared memory ahead of the
- * activation dependencies, consumer warps meet at bounded grid barriers). Both compute the same
- * arithmetic; they differ only in F32 reduction order (last-bit differences).
+ * cooperative kernel (a producer warp streams the weight rows of every phase into a shared-memory
+ * ring ahead of the activation dependencies; consumer warps hand activations between phases as
+ * {tag, value} words that the next phase polls; no grid barrier). Engine 0 takes greedy decoding
+ * with head sizes 16..128 and shapes whose staging fits shared memory (MUYO_EUNSUPPORTED
+ * otherwise, and while a sampler is set). Both compute the same arithmetic in F32; they differ
+ * only in reduction order (last-bit differences, which an F16 cache can turn into one F16 ulp of a
+ * key or value).
  * Graph-engine options (set before muyo_model_finalize; results are bit-identical either way):
  * "pdl" = 1 (default) launches each kernel with programmatic stream serialization, so it starts
  * while the previous kernel drains and waits on the device for that kernel's results; "prefetch" =
@@ -417,16 +421,22 @@ int muyo_model_set_sampler(MuyoModel* m, const MuyoSamplerParams* p, void* strea
  * No counterpart in the reference, which runs on one GPU: the multi-GPU form of its LM head +
  * greedy pick (src/FullModel.cpp:973-998, src/Sampler.cpp:32-43). `world` processes, one per GPU
  * of one node, each own a group. Set-up (allocates; not for the hot path):
- *   muyo_p2p_create   allocates this rank's buffer (a header and the full [rows_total] F32 output)
- *                     and writes its CUDA IPC handle (muyo_p2p_handle_bytes() bytes) to handle_out;
+ *   muyo_p2p_create   allocates this rank's buffer (a header and two slots of the full [rows_total]
+ *                     F32 output) and writes its CUDA IPC handle (muyo_p2p_handle_bytes() bytes) to
+ *                     handle_out;
  *   muyo_p2p_connect  opens every other rank's handle (handles: world of them, in rank order).
  * muyo_cuda_mat_vec_f16_allgather is a collective: every rank calls it, in the same order, with its
  * contiguous shard (rows [row_begin, row_begin + p->rows) of the full matrix). One kernel per GPU
  * computes the shard, stores it into every rank's output over NVLink, exchanges the shards'
  * (max, first index) pairs and flags through peer memory, and writes the greedy index to *token
- * (device int32) on every rank; the full output is then at muyo_p2p_output on every rank. The wait
- * for the peers is bounded (2 s): if a rank does not take part, the others finish with token 0 and
- * muyo_p2p_check (synchronising) reports MUYO_ETIMEOUT. No multicast, no TMA: plain peer stores. */
+ * (device int32) on every rank; the full output is then at muyo_p2p_output on every rank. Calls
+ * alternate between the two output slots, so muyo_p2p_output (the slot of the latest call) changes
+ * from call to call, and a peer that runs one call ahead writes the other slot: the output of a call
+ * stays intact until this rank issues the call after next; read it on the same stream before that.
+ * The wait for the peers is bounded (2 s): if a rank does not take part, the others finish with
+ * token 0 and muyo_p2p_check (synchronising) reports MUYO_ETIMEOUT. The ranks' call counters then
+ * disagree, so the group is dead: later calls return MUYO_ESTATE, and every rank must destroy its
+ * group and create a new one. No multicast, no TMA: plain peer stores. */
 typedef struct MuyoP2PGroup MuyoP2PGroup;
 size_t muyo_p2p_handle_bytes(void);
 int muyo_p2p_create(int world, int rank, uint32_t rows_total, MuyoP2PGroup** out, void* handle_out);

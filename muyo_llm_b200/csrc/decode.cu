@@ -47,7 +47,8 @@ struct Control {
 static_assert(offsetof(Control, prompt_end) == 4 && offsetof(Control, total) == 8, "sampler gate layout");
 }  // namespace muyo
 
-#include "decode_persistent.cuh"
+#include "sync.cuh"
+#include "decode_stream.cuh"
 #include "prefill.cuh"  // after the mbarrier helpers it uses
 
 namespace muyo {
@@ -852,7 +853,7 @@ struct MuyoModel {
     size_t pinned_ints = 0;
     int32_t host_pos = 0;
     bool finalized = false;
-    int engine = 1;                 // 0: persistent kernel, 1: CUDA graph of per-phase kernels (default)
+    int engine = 1;                 // 0: streaming persistent kernel, 1: CUDA graph of per-phase kernels (default)
     bool pdl = true;                // graph engine: kernels launch early and prefetch their weights
     bool prefetch_ahead = true;     // graph engine: each GEMV streams a later kernel's weights into L2
     bool sw = true;                 // graph engine: per-layer GEMVs bulk-copy their weight tile to shared memory
@@ -869,10 +870,16 @@ struct MuyoModel {
     size_t pf_part_floats = 0;
     __half *pf_hi = nullptr, *pf_lo = nullptr;
     double* rope_cs = nullptr;      // [max_seq][head_dim] cos/sin table (float64)
-    muyo::PLayer* d_layers = nullptr;
-    unsigned* bar = nullptr;        // persistent kernel grid-barrier counter
-    int* err = nullptr;             // persistent kernel error word
-    int p_slots = 0, p_slot_bytes = 0, p_region_b = 0, p_smem = 0, p_grid = 0;
+    int* err = nullptr;             // error word of the bounded device waits
+    // streaming persistent engine (decode_stream.cuh)
+    muyo::SLayer* d_slayers = nullptr;
+    unsigned long long* ll = nullptr;  // tagged hand-off words: per-layer blocks, then the greedy pairs
+    int* abort_g = nullptr;         // the launch's abort word
+    muyo::SArgs sa{};               // everything but the per-launch fields
+    int s_smem = 0, s_grid = 0;
+    bool s_ok = false;              // the shapes fit the streaming kernel
+    std::string s_why;              // why not, when they do not
+    unsigned s_tag = 1;             // tag of the next step (never 0)
 };
 
 namespace muyo {
@@ -971,62 +978,50 @@ static int record_step(MuyoModel* m, cudaStream_t st)
                          m->tokens, s.max_seq, false, st);
 }
 
-// ---- persistent engine ----------------------------------------------------------------------------
+// ---- streaming persistent engine -------------------------------------------------------------------
 
 constexpr int kSmemLimit = 227 * 1024;
 
-static size_t round16(size_t n) { return (n + 15) / 16 * 16; }
+static size_t round16w(size_t n) { return (n + 15) / 16 * 16; }  // words, keeping 128-byte alignment
+static int round128i(size_t n) { return (int)((n + 127) / 128 * 128); }
 
-// Shared-memory plan of the persistent kernel: a ring of weight slots, region B (the staged input
-// vector, or one attention work item), the cos/sin row, reduction scratch and the mbarriers.
-static int persistent_plan(MuyoModel* m)
+// Shared-memory and hand-off-buffer plan of the streaming kernel (decode_stream.cuh). Sets m->s_ok, or
+// m->s_why when the shapes do not fit it (the graph engine then runs them).
+static int stream_plan(MuyoModel* m)
 {
     const Shape& s = m->s;
-    // staged input: raw x and norm weights side by side (2 * hidden), the down input (ffn), or the merged
-    // attention output plus its merge scratch (q_dim + 2 * heads * chunks)
-    const size_t x_bytes = sizeof(float) * std::max(std::max((size_t)2 * s.hidden, (size_t)s.ffn),
-                                                    (size_t)s.q_dim + 2 * (size_t)s.heads * s.max_chunks);
-    const size_t attn_bytes = sizeof(float) * (size_t)attn_smem_floats(s.head_dim, s.gqa);
-    const size_t region_b = round16(std::max(x_bytes, attn_bytes));
-    const size_t min_slot = std::max(std::max((size_t)4 * s.hidden, (size_t)2 * s.q_dim), (size_t)2 * s.ffn);
-    // ~56 KB slots: large bulk copies stream at HBM speed (measured 7.0 TB/s with three 56 KB slots
-    // against 6.4 TB/s with six 28 KB slots), and a phase's rows are split evenly over its tiles.
-    const size_t slot = round16(std::max(min_slot, (size_t)57344));
-    const size_t misc = sizeof(double) * s.head_dim + 32 * sizeof(float) + 32 * sizeof(Pair) +
-                        2 * kMaxSlots * sizeof(uint64_t) + 128;
-    if (region_b + misc + 2 * slot > (size_t)kSmemLimit) {
-        set_error("persistent engine: shapes need %zu bytes of shared memory for two slots", region_b + misc + 2 * slot);
-        return MUYO_EUNSUPPORTED;
+    m->s_ok = false;
+    m->s_why.clear();
+    const int hd = s.head_dim;
+    if (s.heads > 64) {
+        m->s_why = "more than 64 query heads";
+        return MUYO_OK;
     }
-    const int slots = (int)std::min<size_t>(kMaxSlots, ((size_t)kSmemLimit - region_b - misc) / slot);
-    m->p_slots = slots;
-    m->p_slot_bytes = (int)slot;
-    m->p_region_b = (int)region_b;
-    m->p_smem = (int)((size_t)slots * slot + region_b + misc);
-    return MUYO_OK;
-}
-
-template <typename KV, int HD>
-static int launch_persistent_t(MuyoModel* m, int n_steps, cudaStream_t st)
-{
-    const Shape& s = m->s;
-    auto k = k_decode_persistent<KV, HD>;
-    if (m->p_grid == 0) {
-        MUYO_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, m->p_smem));
-        int per_sm = 0;
-        MUYO_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kPThreads, m->p_smem));
-        if (per_sm < 1) {
-            set_error("persistent engine: the kernel does not fit on an SM (%d bytes of shared memory)", m->p_smem);
-            return MUYO_EUNSUPPORTED;
-        }
-        m->p_grid = sm_count();
+    const int xs_floats = (std::max(std::max(s.hidden, s.q_dim), s.ffn) + 3) / 4 * 4;
+    // The merge's staged partials or the attention scratch follow the first q_dim floats of xs.
+    const size_t merge_floats = (size_t)s.heads * kSJmax * (hd + 3);
+    const size_t attn_floats = 5 * (size_t)hd + 2 * kSKeys + 4 + 512;
+    const size_t work_floats = std::max((size_t)xs_floats, (size_t)(s.q_dim + 3) / 4 * 4 + std::max(merge_floats, attn_floats));
+    const int off_work = 0;  // relative to the end of the ring
+    const int off_hraw = off_work + round128i(work_floats * sizeof(float));
+    const int off_h1raw = off_hraw + round128i((size_t)s.hidden * sizeof(float));
+    const int off_misc = off_h1raw + round128i((size_t)s.hidden * sizeof(float));
+    const int fixed = off_misc + round128i(s_misc_bytes());
+    // The largest piece of any phase (whole rows, at least one).
+    struct Ph { int K, nmat, M; bool head; } phs[5] = {{s.hidden, 1, s.qkv_rows, false}, {s.q_dim, 1, s.hidden, false},
+                                                      {s.hidden, 2, s.ffn, false}, {s.ffn, 1, s.hidden, false},
+                                                      {s.hidden, 1, s.vocab, true}};
+    size_t max_piece = 0;
+    for (const Ph& p : phs)
+        max_piece = std::max(max_piece, (size_t)round128i((size_t)s_rows_per_piece(p.K, p.nmat, p.head) * p.K * 2 * p.nmat));
+    const int ring = (kSmemLimit - fixed) / 128 * 128;
+    if (ring < (int)(2 * max_piece) || ring < 2 * 16384) {
+        m->s_why = "the shapes leave too little shared memory for the weight ring";
+        return MUYO_OK;
     }
-    PArgs a{};
-    a.layers = m->d_layers;
+    SArgs& a = m->sa;
+    a = SArgs{};
     a.L = s.layers;
-    a.embd = W(m, "token_embd.weight");
-    a.lm = W(m, m->tied_output ? "token_embd.weight" : "output.weight");
-    a.final_norm = F(m, "output_norm.weight");
     a.H = s.hidden;
     a.F = s.ffn;
     a.V = s.vocab;
@@ -1036,53 +1031,129 @@ static int launch_persistent_t(MuyoModel* m, int n_steps, cudaStream_t st)
     a.heads = s.heads;
     a.kv_heads = s.kv_heads;
     a.gqa = s.gqa;
-    a.hd = s.head_dim;
     a.max_seq = s.max_seq;
     a.eps = s.eps;
-    a.attn = AttnDev{s.heads, s.kv_heads, s.gqa, s.max_seq, 0, 1.0f / sqrtf((float)s.head_dim), (double)s.rope_base,
-                     s.max_chunks, m->rope_cs};
-    a.kc = m->kc;
-    a.vc = m->vc;
-    a.kv_layer_elems = (long long)(m->kv_layer_bytes / (s.kv_f16 ? 2 : 4));
-    a.h = m->h;
-    a.h1 = m->ls.h1;
-    a.qkv = m->ls.qkv;
-    a.act = m->ls.act;
-    a.logits = m->logits;
-    a.attn_part = m->ls.part;
-    a.lm_part = m->lm_part;
-    a.ctrl = m->ctrl;
-    a.tokens = m->tokens;
-    a.bar = m->bar;
-    a.err = m->err;
-    a.n_steps = n_steps;
-    a.slots = m->p_slots;
-    a.slot_bytes = m->p_slot_bytes;
-    a.region_b_bytes = m->p_region_b;
-    MUYO_CUDA_TRY(cudaMemsetAsync(m->bar, 0, sizeof(unsigned), st));
-    void* args[] = {&a};
-    MUYO_CUDA_TRY(cudaLaunchCooperativeKernel((const void*)k, dim3(m->p_grid), dim3(kPThreads), args, (size_t)m->p_smem,
-                                              st));
+    a.scale = 1.0f / sqrtf((float)hd);
+    a.ring_bytes = ring;
+    a.off_work = ring + off_work;
+    a.off_hraw = ring + off_hraw;
+    a.off_h1raw = ring + off_h1raw;
+    a.off_misc = ring + off_misc;
+    a.xs_floats = xs_floats;
+    m->s_smem = ring + fixed;
+    // Tagged words: per layer qkv, attention partials, h1, SwiGLU output, layer output; then the
+    // double-buffered greedy pairs of every CTA.
+    size_t w = 0;
+    a.o_qkv = (int)w;
+    w += round16w(s.qkv_rows);
+    a.o_part = (int)w;
+    w += round16w((size_t)s.heads * kSJmax * (hd + 2));
+    a.o_h1 = (int)w;
+    w += round16w(s.hidden);
+    a.o_act = (int)w;
+    w += round16w(s.ffn);
+    a.o_hout = (int)w;
+    w += round16w(s.hidden);
+    a.ll_layer = (long long)w;
+    m->s_ok = true;
     return MUYO_OK;
 }
 
-static int launch_persistent(MuyoModel* m, int n_steps, cudaStream_t st)
+// Device buffers and the cooperative-launch check of the streaming kernel (once per model).
+template <typename KV, int HD>
+static int stream_setup_t(MuyoModel* m)
 {
+    auto k = k_decode_stream<KV, HD>;
+    MUYO_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, m->s_smem));
+    int per_sm = 0;
+    MUYO_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kSThreads, m->s_smem));
+    if (per_sm < 1) {
+        m->s_ok = false;
+        m->s_why = "the streaming kernel does not fit on an SM";
+        return MUYO_OK;
+    }
+    m->s_grid = sm_count();
+    return MUYO_OK;
+}
+
+#define MUYO_STREAM_DISPATCH(FN, ...)                                                        \
+    do {                                                                                     \
+        const Shape& s_ = m->s;                                                              \
+        if (s_.kv_f16) {                                                                     \
+            switch (s_.head_dim) {                                                           \
+                case 16: return FN<__half, 16>(__VA_ARGS__);                                 \
+                case 32: return FN<__half, 32>(__VA_ARGS__);                                 \
+                case 64: return FN<__half, 64>(__VA_ARGS__);                                 \
+                default: return FN<__half, 128>(__VA_ARGS__);                                \
+            }                                                                                \
+        }                                                                                    \
+        switch (s_.head_dim) {                                                               \
+            case 16: return FN<float, 16>(__VA_ARGS__);                                      \
+            case 32: return FN<float, 32>(__VA_ARGS__);                                      \
+            case 64: return FN<float, 64>(__VA_ARGS__);                                      \
+            default: return FN<float, 128>(__VA_ARGS__);                                     \
+        }                                                                                    \
+    } while (0)
+
+static int stream_setup(MuyoModel* m)
+{
+    if (!m->s_ok)
+        return MUYO_OK;
     const Shape& s = m->s;
-    if (s.kv_f16) {
-        switch (s.head_dim) {
-            case 16: return launch_persistent_t<__half, 16>(m, n_steps, st);
-            case 32: return launch_persistent_t<__half, 32>(m, n_steps, st);
-            case 64: return launch_persistent_t<__half, 64>(m, n_steps, st);
-            default: return launch_persistent_t<__half, 128>(m, n_steps, st);
-        }
+    std::vector<SLayer> sl(s.layers);
+    for (int l = 0; l < s.layers; ++l) {
+        const LayerPtrs w = layer_ptrs(m, l);
+        sl[l] = SLayer{w.wqkv, w.bqkv, w.attn_norm, w.wo, w.ffn_norm, w.wgate, w.wup, w.wdown};
     }
-    switch (s.head_dim) {
-        case 16: return launch_persistent_t<float, 16>(m, n_steps, st);
-        case 32: return launch_persistent_t<float, 32>(m, n_steps, st);
-        case 64: return launch_persistent_t<float, 64>(m, n_steps, st);
-        default: return launch_persistent_t<float, 128>(m, n_steps, st);
+    if (!m->d_slayers)
+        MUYO_CUDA_TRY(cudaMalloc(&m->d_slayers, sizeof(SLayer) * s.layers));
+    MUYO_CUDA_TRY(cudaMemcpy(m->d_slayers, sl.data(), sizeof(SLayer) * s.layers, cudaMemcpyHostToDevice));
+    if (!m->ll) {
+        const size_t words = (size_t)m->sa.ll_layer * s.layers + round16w(4 * (size_t)sm_count());
+        MUYO_CUDA_TRY(cudaMalloc(&m->ll, words * sizeof(unsigned long long)));
+        MUYO_CUDA_TRY(cudaMemset(m->ll, 0, words * sizeof(unsigned long long)));
     }
+    MUYO_STREAM_DISPATCH(stream_setup_t, m);
+}
+
+template <typename KV, int HD>
+static int launch_stream_t(MuyoModel* m, int prompt_end, int total, int n_steps, cudaStream_t st)
+{
+    SArgs a = m->sa;
+    a.layers = m->d_slayers;
+    a.embd = W(m, "token_embd.weight");
+    a.lm = W(m, m->tied_output ? "token_embd.weight" : "output.weight");
+    a.final_norm = F(m, "output_norm.weight");
+    a.rope_cs = m->rope_cs;
+    a.kc = m->kc;
+    a.vc = m->vc;
+    a.kv_layer_elems = (long long)(m->kv_layer_bytes / (m->s.kv_f16 ? 2 : 4));
+    a.ll = m->ll;
+    a.ll_best = m->ll + (size_t)a.ll_layer * m->s.layers;
+    a.logits = m->logits;
+    a.ctrl = m->ctrl;
+    a.tokens = m->tokens;
+    a.err = m->err;
+    a.abort_g = m->abort_g;
+    a.tag0 = m->s_tag;
+    a.pos0 = m->host_pos;
+    a.prompt_end = prompt_end;
+    a.total = total;
+    a.n_steps = n_steps;
+    // Tags never repeat within 2^32 steps, and never take the value 0 the buffers start with.
+    m->s_tag += (unsigned)n_steps;
+    if (m->s_tag < (unsigned)n_steps)
+        m->s_tag = 1;
+    MUYO_CUDA_TRY(cudaMemsetAsync(m->abort_g, 0, sizeof(int), st));
+    void* args[] = {&a};
+    MUYO_CUDA_TRY(cudaLaunchCooperativeKernel((const void*)k_decode_stream<KV, HD>, dim3(m->s_grid), dim3(kSThreads),
+                                              args, (size_t)m->s_smem, st));
+    return MUYO_OK;
+}
+
+static int launch_stream(MuyoModel* m, int prompt_end, int total, int n_steps, cudaStream_t st)
+{
+    MUYO_STREAM_DISPATCH(launch_stream_t, m, prompt_end, total, n_steps, st);
 }
 
 __global__ void k_set_control(Control* c, Control v) { *c = v; }
@@ -1277,7 +1348,8 @@ static void free_model(MuyoModel* m)
     if (m->cap_stream)
         cudaStreamDestroy(m->cap_stream);
     cudaFree(m->rope_cs);
-    cudaFree(m->d_layers);
+    cudaFree(m->d_slayers);
+    cudaFree(m->ll);
     cudaFree(m->arena);
     cudaFree(m->kc);
     cudaFree(m->vc);
@@ -1374,8 +1446,8 @@ extern "C" int muyo_model_create(const MuyoQwen2Config* c, int device, MuyoModel
     p += align256(sizeof(Control));
     m->tokens = reinterpret_cast<int32_t*>(p);
     p += align256(sizeof(int32_t) * s.max_seq);
-    m->bar = reinterpret_cast<unsigned*>(p);
-    p += align256(sizeof(unsigned));
+    m->abort_g = reinterpret_cast<int*>(p);
+    p += align256(sizeof(int));
     m->err = reinterpret_cast<int*>(p);
     *out = m;
     return MUYO_OK;
@@ -1504,19 +1576,12 @@ extern "C" int muyo_model_finalize(MuyoModel* m, void* stream)
         MUYO_CUDA_TRY(cudaMemcpy(m->rope_cs, cs.data(), cs.size() * sizeof(double), cudaMemcpyHostToDevice));
         m->s.rope_cs = m->rope_cs;
     }
-    std::vector<PLayer> pl(s.layers);
-    for (int l = 0; l < s.layers; ++l) {
-        const LayerPtrs w = layer_ptrs(m, l);
-        pl[l] = PLayer{w.wqkv, w.bqkv, w.attn_norm, w.wo, w.ffn_norm, w.wgate, w.wup, w.wdown};
-    }
-    if (!m->d_layers)
-        MUYO_CUDA_TRY(cudaMalloc(&m->d_layers, sizeof(PLayer) * s.layers));
-    MUYO_CUDA_TRY(cudaMemcpy(m->d_layers, pl.data(), sizeof(PLayer) * s.layers, cudaMemcpyHostToDevice));
     {
-        const int rc = persistent_plan(m);
+        int rc = stream_plan(m);
+        if (rc == MUYO_OK)
+            rc = stream_setup(m);
         if (rc)
             return rc;
-        m->p_grid = 0;
     }
     const int rc = record_graph(m);
     if (rc)
@@ -1547,10 +1612,16 @@ static int run_steps(MuyoModel* m, int prompt_end, int total, int n_steps, cudaS
         set_error("decode: the device sampler runs in the graph engine (engine 1), not the persistent kernel");
         return MUYO_EUNSUPPORTED;
     }
+    if (m->engine == 0 && !m->s_ok) {
+        set_error("decode: the persistent kernel does not take these shapes (%s); use the graph engine (engine 1)",
+                  m->s_why.c_str());
+        return MUYO_EUNSUPPORTED;
+    }
+    const bool persistent = m->engine == 0;
     k_set_control<<<1, 1, 0, st>>>(m->ctrl, Control{m->host_pos, prompt_end, total, 0});
     MUYO_LAUNCH_CHECK();
-    if (m->engine == 0) {
-        const int rc = launch_persistent(m, n_steps, st);
+    if (persistent) {
+        const int rc = launch_stream(m, prompt_end, total, n_steps, st);
         if (rc)
             return rc;
     } else {

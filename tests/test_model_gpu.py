@@ -162,9 +162,10 @@ def test_engines_agree_on_05b_arch(cuda, kv_dtype):
         outs.append((list(gen), logits))
         m.close()
     assert outs[0][0] == outs[1][0]
-    # The engines reduce the RMSNorm sum of squares over different thread counts (last-bit
-    # differences); with an F16 cache such a difference can flip an F16 rounding of a key or value.
-    tol = 1e-4 if kv_dtype == _abi.KV_F32 else 1e-3
+    # The engines add their F32 partial sums in different orders (last-bit differences); with an F16
+    # cache such a difference can flip the F16 rounding of a key or value. Each engine is held to 1e-3
+    # of the oracle (test_05b_f16_cache), so two of them are within 2e-3 of each other.
+    tol = 1e-4 if kv_dtype == _abi.KV_F32 else 2e-3
     assert_rel_close(outs[0][1], outs[1][1], tol, "step-0 logits, persistent vs graph")
 
 
