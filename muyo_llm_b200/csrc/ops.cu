@@ -878,8 +878,11 @@ __global__ void __launch_bounds__(kThreads) k_pairs_to_pair(const ArgPair* __res
 
 // ---- row-sharded GEMV fused with its all-gather over NVLink peer memory ---------------------------
 // One GPU's share of y = W x over `world` GPUs of one node (one process each). Every rank owns a
-// P2PBuffer (header + the full [rows_total] output), and every rank's buffer is mapped into every
-// other rank through CUDA IPC. A call is one kernel per GPU:
+// P2PBuffer (header + two [rows_total] output slots), and every rank's buffer is mapped into every
+// other rank through CUDA IPC. Call `epoch` uses output slot and pair slot epoch & 1: a peer can be
+// at most one call ahead (it cannot finish call e + 1 before this rank publishes e + 1, which this
+// rank does only after its own call e and whatever the caller queued after it), so a peer's next call
+// writes the other slot while this rank still reads call e's. A call is one kernel per GPU:
 //   1. each CTA computes its rows and stores every value into every rank's output (NVLink stores);
 //   2. each CTA leaves its best (value, global index) in the local header, fences at system scope
 //      and counts itself in;
@@ -892,10 +895,10 @@ constexpr int kP2PMaxRanks = 8;
 constexpr unsigned long long kP2PWaitNs = 2000000000ull;
 
 struct P2PHeader {
-    unsigned flags[kP2PMaxRanks];  // flags[r]: the last epoch rank r has published into this buffer
-    ArgPair pairs[kP2PMaxRanks];   // pairs[r]: rank r's (max value, first global index)
-    int counter;                   // arrivals of this rank's CTAs (reset by the last one)
-    int err;                       // 5: a wait for a peer's flag expired
+    unsigned flags[kP2PMaxRanks];     // flags[r]: the last epoch rank r has published into this buffer
+    ArgPair pairs[2][kP2PMaxRanks];   // pairs[e & 1][r]: rank r's (max value, first global index) of call e
+    int counter;                      // arrivals of this rank's CTAs (reset by the last one)
+    int err;                          // 5: a wait for a peer's flag expired
     int pad[14];
 };
 
@@ -905,7 +908,7 @@ struct P2PArgs {
     int K, k8, local_rows, row_begin, rows_total, world, rank;
     long long lda;
     unsigned epoch;
-    float* y[kP2PMaxRanks];          // every rank's output (this rank's slice is written into each)
+    float* y[kP2PMaxRanks];          // every rank's output slot of this call (this rank's slice goes to each)
     P2PHeader* hdr[kP2PMaxRanks];    // every rank's header
     ArgPair* cta_pairs;              // local scratch: one pair per CTA
     int32_t* token;
@@ -981,12 +984,14 @@ __global__ void __launch_bounds__(kThreads) k_gemv_allgather(P2PArgs p)
         return;
     P2PHeader* own = p.hdr[p.rank];
     own->counter = 0;
+    const int slot = p.epoch & 1;
     for (int r = 0; r < p.world; ++r)
-        p.hdr[r]->pairs[p.rank] = mine;
+        p.hdr[r]->pairs[slot][p.rank] = mine;
     __threadfence_system();
     for (int r = 0; r < p.world; ++r)
         st_release_sys(&p.hdr[r]->flags[p.rank], p.epoch);
-    // every rank's slice and pair are in this buffer once its flag carries this epoch
+    // every rank's slice and pair are in this buffer once its flag carries this epoch (or the next one:
+    // a peer one call ahead has written the other slots)
     const unsigned long long t0 = now_ns_ops();
     bool ok = true;
     for (int r = 0; r < p.world && ok; ++r) {
@@ -1002,7 +1007,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv_allgather(P2PArgs p)
     int bi2 = INT_MAX;
     if (ok)
         for (int r = 0; r < p.world; ++r) {
-            const ArgPair q{__ldcg(&own->pairs[r].v), __ldcg(&own->pairs[r].i)};
+            const ArgPair q{__ldcg(&own->pairs[slot][r].v), __ldcg(&own->pairs[slot][r].i)};
             if (pair_better(q.v, q.i, bv2, bi2))
                 bv2 = q.v, bi2 = q.i;
         }
@@ -1404,9 +1409,16 @@ struct MuyoP2PGroup {
     ArgPair* cta_pairs = nullptr;        // per-CTA scratch (local)
     int max_ctas = 0;
     uint32_t epoch = 0;
+    bool dead = false;                   // a call timed out: the ranks' epochs no longer agree
 };
 
-static size_t p2p_bytes(uint32_t rows_total) { return sizeof(P2PHeader) + (size_t)rows_total * sizeof(float); }
+// Header, then two output slots (call epoch e uses slot e & 1), each 256-byte aligned.
+static size_t p2p_slot_bytes(uint32_t rows_total) { return ((size_t)rows_total * sizeof(float) + 255) / 256 * 256; }
+static size_t p2p_bytes(uint32_t rows_total) { return sizeof(P2PHeader) + 2 * p2p_slot_bytes(rows_total); }
+static float* p2p_slot(char* base, uint32_t rows_total, uint32_t epoch)
+{
+    return reinterpret_cast<float*>(base + sizeof(P2PHeader) + (epoch & 1) * p2p_slot_bytes(rows_total));
+}
 
 extern "C" size_t muyo_p2p_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
 
@@ -1467,7 +1479,7 @@ extern "C" int muyo_p2p_output(MuyoP2PGroup* g, float** y)
 {
     clear_error();
     MUYO_REQUIRE(g && y, "p2p_output: null argument");
-    *y = reinterpret_cast<float*>(g->buf + sizeof(P2PHeader));
+    *y = p2p_slot(g->buf, g->rows_total, g->epoch);
     return MUYO_OK;
 }
 
@@ -1479,7 +1491,9 @@ extern "C" int muyo_p2p_check(MuyoP2PGroup* g)
     MUYO_CUDA_TRY(cudaMemcpy(&e, g->buf + offsetof(P2PHeader, err), sizeof(int), cudaMemcpyDeviceToHost));
     if (e) {
         MUYO_CUDA_TRY(cudaMemset(g->buf + offsetof(P2PHeader, err), 0, sizeof(int)));
-        set_error("p2p: a wait for a peer's flag expired (a rank did not take part in the call)");
+        g->dead = true;
+        set_error("p2p: a wait for a peer's flag expired (a rank did not take part in the call); the group must be "
+                  "destroyed and created again on every rank");
         return MUYO_ETIMEOUT;
     }
     return MUYO_OK;
@@ -1490,6 +1504,11 @@ extern "C" int muyo_cuda_mat_vec_f16_allgather(MuyoP2PGroup* g, const MuyoMatVec
 {
     clear_error();
     MUYO_REQUIRE(g && token, "mat_vec_allgather: null group or token");
+    if (g->dead) {
+        set_error("mat_vec_allgather: an earlier call of this group timed out; destroy it and create a new one on "
+                  "every rank");
+        return MUYO_ESTATE;
+    }
     for (int r = 0; r < g->world; ++r)
         MUYO_REQUIRE(r == g->rank || g->peer[r], "mat_vec_allgather: rank %d is not connected", r);
     MUYO_REQUIRE(p && (p->batches <= 1) && p->fusion_flags == 0, "mat_vec_allgather: one batch, no fusion flags");
@@ -1509,7 +1528,7 @@ extern "C" int muyo_cuda_mat_vec_f16_allgather(MuyoP2PGroup* g, const MuyoMatVec
     for (int r = 0; r < g->world; ++r) {
         char* base = r == g->rank ? g->buf : static_cast<char*>(g->peer[r]);
         args.hdr[r] = reinterpret_cast<P2PHeader*>(base);
-        args.y[r] = reinterpret_cast<float*>(base + sizeof(P2PHeader));
+        args.y[r] = p2p_slot(base, g->rows_total, args.epoch);
     }
     args.cta_pairs = g->cta_pairs;
     args.token = token;

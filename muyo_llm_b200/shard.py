@@ -143,9 +143,6 @@ class P2PShardedGemv:
         blob = bytes(every.cpu().numpy().tobytes())
         _abi.call("muyo_p2p_connect", g, C.create_string_buffer(blob, len(blob)))
         dist.barrier(group=group)  # every rank has opened every handle before the first call
-        yp = C.c_void_p()
-        _abi.call("muyo_p2p_output", g, C.byref(yp))
-        self.y_ptr = yp.value
         self.token = torch.empty(1, dtype=torch.int32, device=w_shard.device)
 
     def __call__(self, x, stream=None):
@@ -155,11 +152,18 @@ class P2PShardedGemv:
                        self.begin, self.token.data_ptr(), s)
         return self.token
 
+    def output_ptr(self) -> int:
+        """Device address of the latest call's full [rows] F32 output (calls alternate between two
+        slots; a slot stays intact until this rank issues the call after next)."""
+        yp = self.C.c_void_p()
+        self._abi.call("muyo_p2p_output", self.g, self.C.byref(yp))
+        return yp.value
+
     def output(self):
-        """The full [rows] F32 output on this rank (a view of the group's buffer)."""
+        """A copy of the latest call's full [rows] F32 output on this rank (stream-ordered)."""
         torch = self.torch
         out = torch.empty(self.rows, dtype=torch.float32, device=self.w.device)
-        self._abi.call("muyo_cuda_copy_f32", _copy_params(self.rows), self.y_ptr, out.data_ptr(),
+        self._abi.call("muyo_cuda_copy_f32", _copy_params(self.rows), self.output_ptr(), out.data_ptr(),
                        torch.cuda.current_stream().cuda_stream)
         return out
 

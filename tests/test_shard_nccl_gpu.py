@@ -120,6 +120,40 @@ def _p2p_worker(rank, world, port, results):
             nodes.mat_vec_f16(nodes.mat_vec_params(COLS, ROWS), torch.from_numpy(w).cuda(), xd, full)
             torch.cuda.synchronize()
             out.append((int(token.item()), plant[0][0], bool(torch.equal(y, full))))
+        # Back-to-back calls with no host synchronisation, a different planted maximum each call (x
+        # selects which planted row wins): each call's token and output slot, copied out on the stream
+        # right after the call, must be that call's, whichever rank runs ahead.
+        plants = [(1000, 1), (100000, 2), (ROWS // 2 - 1, 3), (ROWS // 2, 4), (ROWS - 1, 5), (5, 6)]
+        rng = np.random.default_rng(7)
+        w = (rng.uniform(-1, 1, (ROWS, COLS)) * 0.05).astype(np.float16)
+        for row, col in plants:
+            w[row] = np.float16(0.0)
+            w[row, col] = np.float16(40.0)
+        xs = []
+        for _, col in plants:
+            x = rng.standard_normal(COLS).astype(np.float32)
+            for _, c in plants:
+                x[c] = 0.0
+            x[col] = 1.0
+            xs.append(torch.from_numpy(x).cuda())
+        op.w = torch.from_numpy(w[begin:end]).cuda()
+        tokens = torch.empty(len(plants), dtype=torch.int32, device="cuda")
+        outs = [torch.empty(ROWS, dtype=torch.float32, device="cuda") for _ in plants]
+        dist.barrier()
+        for k in range(len(plants)):
+            tok = op(xs[k])
+            tokens[k:k + 1].copy_(tok)
+            outs[k].copy_(op.output())
+        torch.cuda.synchronize()
+        op.check()
+        wfull = torch.from_numpy(w).cuda()
+        back_to_back = []
+        for k, (row, _) in enumerate(plants):
+            full = torch.empty(ROWS, dtype=torch.float32, device="cuda")
+            nodes.mat_vec_f16(nodes.mat_vec_params(COLS, ROWS), wfull, xs[k], full)
+            torch.cuda.synchronize()
+            back_to_back.append((int(tokens[k].item()), row, bool(torch.equal(outs[k], full))))
+        out.extend(back_to_back)
         # rank 1 sits one call out: rank 0's wait for its flag must expire and be reported
         dist.barrier()
         timed_out = None
@@ -131,6 +165,12 @@ def _p2p_worker(rank, world, port, results):
                 timed_out = False
             except _abi.MuyoError as e:
                 timed_out = e.rc == -3
+            # the group is dead after a timeout: a further call is refused, not run
+            try:
+                op(xd)
+                timed_out = False
+            except _abi.MuyoError as e:
+                timed_out = timed_out and e.rc == -6
         dist.barrier()
         results.put((rank, out, timed_out))
         op.close()  # the ranks' epochs now differ, so the group is not used again
@@ -141,8 +181,10 @@ def _p2p_worker(rank, world, port, results):
 def test_fused_gemv_allgather_two_gpus(cuda):
     """muyo_cuda_mat_vec_f16_allgather: the shards go to every GPU over NVLink stores and the
     pairs and flags through peer memory. The full output is bit-identical to one GPU's GEMV on
-    every rank, and the token is the planted first-index maximum. A rank that skips a call makes
-    the others' bounded wait expire with MUYO_ETIMEOUT (no hang)."""
+    every rank, and the token is the planted first-index maximum, also for back-to-back calls with a
+    different maximum each (the output and pair slots alternate by call). A rank that skips a call
+    makes the others' bounded wait expire with MUYO_ETIMEOUT (no hang), after which the group
+    refuses further calls (MUYO_ESTATE)."""
     import torch
     import torch.multiprocessing as mp
 
