@@ -268,12 +268,19 @@ REF_SAMPLER = os.path.join(HERE, "_ref", "libsampler_ref.so")
 REF_TOKENIZER = os.path.join(HERE, "_ref", "libtokenizer_ref.so")
 
 
+def reference_tree() -> str | None:
+    """The muyo-llm source tree named by the environment variable MUYO_REFERENCE, if it is there."""
+    ref = os.environ.get("MUYO_REFERENCE")
+    return ref if ref and os.path.exists(os.path.join(ref, "src", "Sampler.cpp")) else None
+
+
 def build_ref() -> str | None:
-    """Compile the reference's own sampler and tokenizer into oracle/_ref (needs the reference tree);
-    returns the sampler's path, None if neither the tree nor a built copy is there."""
-    if not os.path.exists(os.path.join("/root/reference", "src", "Sampler.cpp")):
+    """Compile the reference's own sampler and tokenizer into oracle/_ref (needs the reference tree,
+    MUYO_REFERENCE); returns the sampler's path, None if neither the tree nor a built copy is there."""
+    ref = reference_tree()
+    if ref is None:
         return REF_SAMPLER if os.path.exists(REF_SAMPLER) else None
-    subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
+    subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={ref}"], check=True)
     return REF_SAMPLER
 
 

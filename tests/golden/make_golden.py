@@ -171,11 +171,15 @@ def make_full_f16() -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference/tools/reference_qwen2.py")
+    ref_tree = os.environ.get("MUYO_REFERENCE")
+    ap.add_argument("--ref", default=os.path.join(ref_tree, "tools", "reference_qwen2.py") if ref_tree else None,
+                    help="the reference's tools/reference_qwen2.py (default: under $MUYO_REFERENCE)")
     ap.add_argument("--tiny", action="store_true")
     ap.add_argument("--full", action="store_true")
     ap.add_argument("--full-f16", action="store_true")
     a = ap.parse_args()
+    if (a.tiny or a.full or not a.full_f16) and not a.ref:
+        ap.error("give --ref or set MUYO_REFERENCE to the muyo-llm source tree")
     if not (a.tiny or a.full or a.full_f16):
         a.tiny = a.full = a.full_f16 = True
     if a.tiny:
