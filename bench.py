@@ -13,6 +13,7 @@ shard), summed. Timed on the device with CUDA events around K sequences, max ove
   python bench.py --suite ops                              # op latency + multi-row bandwidth sweep
   python bench.py --suite sampler                          # device sampler per call + sampled decode steps
   python bench.py --suite prefill                          # batched-prefill GEMM, prompt-to-first-token, config 4
+  python bench.py --suite layer                            # one fused decoder layer: config 3 and a 7B-class layer
   torchrun --nproc-per-node N bench.py --suite gemv_sharded  # row-sharded GEMV + NCCL gathers (C5)
 
 `--impl reference` times the reference's CPU forward on the host cores instead: the C oracle port
@@ -69,19 +70,30 @@ def bytes_per_token(cfg, pos_avg: float, kv_bytes: int = 2) -> float:
     return L * (per_layer + kv) + V * H * 2 + H * 4 + H * 2
 
 
-def step_traffic(cfg, pos_avg: float):
-    """DRAM bytes of one graph-engine decode step from the committed ncu capture
-    (profiles/decode_step_dram_traffic_c4short.md, positions 0..7, warm caches), plus the algorithmic
-    difference in KV-cache reads between those positions and pos_avg. None if the summary is absent."""
-    path = os.path.join(ROOT, "profiles", "decode_step_dram_traffic_c4short.md")
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one graph-engine decode step, summed over
+# its 122 launches in one ncu capture at positions 0..7 with warm caches; the command and the per-kernel
+# split are in profiles/decode_step_dram_traffic_c4short.md.
+GRAPH_STEP_DRAM_BYTES = 1014109440
+GRAPH_STEP_DRAM_POS_AVG = 3.5
+
+
+def step_traffic(cfg, pos_avg: float) -> float:
+    """The measured DRAM bytes of one graph-engine decode step (GRAPH_STEP_DRAM_BYTES) plus the
+    algorithmic difference in KV-cache reads between the captured positions and pos_avg."""
+    return GRAPH_STEP_DRAM_BYTES + bytes_per_token(cfg, pos_avg) - bytes_per_token(cfg, GRAPH_STEP_DRAM_POS_AVG)
+
+
+def host_threads() -> int:
+    """Physical cores this process may run on (SMT siblings share a core's vector units, and the
+    oracle's row loops gain nothing from them)."""
+    allowed = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
     try:
-        for line in open(path):
-            if line.startswith("dram bytes per decode step:"):
-                measured = float(line.split(":")[1])
-                return measured + bytes_per_token(cfg, pos_avg) - bytes_per_token(cfg, 3.5)
-    except OSError:
-        pass
-    return None
+        import psutil
+
+        physical = psutil.cpu_count(logical=False) or allowed
+    except Exception:
+        physical = allowed
+    return max(1, min(allowed, physical))
 
 
 class ClockSampler:
@@ -129,23 +141,27 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.rows)}
 
 
-def cpu_baseline(cfg, tensors, prompt, n_tokens: int):
-    """The oracle port on the host cores: wall time of the first n_tokens decode steps."""
+def cpu_baseline(cfg, tensors, prompt, n_tokens: int, seq_len: int = N_PROMPT + N_PREDICT):
+    """The oracle port on the host's physical cores: wall time of n_tokens decode steps at positions
+    spread evenly over a config-4 sequence (0 .. seq_len - 1). A step's cost is the same whatever
+    the cache holds (the weights dominate; attention reads rows 0..pos), so the sample costs what
+    the whole sequence costs per token."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
 
-    threads = os.cpu_count() or 1
+    threads = host_threads()
     oracle.set_threads(threads)
     om = oracle.Qwen2(cfg, tensors, kv_f16=True)
     om.step(int(prompt[0]), 0)  # warm the F16 table and page in the weights
     om.reset()
+    positions = [round(i * (seq_len - 1) / max(n_tokens - 1, 1)) for i in range(n_tokens)]
     t0 = time.perf_counter()
-    for pos in range(n_tokens):
-        om.step(int(prompt[pos % len(prompt)]), pos)
+    for i, pos in enumerate(positions):
+        om.step(int(prompt[i % len(prompt)]), pos)
     dt = time.perf_counter() - t0
     return {"value": n_tokens / dt, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"first {n_tokens} decode steps of a config-4 sequence (oracle/oracle.c, F16 KV cache, "
-                      f"{threads} threads, row-parallel)"}
+            "sample": f"{n_tokens} decode steps at positions {positions[0]}..{positions[-1]} spread over a config-4 "
+                      f"sequence (oracle/oracle.c, F16 KV cache, {threads} threads on physical cores, row-parallel)"}
 
 
 def run_reference(args, rank, world):
@@ -168,7 +184,8 @@ def run_reference(args, rank, world):
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 0, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f16 weights / f32 compute", "data": "synthetic (seeded random-init)",
-            "config": {"workload": f"config 4 sample: {n_tok} decode steps per step", "model": "Qwen2.5-0.5B arch",
+            "config": {"workload": f"config 4 sample: {n_tok} decode steps per step, positions spread over 0..287",
+                       "model": "Qwen2.5-0.5B arch",
                        "global_batch": 1, "seq_len": n_tok, "parallelism": "host threads"},
             "cpu_baseline": cb, "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -260,6 +277,18 @@ def run_b200(args, rank, world, local_rank):
     cb = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = cpu_baseline(cfg, tensors, prompt, 8)
+    model.close()
+    # With N > 1: BASELINE config 5 after the decode measurement, on the same ranks - the LM head
+    # (151936 x 896, cross-GPU greedy pick) and the 7B-class GEMVs row-sharded over the N GPUs, through
+    # the NCCL gathers and through the fused NVLink kernel; each rank checks its gathered output and
+    # token against one GPU computing the whole matrix.
+    sharded = None
+    if world > 1 and not args.no_sharded:
+        from muyo_llm_b200 import sweep
+
+        torch.cuda.synchronize()
+        dist.barrier()
+        sharded = sweep.gemv_sharded(rank, world, dist, 0, measured_peaks()[0], check=True)
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
@@ -275,8 +304,9 @@ def run_b200(args, rank, world, local_rank):
                            "ms_per_token": ms / steps_per_seq},
                 "e2e": e2e, "roofline": roofline, "cpu_baseline": cb, "clocks": clocks.summary(),
                 "gpu_launches": launches, "engine": args.engine}
+        if sharded is not None:
+            line["sharded_gemv"] = sharded
         print(json.dumps(line), flush=True)
-    model.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -320,6 +350,8 @@ def run_suite(args):
         elif args.suite == "prefill":
             res = sweep.prefill(args.iters, peak, n_prompt=args.n_prompt, n_predict=args.n_predict,
                                 gemm_only=args.shapes == "gemm")
+        elif args.suite == "layer":
+            res = sweep.layer(args.iters, peak)
         elif args.suite == "sampler":
             res = sweep.sampler(args.iters, peak, n_prompt=args.n_prompt, n_predict=args.n_predict)
         else:
@@ -337,8 +369,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sharded", action="store_true", help="N > 1: skip the config-5 row-sharded GEMV lines")
     ap.add_argument("--engine", default="graph", choices=["persistent", "graph"])
-    ap.add_argument("--suite", default="decode", choices=["decode", "gemv", "ops", "gemv_sharded", "sampler", "prefill"],
+    ap.add_argument("--suite", default="decode",
+                    choices=["decode", "gemv", "ops", "gemv_sharded", "sampler", "prefill", "layer"],
                     help="decode: the config-4 headline line (default); gemv / ops: kernel sweeps, one JSON line "
                          "per case (1 GPU)")
     ap.add_argument("--shapes", default="", help="gemv suite: comma-separated ROWSxCOLS list (default: all); "

@@ -2,6 +2,7 @@
 // tolerances are the reference checks' own; the expected values come from plain CPU loops here.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -439,12 +440,127 @@ int RunKvCache()
     });
 }
 
-// One Qwen2 decoder layer (src/TransformerLayer.cpp's check: hidden 64, 8 cached positions,
-// feed-forward 128, tol 1e-3) through muyo_cuda_layer_step: one head of 64, F32 cache, positions
-// 0..7 decoded in turn, every output compared with a CPU restatement of the same layer.
-int RunTransformerLayer()
+// src/TransformerLayer.cpp's check itself: its inputs (:257-286: hidden 64, 8 cached keys, feed-forward
+// 128, F32 weights in small integer patterns, position 0) through its 14 nodes as the op-level entry
+// points (rms_norm, mat_vec_f32, rope_neox, mat_vec_f32, soft_max, mat_vec_f32, mat_vec_f32, add,
+// rms_norm, mat_vec_f32 x2, swiglu, mat_vec_f32, add), against the same CPU sequence (:537-590) at the
+// check's tolerance 1e-3 * (1 + |e|) (:602).
+static bool ReferenceLayerChain()
 {
-    return Guard("layer", [] {
+    const uint32_t H = 64, S = 8, F = 128;
+    const float eps = 1e-6F, scale = 1.0F / 8.0F;
+    std::vector<float> hidden(H), n1(H), n2(H), wq((size_t)H * H), wo((size_t)H * H), wg((size_t)F * H),
+        wu((size_t)F * H), wd((size_t)H * F), keys((size_t)S * H), vt((size_t)H * S);
+    for (uint32_t i = 0; i < H; ++i) {
+        hidden[i] = (float)((int)(i % 7) - 3);
+        n1[i] = 0.5F + 0.01F * (float)(i % 5);
+        n2[i] = 0.6F + 0.01F * (float)(i % 3);
+    }
+    for (uint32_t i = 0; i < H * H; ++i) {
+        wq[i] = (float)((int)(i % 3) - 1);
+        wo[i] = (float)((int)(i % 5) - 2) * 0.5F;
+    }
+    for (uint32_t i = 0; i < F * H; ++i) {
+        wg[i] = (float)((int)(i % 3) - 1);
+        wu[i] = (float)((int)(i % 4) - 1);
+    }
+    for (uint32_t i = 0; i < H * F; ++i)
+        wd[i] = (float)((int)(i % 5) - 2) * 0.25F;
+    for (uint32_t k = 0; k < S; ++k)
+        for (uint32_t d = 0; d < H; ++d) {
+            keys[(size_t)k * H + d] = (float)((int)((k + d) % 3) - 1);
+            vt[(size_t)d * S + k] = (float)((int)((k * 2 + d) % 7) - 3);
+        }
+    // CPU sequence (float sums as the check's Gemv; double sum of squares as its RmsNorm)
+    auto gemv = [](const std::vector<float>& w, const std::vector<float>& x, uint32_t rows) {
+        std::vector<float> y(rows);
+        for (uint32_t r = 0; r < rows; ++r) {
+            float s = 0.0F;
+            for (size_t k = 0; k < x.size(); ++k)
+                s += w[r * x.size() + k] * x[k];
+            y[r] = s;
+        }
+        return y;
+    };
+    auto norm = [&](const std::vector<float>& x, const std::vector<float>& w) {
+        double ss = 0.0;
+        for (float v : x)
+            ss += (double)v * v;
+        const float sc = (float)(1.0 / std::sqrt(ss / x.size() + eps));
+        std::vector<float> y(x.size());
+        for (size_t i = 0; i < x.size(); ++i)
+            y[i] = x[i] * sc * w[i];
+        return y;
+    };
+    const std::vector<float> xn = norm(hidden, n1), q = gemv(wq, xn, H);
+    std::vector<float> qr(q);  // position 0: the rotation is the identity (cos 0 = 1, sin 0 = 0)
+    const std::vector<float> sc = gemv(keys, qr, S);
+    float mx = -1e30F;
+    for (float v : sc)
+        mx = std::max(mx, v * scale);
+    std::vector<float> pr(S);
+    double sum = 0.0;
+    for (uint32_t k = 0; k < S; ++k)
+        pr[k] = std::exp(sc[k] * scale - mx), sum += pr[k];
+    for (float& v : pr)
+        v = (float)(v / sum);
+    const std::vector<float> o = gemv(wo, gemv(vt, pr, H), H);
+    std::vector<float> x1(H);
+    for (uint32_t i = 0; i < H; ++i)
+        x1[i] = hidden[i] + o[i];
+    const std::vector<float> xn2 = norm(x1, n2), g = gemv(wg, xn2, F), u = gemv(wu, xn2, F);
+    std::vector<float> act(F);
+    for (uint32_t i = 0; i < F; ++i)
+        act[i] = g[i] / (1.0F + std::exp(-g[i])) * u[i];
+    const std::vector<float> mlp = gemv(wd, act, H);
+    std::vector<float> e(H);
+    for (uint32_t i = 0; i < H; ++i)
+        e[i] = x1[i] + mlp[i];
+    // device: the 14 nodes
+    Dev<float> dh(hidden), dn1(n1), dn2(n2), dwq(wq), dwo(wo), dwg(wg), dwu(wu), dwd(wd), dk(keys), dvt(vt);
+    Dev<float> dxn(H), dq(H), dqr(H), dsc(S), dpr(S), datt(H), dout1(H), dx1(H), dxn2(H), dg(F), du(F), dact(F),
+        dmlp(H), dy(H);
+    Dev<int32_t> dpos(std::vector<int32_t>{0});
+    MuyoBinaryParams pn = Vec(H);
+    pn.param1 = eps;
+    MuyoRopeParams pr_{};
+    pr_.rope_mode = MUYO_ROPE_NEOX, pr_.nrows = 1, pr_.n_dims = H, pr_.n_offs = 0;
+    pr_.freq_scale = 1.0F, pr_.freq_base = 10000.0F, pr_.attn_factor = 1.0F;
+    pr_.theta_scale = std::pow(10000.0F, -2.0F / (float)H);
+    pr_.ne00 = H, pr_.ne01 = 1, pr_.ne02 = 1, pr_.nb01 = H, pr_.nb11 = H;
+    MuyoSoftMaxParams psm{};
+    psm.KX = S, psm.ne00 = S, psm.ne01 = 1, psm.ne02 = psm.ne12 = psm.ne13 = 1, psm.scale = scale, psm.nrows_x = 1;
+    MuyoGluParams pg{};
+    pg.N = F, pg.ne00 = F, pg.ne20 = F, pg.mode = MUYO_GLU_SPLIT;
+    pg.nb00 = pg.nb10 = pg.nb20 = 1;
+    pg.nb01 = pg.nb11 = pg.nb21 = F, pg.nb02 = pg.nb03 = pg.nb12 = pg.nb13 = pg.nb22 = pg.nb23 = F;
+    pg.ne21 = pg.ne22 = 1;
+    const MuyoMatVecParams mhh = MatVec(H, H), mhs = MatVec(H, S), msh = MatVec(S, H), mhf = MatVec(H, F),
+                           mfh = MatVec(F, H);
+    const MuyoBinaryParams pa = Vec(H);
+    Check(muyo_cuda_rms_norm(&pn, dh.p, dn1.p, dxn.p, nullptr), "PreNorm");
+    Check(muyo_cuda_mat_vec_f32(&mhh, dwq.p, dxn.p, dq.p, nullptr, nullptr, nullptr), "QProj");
+    Check(muyo_cuda_rope(&pr_, dq.p, dpos.p, nullptr, dqr.p, nullptr), "QRope");
+    Check(muyo_cuda_mat_vec_f32(&mhs, dk.p, dqr.p, dsc.p, nullptr, nullptr, nullptr), "AttnScores");
+    Check(muyo_cuda_soft_max(&psm, dsc.p, nullptr, nullptr, dpr.p, nullptr), "AttnWeights");
+    Check(muyo_cuda_mat_vec_f32(&msh, dvt.p, dpr.p, datt.p, nullptr, nullptr, nullptr), "AttnOut");
+    Check(muyo_cuda_mat_vec_f32(&mhh, dwo.p, datt.p, dout1.p, nullptr, nullptr, nullptr), "OProj");
+    Check(muyo_cuda_add(&pa, dh.p, dout1.p, dx1.p, nullptr), "Residual1");
+    Check(muyo_cuda_rms_norm(&pn, dx1.p, dn2.p, dxn2.p, nullptr), "PostNorm");
+    Check(muyo_cuda_mat_vec_f32(&mhf, dwg.p, dxn2.p, dg.p, nullptr, nullptr, nullptr), "GateProj");
+    Check(muyo_cuda_mat_vec_f32(&mhf, dwu.p, dxn2.p, du.p, nullptr, nullptr, nullptr), "UpProj");
+    Check(muyo_cuda_swiglu(&pg, dg.p, du.p, dact.p, nullptr), "SwiGLU");
+    Check(muyo_cuda_mat_vec_f32(&mfh, dwd.p, dact.p, dmlp.p, nullptr, nullptr, nullptr), "DownProj");
+    Check(muyo_cuda_add(&pa, dx1.p, dmlp.p, dy.p, nullptr), "Residual2");
+    return Close(dy.Get(), e, 1e-3, "layer (the reference check's 14 nodes)");
+}
+
+// The decode step's fused layer (muyo_cuda_layer_step, five kernels) on a small Qwen2 layer with the
+// same sizes: one head of 64, F32 cache, positions 0..7 decoded in turn, every output compared with a
+// CPU restatement of the layer.
+static bool FusedLayerSteps()
+{
+    {
         const uint32_t H = 64, F = 128, S = 8, hd = 64;
         const float eps = 1e-6F, base = 10000.0F;
         auto pat = [](uint32_t i, uint32_t m, float s) { return s * (float)((int)((i * 37u + 11u) % m) - (int)(m / 2)); };
@@ -551,6 +667,15 @@ int RunTransformerLayer()
             ok = Close(dy.Get(), e, 1e-3, what.c_str()) && ok;
         }
         return ok;
+    }
+}
+
+int RunTransformerLayer()
+{
+    return Guard("layer", [] {
+        const bool a = ReferenceLayerChain();
+        const bool b = FusedLayerSteps();
+        return a && b;
     });
 }
 }  // namespace muyo_llm

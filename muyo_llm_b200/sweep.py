@@ -130,6 +130,68 @@ SAMPLER_CASES = [  # (label, SamplerParams fields): the reference's flags (src/m
 ]
 
 
+LAYER_ARCHS = {  # (hidden, ffn, heads, kv_heads): BASELINE config 3 and a 7B-class layer
+    "0.5b": (896, 4864, 14, 2),
+    "7b": (4096, 14336, 32, 8),
+}
+
+
+def layer(iters: int = 0, peak_gbs: float = 6462.1, seed: int = 7, archs=("0.5b", "7b"), pos: int = 1023):
+    """muyo_cuda_layer_step (the five fused kernels of one decoder layer: rms_norm + QKV + bias,
+    RoPE + KV append + split-K attention, merge + O + residual, rms_norm + gate/up + SwiGLU,
+    down + residual) at position `pos` with an F16 cache of 2048 positions. Weights N(0, 0.02) F16;
+    enough weight sets rotate that no call finds its weights in L2. Algorithmic bytes: every weight
+    once, the KV rows 0..pos read, the new row written."""
+    import numpy as np
+
+    from . import _abi
+
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    out = []
+    for arch in archs:
+        H, F, nh, nkv = LAYER_ARCHS[arch]
+        hd = H // nh
+        qkv_rows = H + 2 * nkv * hd
+        S = 2048
+        cfg = _abi.Qwen2Config(1, H, F, nh, nkv, 8, S, 1e-6, 1e6, _abi.KV_F16)
+        wbytes = (qkv_rows * H + H * H + 3 * F * H) * 2
+        n_set = max(1, math.ceil(2 * L2_BYTES / wbytes))
+
+        def mat(r, c):
+            return (torch.randn(r, c, generator=g, device="cuda") * 0.02).half()
+
+        sets = []
+        for _ in range(n_set):
+            t = {"attn_norm": torch.ones(H, device="cuda"), "wqkv": mat(qkv_rows, H),
+                 "bqkv": torch.randn(qkv_rows, generator=g, device="cuda") * 0.02, "wo": mat(H, H),
+                 "ffn_norm": torch.ones(H, device="cuda"), "wgate": mat(F, H), "wup": mat(F, H), "wdown": mat(H, F)}
+            w = _abi.LayerWeights(*[t[n].data_ptr() for n in ("attn_norm", "wqkv", "bqkv", "wo", "ffn_norm", "wgate",
+                                                              "wup", "wdown")])
+            sets.append((t, w))
+        kc = (torch.randn(nkv, S, hd, generator=g, device="cuda")).half()
+        vc = (torch.randn(nkv, S, hd, generator=g, device="cuda")).half()
+        posd = torch.tensor([pos], dtype=torch.int32, device="cuda")
+        x = torch.randn(H, generator=g, device="cuda")
+        y = torch.empty(H, device="cuda")
+        ws_bytes = _abi.lib().muyo_cuda_layer_workspace_size(cfg)
+        ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda")
+        stream = torch.cuda.current_stream().cuda_stream
+
+        def call(i):
+            _abi.call("muyo_cuda_layer_step", cfg, sets[i][1], kc.data_ptr(), vc.data_ptr(), posd.data_ptr(),
+                      x.data_ptr(), y.data_ptr(), ws.data_ptr(), ws_bytes, stream)
+
+        n = iters or 200
+        ms = _time_calls(call, n_set, n)
+        alg = wbytes + qkv_rows * 4 + 2 * H * 4 + 2 * nkv * (pos + 1) * hd * 2 + 2 * nkv * hd * 2
+        out.append(_result("muyo_cuda_layer_step", [H, F, nh, nkv, hd], alg, ms, peak_gbs, arch=arch, pos=pos,
+                           weight_sets=n_set, kernels=5))
+        del sets, kc, vc
+        torch.cuda.empty_cache()
+    return out
+
+
 def sampler(iters: int = 0, peak_gbs: float = 6462.1, seed: int = 7, n_prompt: int = 32, n_predict: int = 256):
     """muyo_cuda_sample on a 151936-entry logits row (N(0, 3^2), 64 history ids), device time per call:
     a CUDA graph of `iters` (restore copy of the row, sample) pairs, minus a graph of the copies
@@ -311,7 +373,7 @@ SHARDED_SHAPES = [(151936, 896), (4096, 4096), (14336, 4096), (128256, 4096)]
 
 
 def gemv_sharded(rank: int, world: int, dist=None, iters: int = 0, peak_gbs: float = 6462.1, seed: int = 7,
-                 shapes=None):
+                 shapes=None, check: bool = False):
     """Row-sharded GEMV (muyo_llm_b200/shard.py) over `world` GPUs, one rank per GPU: each rank holds
     ceil(M / world) rows of W. Per shape, two timings on the device (max over ranks):
     * kernel: the local muyo_cuda_mat_vec_f16_argmax alone -> per-GPU GB/s of its shard;
@@ -319,7 +381,10 @@ def gemv_sharded(rank: int, world: int, dist=None, iters: int = 0, peak_gbs: flo
       the cross-rank pick, NCCL all-gather of the output slices -> aggregate GB/s of the full matrix.
     * fused (N > 1): muyo_cuda_mat_vec_f16_allgather, the same result from one kernel per GPU that
       stores its slice and pair into every GPU over NVLink.
-    Shards rotate over enough copies that more than 4x L2 is touched between two reads of one copy."""
+    Shards rotate over enough copies that more than 4x L2 is touched between two reads of one copy.
+    With `check`, every rank also compares the gathered output of both paths with one GPU's GEMV of
+    the whole matrix (bit-identical: each row's arithmetic does not depend on the sharding) and the
+    token with that output's first-index maximum; `parity` is true when every rank agrees."""
     from . import shard
 
     g = torch.Generator(device="cuda")
@@ -371,6 +436,7 @@ def gemv_sharded(rank: int, world: int, dist=None, iters: int = 0, peak_gbs: flo
         ms_k = timed(lambda i: backends[i].gemv_argmax(x))
         ms_e = timed(lambda i: calls[i](x))
         ms_p = None
+        parity = None
         if dist is not None and local > 0:
             p2p = shard.P2PShardedGemv(W[0], rows, world, rank)
 
@@ -380,6 +446,8 @@ def gemv_sharded(rank: int, world: int, dist=None, iters: int = 0, peak_gbs: flo
 
             ms_p = timed(fused)
             p2p.check()
+            if check:
+                parity = _sharded_parity(calls[0], p2p, W[0], x, rows, cols, world, begin, local, dist)
             dist.barrier()
             p2p.close()
         total = rows * cols * 2 + cols * 4 + rows * 4
@@ -393,10 +461,42 @@ def gemv_sharded(rank: int, world: int, dist=None, iters: int = 0, peak_gbs: flo
                     "fused_GB_s_aggregate": None if ms_p is None else total / (ms_p * 1e-3) / 1e9,
                     "fused_includes": "one kernel per GPU: local GEMV, output stored into every GPU over NVLink, pairs "
                                       "and flags through peer memory, pick",
+                    "issue": "each call issued from Python (host issue time included in the e2e columns)",
+                    "parity": parity,
                     "shard_copies": n_buf, "calls": n})
         del W, backends, calls
         torch.cuda.empty_cache()
     return out
+
+
+def _sharded_parity(call, p2p, w_local, x, rows, cols, world, begin, local, dist) -> bool:
+    """Both sharded paths against one GPU computing the whole matrix: the full W is rebuilt on every
+    rank from the ranks' shards (NCCL all-gather of the padded shards), its GEMV taken by
+    muyo_cuda_mat_vec_f16, and the first-index maximum taken on the host."""
+    from . import shard
+
+    per = shard.rows_per_rank(rows, world)
+    pad = torch.zeros(per, cols, dtype=torch.float16, device="cuda")
+    pad[:local] = w_local[:local]
+    every = torch.empty(world * per, cols, dtype=torch.float16, device="cuda")
+    dist.all_gather_into_tensor(every, pad)
+    full_w = torch.cat([every[r * per:r * per + (shard.shard_rows(rows, world, r)[1] - shard.shard_rows(rows, world, r)[0])]
+                        for r in range(world)])
+    full = torch.empty(rows, dtype=torch.float32, device="cuda")
+    nodes.mat_vec_f16(nodes.mat_vec_params(cols, rows), full_w, x, full)
+    tok_n, y_n = call(x)
+    p2p.w = w_local
+    tok_p = p2p(x)
+    y_p = p2p.output()
+    torch.cuda.synchronize()
+    ref = full.cpu().numpy()
+    best = int(ref.argmax())  # numpy's argmax returns the first index of the maximum
+    ok = (bool(torch.equal(y_n, full)) and bool(torch.equal(y_p, full)) and int(tok_n.item()) == best
+          and int(tok_p.item()) == best)
+    t = torch.tensor([1 if ok else 0], dtype=torch.int32, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    del full_w, every, pad
+    return bool(t.item())
 
 
 class _LocalBackend:
