@@ -98,6 +98,7 @@ struct GemvFused {
     // the error word a timed-out wait for the tile sets (MUYO_ETIMEOUT on the host)
     unsigned wofs;
     int* err;
+    int prefetch_all;  // non-SW path: every CTA asks L2 for all its rows before the dependency wait
 };
 
 // Stage the merged attention output (the O projection's input, K = heads * hd) from the split-K
@@ -321,13 +322,19 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvFused a)
             if (NMAT > 1)
                 bulk_g2s(wsm + tile_bytes, a.w1 + (size_t)r0 * a.K, bytes, &wbar);
         }
-    } else if (threadIdx.x == 0 && (int)blockIdx.x * RG * ROWS < a.rows) {
-        // The weights do not depend on the previous kernel: start streaming this CTA's first tile
-        // into L2 while the input is staged.
-        const int r0 = blockIdx.x * RG * ROWS, nr = min(RG * ROWS, a.rows - r0);
-        prefetch_rows_l2(a.w0, a.ldw, r0, nr);
-        if (NMAT > 1)
-            prefetch_rows_l2(a.w1, a.ldw, r0, nr);
+    } else if (threadIdx.x == 0) {
+        // The weights do not depend on the previous kernel: start streaming this CTA's tiles into L2
+        // while the previous kernel drains and the input is staged - all of them when the matrices fit
+        // L2 (prefetch_all), else the first.
+        const int ntl = (a.rows + RG * ROWS - 1) / (RG * ROWS);
+        for (int t = blockIdx.x; t < ntl; t += gridDim.x) {
+            const int r0 = t * RG * ROWS, nr = min(RG * ROWS, a.rows - r0);
+            prefetch_rows_l2(a.w0, a.ldw, r0, nr);
+            if (NMAT > 1)
+                prefetch_rows_l2(a.w1, a.ldw, r0, nr);
+            if (!a.prefetch_all)
+                break;
+        }
     }
     if (threadIdx.x == 0) {
 #pragma unroll
@@ -386,7 +393,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvFused a)
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
         const int row0 = (tile * RG + rg) * ROWS;
         const int nvalid = min(ROWS, a.rows - row0);
-        if (!SW && threadIdx.x == 0 && tile + (int)gridDim.x < ntiles) {  // the next tile of this CTA, to L2
+        if (!SW && !a.prefetch_all && threadIdx.x == 0 && tile + (int)gridDim.x < ntiles) {  // the next tile, to L2
             const int r1 = (tile + gridDim.x) * RG * ROWS, nr = min(RG * ROWS, a.rows - r1);
             prefetch_rows_l2(a.w0, a.ldw, r1, nr);
             if (NMAT > 1)
@@ -578,10 +585,11 @@ static int launch_gemv(const GemvFused& a, int max_ctas, cudaStream_t s, bool pd
     if (smem > 48 * 1024)
         MUYO_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int grid = ntiles < max_ctas ? ntiles : max_ctas;
+    GemvFused b = a;
+    b.prefetch_all = (size_t)a.rows * a.ldw * 2 * NMAT <= (64ull << 20) ? 1 : 0;
     const int resident = resident_ctas(k, kGemvThreads, smem);
     if (grid > resident)
         grid = resident;
-    GemvFused b = a;
     set_prefetch_slices(b.pf, grid);
     MUYO_CUDA_TRY(launch_kernel(k, dim3(grid), dim3(kGemvThreads), smem, s, pdl, b));
     MUYO_LAUNCH_CHECK();
@@ -684,6 +692,17 @@ struct LayerPtrs {
     const __half* wdown;
 };
 
+// Where the attention chunks' partials are merged. Every CTA of the O projection re-merges all of them
+// while staging its input: cheap while the partial set is small (0.5B: 118 KB at 2048 positions),
+// not for wide models with long caches (7B-class: 532 KB per CTA). Above this size the last CTA of
+// each KV head merges its group's partials and writes the attention output instead.
+constexpr size_t kMergeInOBytes = 128 * 1024;
+
+static bool merge_in_o(const Shape& s)
+{
+    return sizeof(float) * (size_t)s.heads * s.max_chunks * (s.head_dim + 2) <= kMergeInOBytes;
+}
+
 template <typename KV, int HD>
 static int launch_attention_fused(const Shape& s, const float* qkv, void* kc, void* vc, const int32_t* pos,
                                   float* out, float* part, int32_t* counters, cudaStream_t st, bool pdl)
@@ -691,15 +710,15 @@ static int launch_attention_fused(const Shape& s, const float* qkv, void* kc, vo
     AttnDev p{s.heads, s.kv_heads, s.gqa, s.max_seq, 0, 1.0f / sqrtf((float)s.head_dim), (double)s.rope_base,
               s.max_chunks, s.rope_cs};
     const size_t smem = (size_t)attn_smem_floats(HD, s.gqa) * sizeof(float);
-    // Every chunk writes its partial (no output pointer, no inline merge): the O projection merges
-    // them while staging its input.
-    auto k = k_attention<KV, HD, true, false>;
+    // merge_in_o: every chunk writes its partial and the O projection merges them while staging its
+    // input; else the last CTA of each KV head merges into `out` (a single chunk writes it directly).
+    const bool in_o = merge_in_o(s);
+    auto k = in_o ? k_attention<KV, HD, true, false> : k_attention<KV, HD, true, true>;
     MUYO_CUDA_TRY(max_shared_carveout(k));
     if (smem > 48 * 1024)
         MUYO_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    (void)out;
     MUYO_CUDA_TRY(launch_kernel(k, dim3(s.kv_heads, s.max_chunks), dim3(kAttnThreads), smem, st, pdl, p, qkv,
-                                static_cast<KV*>(kc), static_cast<KV*>(vc), pos, static_cast<float*>(nullptr), part,
+                                static_cast<KV*>(kc), static_cast<KV*>(vc), pos, in_o ? nullptr : out, part,
                                 counters));
     MUYO_LAUNCH_CHECK();
     return MUYO_OK;
@@ -764,7 +783,7 @@ static int layer_forward(const Shape& s, const LayerPtrs& w, void* kc, void* vc,
     rc = attention_fused(s, ws.qkv, kc, vc, pos, ws.attn, ws.part, ws.counters, st, pdl);
     if (rc)
         return rc;
-    // 3. merge of the attention partials -> o_proj + residual
+    // 3. merge of the attention partials (or the merged output) -> o_proj + residual
     GemvFused o{};
     o.attn_part = ws.part;
     o.pos = pos;
@@ -781,7 +800,12 @@ static int layer_forward(const Shape& s, const LayerPtrs& w, void* kc, void* vc,
     o.err = err;
     if (pf)
         o.pf = pf[1];
-    rc = launch_gemv<1, 4, 1, 2, PRO_MERGE, EPI_RESIDUAL, 2, 4>(o, sms * 8, st, pdl);
+    if (merge_in_o(s)) {
+        rc = launch_gemv<1, 4, 1, 2, PRO_MERGE, EPI_RESIDUAL, 2, 4>(o, sms * 8, st, pdl);
+    } else {
+        o.x = ws.attn;
+        rc = launch_gemv<1, 4, 1, 2, PRO_PLAIN, EPI_RESIDUAL, 2, 4>(o, sms * 8, st, pdl);
+    }
     if (rc)
         return rc;
     // 4. rms_norm -> gate, up -> SwiGLU
