@@ -469,10 +469,14 @@ def gemv_sharded(rank: int, world: int, dist=None, iters: int = 0, peak_gbs: flo
     return out
 
 
-def _sharded_parity(call, p2p, w_local, x, rows, cols, world, begin, local, dist) -> bool:
+def _sharded_parity(call, p2p, w_local, x, rows, cols, world, begin, local, dist) -> dict:
     """Both sharded paths against one GPU computing the whole matrix: the full W is rebuilt on every
-    rank from the ranks' shards (NCCL all-gather of the padded shards), its GEMV taken by
-    muyo_cuda_mat_vec_f16, and the first-index maximum taken on the host."""
+    rank from the ranks' shards (NCCL all-gather of the padded shards) and its GEMV taken by
+    muyo_cuda_mat_vec_f16. `ok` (on every rank): the two paths' gathered outputs are bit-identical
+    and each token is the first index of the maximum of its output; the outputs are within
+    1e-4 (1 + |e|) of one GPU's (a shard of K >= 2048 columns may split K over other warp counts
+    than the whole matrix, so its F32 sums can differ in the last bits); `bit_identical` and
+    `token_equal`: against one GPU exactly."""
     from . import shard
 
     per = shard.rows_per_rank(rows, world)
@@ -489,14 +493,16 @@ def _sharded_parity(call, p2p, w_local, x, rows, cols, world, begin, local, dist
     tok_p = p2p(x)
     y_p = p2p.output()
     torch.cuda.synchronize()
-    ref = full.cpu().numpy()
-    best = int(ref.argmax())  # numpy's argmax returns the first index of the maximum
-    ok = (bool(torch.equal(y_n, full)) and bool(torch.equal(y_p, full)) and int(tok_n.item()) == best
-          and int(tok_p.item()) == best)
-    t = torch.tensor([1 if ok else 0], dtype=torch.int32, device="cuda")
+    yn, yp, ref = y_n.cpu().numpy(), y_p.cpu().numpy(), full.cpu().numpy()
+    tn, tp = int(tok_n.item()), int(tok_p.item())
+    close = bool((abs(yn.astype("float64") - ref) <= 1e-4 * (1 + abs(ref.astype("float64")))).all())
+    ok = bool((yn == yp).all()) and tn == tp == int(yn.argmax()) and close
+    exact = bool((yn == ref).all())
+    same_tok = tn == int(ref.argmax())
+    t = torch.tensor([int(ok), int(exact), int(same_tok)], dtype=torch.int32, device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MIN)
     del full_w, every, pad
-    return bool(t.item())
+    return {"ok": bool(t[0].item()), "bit_identical": bool(t[1].item()), "token_equal": bool(t[2].item())}
 
 
 class _LocalBackend:
