@@ -431,8 +431,13 @@ int muyo_model_set_sampler(MuyoModel* m, const MuyoSamplerParams* p, void* strea
  * (max, first index) pairs and flags through peer memory, and writes the greedy index to *token
  * (device int32) on every rank; the full output is then at muyo_p2p_output on every rank. Calls
  * alternate between the two output slots, so muyo_p2p_output (the slot of the latest call) changes
- * from call to call, and a peer that runs one call ahead writes the other slot: the output of a call
- * stays intact until this rank issues the call after next; read it on the same stream before that.
+ * from call to call, and a peer that runs one call ahead writes the other slot. A peer reaches the
+ * call after next (which rewrites this slot) only once this rank's next call has posted its flags, so
+ * the output of a call stays intact until this rank's next call: read it on the same stream before.
+ * The call count lives on the device, so calls may be captured in a CUDA graph and replayed (every
+ * rank replaying the same calls): the n-th call since the group was created uses slot n & 1, and
+ * muyo_p2p_output counts only the calls issued directly - after replays of a graph holding an odd
+ * number of calls the caller picks the slot by the parity of its own total.
  * The wait for the peers is bounded (2 s): if a rank does not take part, the others finish with
  * token 0 and muyo_p2p_check (synchronising) reports MUYO_ETIMEOUT. The ranks' call counters then
  * disagree, so the group is dead: later calls return MUYO_ESTATE, and every rank must destroy its

@@ -115,6 +115,50 @@ __device__ __forceinline__ void warp_gemv_f16_range_xg(const GemvArgs<ROWS, U, 1
     }
 }
 
+// One row tile of the F16 GEMV. Row group rg = warp / KSPLIT holds ROWS rows from row0; its KSPLIT
+// warps add the contiguous chunk ranges [c_begin, c_end) of those rows, and their sums meet in
+// shared memory in a fixed order. On return the group's ks == 0 warp holds the rows' sums in every
+// lane. Every warp of the CTA calls it the same number of times (barriers inside when KSPLIT > 1).
+template <int ROWS, int U, int KSPLIT, bool XG>
+__device__ __forceinline__ void mat_vec_tile_f16(const GemvArgs<ROWS, U, 1>& ga, int row0, int nvalid,
+                                                 const float* xs, const float* xg, int k8, int ncols, int c_begin,
+                                                 int c_end, int lane, int warp, int ks, float (*ksum)[ROWS],
+                                                 float (&acc)[1][ROWS])
+{
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r)
+        acc[0][r] = 0.0f;
+    if (nvalid > 0) {
+        if (XG) {
+            warp_gemv_f16_range_xg<ROWS, U>(ga, row0, nvalid, xg, c_begin, c_end, lane, acc);
+        } else {
+            warp_gemv_f16_range<ROWS, U, 1>(ga, row0, nvalid, xs, k8, c_begin, c_end, lane, acc);
+            if (ks == KSPLIT - 1)  // columns past the last full chunk
+                warp_gemv_f16_tail<ROWS, 1>(ga.w, ga.ldw, row0, nvalid, xs, k8, ncols, lane, acc);
+        }
+        warp_reduce_acc<ROWS, 1>(acc);
+    }
+    if (KSPLIT > 1) {
+        if (lane == 0) {
+#pragma unroll
+            for (int r = 0; r < ROWS; ++r)
+                ksum[warp][r] = acc[0][r];
+        }
+        __syncthreads();
+        if (ks == 0) {
+#pragma unroll
+            for (int r = 0; r < ROWS; ++r) {
+                float t = ksum[warp][r];
+#pragma unroll
+                for (int j = 1; j < KSPLIT; ++j)
+                    t += ksum[warp + j][r];
+                acc[0][r] = t;
+            }
+        }
+        __syncthreads();
+    }
+}
+
 // XG: x is read from global memory (K a multiple of 8, x 16-byte aligned, one batch, small weights):
 // the first weight and x loads leave together, with no staging round trip and no block barrier
 // before them.
@@ -154,38 +198,8 @@ __global__ void __launch_bounds__(kThreads) k_mat_vec_f16(MatVecDev p, const __h
         if (p.k8 > 0 && warp == 0 && lane == 0 && next0 < p.rows)
             prefetch_rows_l2(Ab, (size_t)p.stride_a, next0, min(block_rows, p.rows - next0));
         float acc[1][ROWS];
-#pragma unroll
-        for (int r = 0; r < ROWS; ++r)
-            acc[0][r] = 0.0f;
-        if (nvalid > 0) {
-            if (XG) {
-                warp_gemv_f16_range_xg<ROWS, U>(ga, row0, nvalid, Bb, c_begin, c_end, lane, acc);
-            } else {
-                warp_gemv_f16_range<ROWS, U, 1>(ga, row0, nvalid, xs, p.k8, c_begin, c_end, lane, acc);
-                if (ks == KSPLIT - 1)  // columns past the last full chunk
-                    warp_gemv_f16_tail<ROWS, 1>(ga.w, ga.ldw, row0, nvalid, xs, p.k8, p.ncols, lane, acc);
-            }
-            warp_reduce_acc<ROWS, 1>(acc);
-        }
-        if (KSPLIT > 1) {
-            if (lane == 0) {
-#pragma unroll
-                for (int r = 0; r < ROWS; ++r)
-                    ksum[warp][r] = acc[0][r];
-            }
-            __syncthreads();
-            if (ks == 0) {
-#pragma unroll
-                for (int r = 0; r < ROWS; ++r) {
-                    float t = ksum[warp][r];
-#pragma unroll
-                    for (int j = 1; j < KSPLIT; ++j)
-                        t += ksum[warp + j][r];
-                    acc[0][r] = t;
-                }
-            }
-            __syncthreads();
-        }
+        mat_vec_tile_f16<ROWS, U, KSPLIT, XG>(ga, row0, nvalid, xs, Bb, p.k8, p.ncols, c_begin, c_end, lane, warp, ks,
+                                              ksum, acc);
         if (ks == 0 && lane == 0 && nvalid > 0) {
 #pragma unroll
             for (int r = 0; r < ROWS; ++r)
@@ -313,6 +327,19 @@ static int mat_vec_prepare(const MuyoMatVecParams* p, const void* a, const float
     return MUYO_OK;
 }
 
+// Few row blocks per SM (with long rows): 2 or 4 warps per row, so the blocks are smaller and spread
+// evenly over the SMs, and more loads are in flight at the start and in the tail. Loads in flight per
+// lane then grow with K so that a warp covers a long row in few round trips: U = 8 chunks of 16 bytes
+// per row per lane from 8 chunks per lane on, else 4 (each lane still adds its chunks in column order).
+static int mat_vec_ksplit(const MatVecDev& q, int batches, int rows_per_warp)
+{
+    const int tiles1 = (q.rows + 8 * rows_per_warp - 1) / (8 * rows_per_warp);
+    return q.k8 < 256 || batches > 1 ? 1 : (tiles1 < 2 * sm_count() ? 4 : (tiles1 < 6 * sm_count() ? 2 : 1));
+}
+
+// Rows per warp of the F16 GEMV: 2 once there are two 16-row blocks per SM.
+static bool mat_vec_two_rows(const MatVecDev& q) { return (q.rows + 15) / 16 >= 2 * sm_count(); }
+
 template <int ROWS>
 static int launch_mat_vec(bool f16, const MatVecDev& q, int batches, const void* a, const float* b, float* d,
                           const float* f0, const float* f1, cudaStream_t s)
@@ -328,14 +355,9 @@ static int launch_mat_vec(bool f16, const MatVecDev& q, int batches, const void*
     const size_t smem = (size_t)q.ncols * sizeof(float);
     dim3 grid(gx, batches);
     if (f16) {
-        // Few row blocks per SM (with long rows): 2 or 4 warps per row, so the blocks are smaller and
-        // spread evenly over the SMs, and more loads are in flight at the start and in the tail.
-        const int tiles1 = (q.rows + 8 * ROWS - 1) / (8 * ROWS);
-        const int ksplit = q.k8 < 256 || batches > 1 ? 1 : (tiles1 < 2 * sm_count() ? 4 : (tiles1 < 6 * sm_count() ? 2 : 1));
+        const int ksplit = mat_vec_ksplit(q, batches, ROWS);
         if (ksplit > 1)
             grid.x = (unsigned)((q.rows + 8 / ksplit * ROWS - 1) / (8 / ksplit * ROWS));
-        // Loads in flight per lane grow with K so that a warp covers a long row in few round trips:
-        // U chunks of 16 bytes per row per lane (each lane still adds its chunks in column order).
         const int lane_chunks = q.k8 / ksplit / 32;
         // Below 16 MB of weights a call is mostly its fixed chain, which reading x from global memory
         // shortens (896x4864: 4.98 -> 4.05 us); for streaming shapes the x reads through L1 cost more
@@ -383,7 +405,7 @@ static int mat_vec_any(bool f16, const MuyoMatVecParams* p, const void* a, const
     if (rc != MUYO_OK)
         return rc;
     const int batches = p->batches ? (int)p->batches : 1;
-    const bool two_rows = (q.rows + 15) / 16 >= 2 * sm_count();
+    const bool two_rows = mat_vec_two_rows(q);
     return two_rows ? launch_mat_vec<2>(f16, q, batches, a, b, d, f0, f1, as_stream(stream))
                     : launch_mat_vec<1>(f16, q, batches, a, b, d, f0, f1, as_stream(stream));
 }
@@ -879,10 +901,12 @@ __global__ void __launch_bounds__(kThreads) k_pairs_to_pair(const ArgPair* __res
 // ---- row-sharded GEMV fused with its all-gather over NVLink peer memory ---------------------------
 // One GPU's share of y = W x over `world` GPUs of one node (one process each). Every rank owns a
 // P2PBuffer (header + two [rows_total] output slots), and every rank's buffer is mapped into every
-// other rank through CUDA IPC. Call `epoch` uses output slot and pair slot epoch & 1: a peer can be
-// at most one call ahead (it cannot finish call e + 1 before this rank publishes e + 1, which this
-// rank does only after its own call e and whatever the caller queued after it), so a peer's next call
-// writes the other slot while this rank still reads call e's. A call is one kernel per GPU:
+// other rank through CUDA IPC. Call number `epoch` (the rank's own count of calls, kept in its header
+// on the device, so that calls captured in a CUDA graph count too) uses output slot and pair slot
+// epoch & 1: a peer can be at most one call ahead (it cannot finish call e + 1 before this rank
+// publishes e + 1, which this rank does only after its own call e and whatever the caller queued
+// after it), so a peer's next call writes the other slot while this rank still reads call e's. A call
+// is one kernel per GPU:
 //   1. each CTA computes its rows and stores every value into every rank's output (NVLink stores);
 //   2. each CTA leaves its best (value, global index) in the local header, fences at system scope
 //      and counts itself in;
@@ -899,7 +923,8 @@ struct P2PHeader {
     ArgPair pairs[2][kP2PMaxRanks];   // pairs[e & 1][r]: rank r's (max value, first global index) of call e
     int counter;                      // arrivals of this rank's CTAs (reset by the last one)
     int err;                          // 5: a wait for a peer's flag expired
-    int pad[14];
+    unsigned calls;                   // this rank's calls so far (written by the last CTA of each call)
+    int pad[13];
 };
 
 struct P2PArgs {
@@ -907,8 +932,8 @@ struct P2PArgs {
     const float* x;
     int K, k8, local_rows, row_begin, rows_total, world, rank;
     long long lda;
-    unsigned epoch;
-    float* y[kP2PMaxRanks];          // every rank's output slot of this call (this rank's slice goes to each)
+    long long slot_floats;           // floats from output slot 0 to slot 1
+    float* y[kP2PMaxRanks];          // every rank's output slot 0 (this rank's slice goes to each)
     P2PHeader* hdr[kP2PMaxRanks];    // every rank's header
     ArgPair* cta_pairs;              // local scratch: one pair per CTA
     int32_t* token;
@@ -926,40 +951,72 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p)
     return v;
 }
 
-template <int ROWS>
+// Rows of a CTA's output gathered in shared memory before they leave for every rank (a multiple of
+// every tile height 8 / KSPLIT * ROWS).
+constexpr int kP2PChunkRows = 256;
+
+// Step 1 runs the row tiles of k_mat_vec_f16 with the same ROWS, U and KSPLIT (mat_vec_ksplit), so a
+// shard's values are bit-identical to muyo_cuda_mat_vec_f16 on that shard. Each CTA takes a
+// contiguous range of tiles; its values collect in shared memory and leave in runs of up to
+// kP2PChunkRows rows, consecutive threads storing consecutive rows of one rank's slot.
+template <int ROWS, int U, int KSPLIT>
 __global__ void __launch_bounds__(kThreads) k_gemv_allgather(P2PArgs p)
 {
+    constexpr int RG = kThreads / 32 / KSPLIT, BR = RG * ROWS;
+    static_assert(kP2PChunkRows % BR == 0, "the chunk holds whole tiles");
     extern __shared__ float xs[];
+    __shared__ float ksum[kThreads / 32][ROWS];
+    __shared__ float ybuf[kP2PChunkRows];
     __shared__ int last_sm;
-    pdl_wait();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int rg = warp / KSPLIT, ks = warp % KSPLIT;
+    const int ntiles = (p.local_rows + BR - 1) / BR;
+    const int t_begin = (int)((long long)ntiles * blockIdx.x / gridDim.x);
+    const int t_end = (int)((long long)ntiles * (blockIdx.x + 1) / gridDim.x);
+    if (threadIdx.x == 0 && t_begin < t_end)
+        prefetch_rows_l2(p.A, (size_t)p.lda, t_begin * BR, min(BR, p.local_rows - t_begin * BR));
+    pdl_wait();  // the L2 prefetch above is only a hint; every read of A, x or the buffers comes after this wait
     pdl_trigger();
+    // This call's number: the previous call's last CTA stored its own (stream order makes it visible);
+    // this call's last CTA stores the next one only after every CTA of this call has arrived.
+    const unsigned epoch = __ldcg(&p.hdr[p.rank]->calls) + 1u;
+    const long long slot = (long long)(epoch & 1u) * p.slot_floats;
     stage_x_split(xs, p.x, p.K, p.k8);
     __syncthreads();
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    GemvArgs<ROWS, 4, 1> ga{{p.A}, (size_t)p.lda};
+    const int c_begin = (int)((long long)p.k8 * ks / KSPLIT), c_end = (int)((long long)p.k8 * (ks + 1) / KSPLIT);
+    GemvArgs<ROWS, U, 1> ga{{p.A}, (size_t)p.lda};
     float bv = -INFINITY;
     int bi = INT_MAX;
-    for (int row0 = (blockIdx.x * nw + warp) * ROWS; row0 < p.local_rows; row0 += gridDim.x * nw * ROWS) {
+    int chunk0 = t_begin * BR;  // first local row held in ybuf
+    for (int tile = t_begin; tile < t_end; ++tile) {  // the same trip count in every warp
+        const int row0 = tile * BR + rg * ROWS;
         const int nvalid = min(ROWS, p.local_rows - row0);
+        const int next0 = (tile + 1) * BR;
+        if (warp == 0 && lane == 0 && tile + 1 < t_end)
+            prefetch_rows_l2(p.A, (size_t)p.lda, next0, min(BR, p.local_rows - next0));
         float acc[1][ROWS];
-#pragma unroll
-        for (int r = 0; r < ROWS; ++r)
-            acc[0][r] = 0.0f;
-        warp_gemv_f16<ROWS, 4, 1>(ga, row0, nvalid, xs, p.k8, lane, acc);
-        warp_gemv_f16_tail<ROWS, 1>(ga.w, ga.ldw, row0, nvalid, xs, p.k8, p.K, lane, acc);
-        warp_reduce_acc<ROWS, 1>(acc);
-        // lanes 0 .. world-1 each store the rows into one rank's output
-        if (lane < p.world) {
-            float* yr = p.y[lane] + p.row_begin;
+        mat_vec_tile_f16<ROWS, U, KSPLIT, false>(ga, row0, nvalid, xs, p.x, p.k8, p.K, c_begin, c_end, lane, warp, ks,
+                                                 ksum, acc);
+        if (ks == 0 && lane == 0) {
 #pragma unroll
             for (int r = 0; r < ROWS; ++r)
-                if (r < nvalid)
-                    yr[row0 + r] = acc[0][r];
+                if (r < nvalid) {
+                    ybuf[row0 + r - chunk0] = acc[0][r];
+                    if (pair_better(acc[0][r], p.row_begin + row0 + r, bv, bi))
+                        bv = acc[0][r], bi = p.row_begin + row0 + r;
+                }
         }
-#pragma unroll
-        for (int r = 0; r < ROWS; ++r)
-            if (r < nvalid && pair_better(acc[0][r], p.row_begin + row0 + r, bv, bi))
-                bv = acc[0][r], bi = p.row_begin + row0 + r;
+        const int held = next0 - chunk0;
+        if (held == kP2PChunkRows || tile + 1 == t_end) {  // uniform across the CTA
+            __syncthreads();
+            const int n = min(held, p.local_rows - chunk0);
+            for (int t = threadIdx.x; t < p.world * n; t += blockDim.x) {
+                const int r = t / n, i = t - r * n;
+                p.y[r][slot + p.row_begin + chunk0 + i] = ybuf[i];
+            }
+            __syncthreads();
+            chunk0 = next0;
+        }
     }
     const ArgPair cta = block_argmax(bv, bi);  // uniform across the CTA after its last __syncthreads
     __syncthreads();
@@ -984,18 +1041,18 @@ __global__ void __launch_bounds__(kThreads) k_gemv_allgather(P2PArgs p)
         return;
     P2PHeader* own = p.hdr[p.rank];
     own->counter = 0;
-    const int slot = p.epoch & 1;
+    const int ps = epoch & 1u;
     for (int r = 0; r < p.world; ++r)
-        p.hdr[r]->pairs[slot][p.rank] = mine;
+        p.hdr[r]->pairs[ps][p.rank] = mine;
     __threadfence_system();
     for (int r = 0; r < p.world; ++r)
-        st_release_sys(&p.hdr[r]->flags[p.rank], p.epoch);
+        st_release_sys(&p.hdr[r]->flags[p.rank], epoch);
     // every rank's slice and pair are in this buffer once its flag carries this epoch (or the next one:
     // a peer one call ahead has written the other slots)
     const unsigned long long t0 = now_ns_ops();
     bool ok = true;
     for (int r = 0; r < p.world && ok; ++r) {
-        while ((int)(ld_acquire_sys(&own->flags[r]) - p.epoch) < 0) {
+        while ((int)(ld_acquire_sys(&own->flags[r]) - epoch) < 0) {
             if (now_ns_ops() - t0 > kP2PWaitNs) {
                 ok = false;
                 atomicMax(&own->err, 5);
@@ -1007,11 +1064,12 @@ __global__ void __launch_bounds__(kThreads) k_gemv_allgather(P2PArgs p)
     int bi2 = INT_MAX;
     if (ok)
         for (int r = 0; r < p.world; ++r) {
-            const ArgPair q{__ldcg(&own->pairs[slot][r].v), __ldcg(&own->pairs[slot][r].i)};
+            const ArgPair q{__ldcg(&own->pairs[ps][r].v), __ldcg(&own->pairs[ps][r].i)};
             if (pair_better(q.v, q.i, bv2, bi2))
                 bv2 = q.v, bi2 = q.i;
         }
     *p.token = bi2 == INT_MAX ? 0 : bi2;
+    own->calls = epoch;
 }
 }  // namespace muyo
 
@@ -1408,7 +1466,7 @@ struct MuyoP2PGroup {
     void* peer[kP2PMaxRanks] = {};       // opened peer buffers (nullptr for this rank)
     ArgPair* cta_pairs = nullptr;        // per-CTA scratch (local)
     int max_ctas = 0;
-    uint32_t epoch = 0;
+    uint32_t epoch = 0;                  // calls issued through muyo_cuda_mat_vec_f16_allgather (not replays)
     bool dead = false;                   // a call timed out: the ranks' epochs no longer agree
 };
 
@@ -1524,28 +1582,43 @@ extern "C" int muyo_cuda_mat_vec_f16_allgather(MuyoP2PGroup* g, const MuyoMatVec
     args.x = b;
     args.K = q.ncols, args.k8 = q.k8, args.local_rows = q.rows, args.row_begin = (int)row_begin;
     args.rows_total = (int)g->rows_total, args.world = g->world, args.rank = g->rank, args.lda = q.stride_a;
-    args.epoch = ++g->epoch;
+    args.slot_floats = (long long)(p2p_slot_bytes(g->rows_total) / sizeof(float));
+    ++g->epoch;
     for (int r = 0; r < g->world; ++r) {
         char* base = r == g->rank ? g->buf : static_cast<char*>(g->peer[r]);
         args.hdr[r] = reinterpret_cast<P2PHeader*>(base);
-        args.y[r] = p2p_slot(base, g->rows_total, args.epoch);
+        args.y[r] = p2p_slot(base, g->rows_total, 0);
     }
     args.cta_pairs = g->cta_pairs;
     args.token = token;
-    const bool two_rows = (q.rows + 15) / 16 >= 2 * sm_count();
-    const int rows_per_cta = (two_rows ? 2 : 1) * (kThreads / 32);
-    int grid = (q.rows + rows_per_cta - 1) / rows_per_cta;
+    // The tile shape of muyo_cuda_mat_vec_f16 for the same shard (bit-identical values); the grid is what
+    // is resident at once, each CTA taking a contiguous range of tiles.
+    const bool two_rows = mat_vec_two_rows(q);
+    const int ksplit = mat_vec_ksplit(q, 1, two_rows ? 2 : 1);
+    const bool u8 = q.k8 / ksplit / 32 >= 8;
+    auto k = k_gemv_allgather<1, 4, 1>;
+#define MUYO_P2P_PICK(R)                                                                          \
+    k = ksplit == 4 ? (u8 ? k_gemv_allgather<R, 8, 4> : k_gemv_allgather<R, 4, 4>)                \
+                    : ksplit == 2 ? (u8 ? k_gemv_allgather<R, 8, 2> : k_gemv_allgather<R, 4, 2>)  \
+                                  : (u8 ? k_gemv_allgather<R, 8, 1> : k_gemv_allgather<R, 4, 1>)
+    if (two_rows)
+        MUYO_P2P_PICK(2);
+    else
+        MUYO_P2P_PICK(1);
+#undef MUYO_P2P_PICK
+    const int tile_rows = 8 / ksplit * (two_rows ? 2 : 1);
+    const int ntiles = (q.rows + tile_rows - 1) / tile_rows;
+    const size_t smem = (size_t)q.ncols * sizeof(float);
+    MUYO_CUDA_TRY(set_smem(k, smem));
+    int per_sm = 0;
+    MUYO_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, smem));
+    int grid = per_sm > 0 ? per_sm * sm_count() : 1;
     if (grid > g->max_ctas)
         grid = g->max_ctas;
-    const size_t smem = (size_t)q.ncols * sizeof(float);
+    if (grid > ntiles)
+        grid = ntiles;
     const cudaStream_t s = as_stream(stream);
-    if (two_rows) {
-        MUYO_CUDA_TRY(set_smem(k_gemv_allgather<2>, smem));
-        MUYO_CUDA_TRY(launch_kernel(k_gemv_allgather<2>, dim3(grid), dim3(kThreads), smem, s, true, args));
-    } else {
-        MUYO_CUDA_TRY(set_smem(k_gemv_allgather<1>, smem));
-        MUYO_CUDA_TRY(launch_kernel(k_gemv_allgather<1>, dim3(grid), dim3(kThreads), smem, s, true, args));
-    }
+    MUYO_CUDA_TRY(launch_kernel(k, dim3(grid), dim3(kThreads), smem, s, true, args));
     MUYO_LAUNCH_CHECK();
     return MUYO_OK;
 }

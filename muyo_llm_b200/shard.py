@@ -154,7 +154,8 @@ class P2PShardedGemv:
 
     def output_ptr(self) -> int:
         """Device address of the latest call's full [rows] F32 output (calls alternate between two
-        slots; a slot stays intact until this rank issues the call after next)."""
+        slots; peers rewrite a slot only after this rank's next call, so read it on the same stream
+        before issuing that call)."""
         yp = self.C.c_void_p()
         self._abi.call("muyo_p2p_output", self.g, self.C.byref(yp))
         return yp.value

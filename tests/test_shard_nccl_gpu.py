@@ -147,13 +147,37 @@ def _p2p_worker(rank, world, port, results):
         torch.cuda.synchronize()
         op.check()
         wfull = torch.from_numpy(w).cuda()
-        back_to_back = []
+        back_to_back, fulls = [], []
         for k, (row, _) in enumerate(plants):
             full = torch.empty(ROWS, dtype=torch.float32, device="cuda")
             nodes.mat_vec_f16(nodes.mat_vec_params(COLS, ROWS), wfull, xs[k], full)
             torch.cuda.synchronize()
+            fulls.append(full)
             back_to_back.append((int(tokens[k].item()), row, bool(torch.equal(outs[k], full))))
         out.extend(back_to_back)
+        # Two of those calls captured in a CUDA graph and replayed twice: the call count lives on the
+        # device, so each replay advances the epoch and the slots (two calls keep the host's slot
+        # parity, used for the captured output copies, in step with the device's).
+        g_tokens = torch.empty(2, dtype=torch.int32, device="cuda")
+        g_outs = [torch.empty(ROWS, dtype=torch.float32, device="cuda") for _ in range(2)]
+        torch.cuda.synchronize()
+        dist.barrier()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for k in range(2):
+                tok = op(xs[k])
+                g_tokens[k:k + 1].copy_(tok)
+                g_outs[k].copy_(op.output())
+        for _ in range(2):
+            g_tokens.fill_(-1)
+            for o in g_outs:
+                o.zero_()
+            graph.replay()
+            torch.cuda.synchronize()
+            op.check()
+            out.extend((int(g_tokens[k].item()), plants[k][0], bool(torch.equal(g_outs[k], fulls[k])))
+                       for k in range(2))
+        del graph
         # rank 1 sits one call out: rank 0's wait for its flag must expire and be reported
         dist.barrier()
         timed_out = None
@@ -182,7 +206,8 @@ def test_fused_gemv_allgather_two_gpus(cuda):
     """muyo_cuda_mat_vec_f16_allgather: the shards go to every GPU over NVLink stores and the
     pairs and flags through peer memory. The full output is bit-identical to one GPU's GEMV on
     every rank, and the token is the planted first-index maximum, also for back-to-back calls with a
-    different maximum each (the output and pair slots alternate by call). A rank that skips a call
+    different maximum each (the output and pair slots alternate by call) and for calls replayed from a
+    CUDA graph (the call count lives on the device). A rank that skips a call
     makes the others' bounded wait expire with MUYO_ETIMEOUT (no hang), after which the group
     refuses further calls (MUYO_ESTATE)."""
     import torch
