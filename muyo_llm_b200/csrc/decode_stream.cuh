@@ -13,7 +13,7 @@
 //              memory, one piece of whole rows at a time, each piece guarded by a full/empty mbarrier
 //              pair. The ring holds most of a layer, so the weights of later phases arrive while the
 //              current phase waits on its inputs. The producer keeps only a few pieces in flight
-//              while a layer runs (16 KB pieces, 4 deep: deep copy queues stretch the latency of the
+//              while a layer runs (28 KB pieces, 2 deep: deep copy queues stretch the latency of the
 //              activation hand-offs) and more for the LM head (28 KB, 6 deep), which has no chain.
 //   hand-offs  every activation a phase produces (q/k/v, attention partials, h1, the SwiGLU output,
 //              the layer output) is written as 64-bit words {tag, value}: a single-copy-atomic store
