@@ -426,13 +426,15 @@ int muyo_model_set_sampler(MuyoModel* m, const MuyoSamplerParams* p, void* strea
  *                     handle_out;
  *   muyo_p2p_connect  opens every other rank's handle (handles: world of them, in rank order).
  * muyo_cuda_mat_vec_f16_allgather is a collective: every rank calls it, in the same order, with its
- * contiguous shard (rows [row_begin, row_begin + p->rows) of the full matrix). One kernel per GPU
+ * contiguous shard (rows [row_begin, row_begin + p->rows) of the full matrix; p->rows may be 0 when
+ * there are more ranks than rows, and A is then not read). One kernel per GPU
  * computes the shard, stores it into every rank's output over NVLink, exchanges the shards'
- * (max, first index) pairs and flags through peer memory, and writes the greedy index to *token
+ * (max, first index) pairs through peer memory as words tagged with the call's number (a pair that
+ * arrives also says its rank's rows are in), and writes the greedy index to *token
  * (device int32) on every rank; the full output is then at muyo_p2p_output on every rank. Calls
  * alternate between the two output slots, so muyo_p2p_output (the slot of the latest call) changes
  * from call to call, and a peer that runs one call ahead writes the other slot. A peer reaches the
- * call after next (which rewrites this slot) only once this rank's next call has posted its flags, so
+ * call after next (which rewrites this slot) only once this rank's next call has posted its pair, so
  * the output of a call stays intact until this rank's next call: read it on the same stream before.
  * The call count lives on the device, so calls may be captured in a CUDA graph and replayed (every
  * rank replaying the same calls): the n-th call since the group was created uses slot n & 1, and

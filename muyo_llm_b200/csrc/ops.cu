@@ -910,21 +910,24 @@ __global__ void __launch_bounds__(kThreads) k_pairs_to_pair(const ArgPair* __res
 //   1. each CTA computes its rows and stores every value into every rank's output (NVLink stores);
 //   2. each CTA leaves its best (value, global index) in the local header, fences at system scope
 //      and counts itself in;
-//   3. the last CTA reduces the rank's pair, stores it into every rank's pair slot, fences, and
-//      releases its flag slot in every rank (system scope) with the call's epoch;
-//   4. it then waits (bounded) for every rank's flag in its own header, and writes the first-index
+//   3. the last CTA fences at system scope (every CTA's rows now precede what it stores next),
+//      reduces the rank's pair and stores it into every rank's pair slot as two 64-bit words
+//      {epoch, value bits} and {epoch, index}: each word is single-copy atomic, so a reader that
+//      sees the epoch in both sees the pair, and the pair doubles as the rank's "rows are in" flag;
+//   4. it then waits (bounded) until every rank's words in its own header carry the epoch, fences
+//      at system scope (the peers' rows become visible to what follows), and writes the first-index
 //      maximum over the ranks' pairs as the token.
-// The epoch is the caller's call counter, identical on every rank, so flags never need resetting.
+// The epoch counts the calls, identically on every rank, so the slots never need resetting.
 constexpr int kP2PMaxRanks = 8;
 constexpr unsigned long long kP2PWaitNs = 2000000000ull;
 
-struct P2PHeader {
-    unsigned flags[kP2PMaxRanks];     // flags[r]: the last epoch rank r has published into this buffer
-    ArgPair pairs[2][kP2PMaxRanks];   // pairs[e & 1][r]: rank r's (max value, first global index) of call e
-    int counter;                      // arrivals of this rank's CTAs (reset by the last one)
-    int err;                          // 5: a wait for a peer's flag expired
-    unsigned calls;                   // this rank's calls so far (written by the last CTA of each call)
-    int pad[13];
+struct alignas(16) P2PHeader {
+    // pair[e & 1][r]: rank r's pair of call e as {e << 32 | value bits, e << 32 | index}
+    unsigned long long pair[2][kP2PMaxRanks][2];
+    int counter;      // arrivals of this rank's CTAs (reset by the last one)
+    int err;          // 5: a wait for a peer's pair expired
+    unsigned calls;   // this rank's calls so far (written by the last CTA of each call)
+    int pad[29];
 };
 
 struct P2PArgs {
@@ -939,16 +942,15 @@ struct P2PArgs {
     int32_t* token;
 };
 
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v)
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v)
 {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p)
+__device__ __forceinline__ void ld_relaxed_sys_v2u64(const unsigned long long* p, unsigned long long& a,
+                                                     unsigned long long& b)
 {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 
 // Rows of a CTA's output gathered in shared memory before they leave for every rank (a multiple of
@@ -1042,32 +1044,35 @@ __global__ void __launch_bounds__(kThreads) k_gemv_allgather(P2PArgs p)
     P2PHeader* own = p.hdr[p.rank];
     own->counter = 0;
     const int ps = epoch & 1u;
-    for (int r = 0; r < p.world; ++r)
-        p.hdr[r]->pairs[ps][p.rank] = mine;
-    __threadfence_system();
-    for (int r = 0; r < p.world; ++r)
-        st_release_sys(&p.hdr[r]->flags[p.rank], epoch);
-    // every rank's slice and pair are in this buffer once its flag carries this epoch (or the next one:
-    // a peer one call ahead has written the other slots)
+    const unsigned long long tag = (unsigned long long)epoch << 32;
+    for (int r = 0; r < p.world; ++r) {
+        st_relaxed_sys_u64(&p.hdr[r]->pair[ps][p.rank][0], tag | __float_as_uint(mine.v));
+        st_relaxed_sys_u64(&p.hdr[r]->pair[ps][p.rank][1], tag | (unsigned)mine.i);
+    }
+    // Every rank's slice and pair are in this buffer once its pair words carry this epoch (a peer one
+    // call ahead writes the other slot).
     const unsigned long long t0 = now_ns_ops();
     bool ok = true;
+    float bv2 = -INFINITY;
+    int bi2 = INT_MAX;
     for (int r = 0; r < p.world && ok; ++r) {
-        while ((int)(ld_acquire_sys(&own->flags[r]) - epoch) < 0) {
+        unsigned long long wv, wi;
+        for (;;) {
+            ld_relaxed_sys_v2u64(&own->pair[ps][r][0], wv, wi);
+            if ((unsigned)(wv >> 32) == epoch && (unsigned)(wi >> 32) == epoch)
+                break;
             if (now_ns_ops() - t0 > kP2PWaitNs) {
                 ok = false;
                 atomicMax(&own->err, 5);
                 break;
             }
         }
+        if (ok && pair_better(__uint_as_float((unsigned)wv), (int)(unsigned)wi, bv2, bi2))
+            bv2 = __uint_as_float((unsigned)wv), bi2 = (int)(unsigned)wi;
     }
-    float bv2 = -INFINITY;
-    int bi2 = INT_MAX;
-    if (ok)
-        for (int r = 0; r < p.world; ++r) {
-            const ArgPair q{__ldcg(&own->pairs[ps][r].v), __ldcg(&own->pairs[ps][r].i)};
-            if (pair_better(q.v, q.i, bv2, bi2))
-                bv2 = q.v, bi2 = q.i;
-        }
+    __threadfence_system();  // the peers' rows, published before their pair words, precede what follows
+    if (!ok)
+        bi2 = INT_MAX;
     *p.token = bi2 == INT_MAX ? 0 : bi2;
     own->calls = epoch;
 }
@@ -1573,9 +1578,20 @@ extern "C" int muyo_cuda_mat_vec_f16_allgather(MuyoP2PGroup* g, const MuyoMatVec
     MUYO_REQUIRE((uint64_t)row_begin + p->rows <= g->rows_total, "mat_vec_allgather: rows [%u, %u) exceed %u", row_begin,
                  row_begin + p->rows, g->rows_total);
     MatVecDev q{};
-    int rc = mat_vec_prepare(p, a, b, reinterpret_cast<float*>(g->buf), nullptr, nullptr, 2, q);
-    if (rc != MUYO_OK)
-        return rc;
+    if (p->rows == 0) {
+        // An empty shard (more ranks than rows): the rank still takes part in the exchange, with a
+        // pair that never wins; A is not read.
+        MUYO_REQUIRE(b && p->ncols > 0 && p->ncols <= (uint32_t)kMaxStagedK, "mat_vec_allgather: ncols %u outside 1..%d",
+                     p->ncols, kMaxStagedK);
+        q.ncols = (int)p->ncols;
+        q.rows = 0;
+        q.stride_a = q.ncols;
+        q.k8 = q.ncols / 8;
+    } else {
+        int rc = mat_vec_prepare(p, a, b, reinterpret_cast<float*>(g->buf), nullptr, nullptr, 2, q);
+        if (rc != MUYO_OK)
+            return rc;
+    }
     MUYO_REQUIRE(q.k8 > 0 && aligned16(b), "mat_vec_allgather: A and x must be 16-byte aligned with rows a multiple of 8");
     P2PArgs args{};
     args.A = static_cast<const __half*>(a);
@@ -1616,7 +1632,7 @@ extern "C" int muyo_cuda_mat_vec_f16_allgather(MuyoP2PGroup* g, const MuyoMatVec
     if (grid > g->max_ctas)
         grid = g->max_ctas;
     if (grid > ntiles)
-        grid = ntiles;
+        grid = ntiles > 0 ? ntiles : 1;  // an empty shard runs one CTA: the exchange alone
     const cudaStream_t s = as_stream(stream);
     MUYO_CUDA_TRY(launch_kernel(k, dim3(grid), dim3(kThreads), smem, s, true, args));
     MUYO_LAUNCH_CHECK();

@@ -178,6 +178,19 @@ def _p2p_worker(rank, world, port, results):
             out.extend((int(g_tokens[k].item()), plants[k][0], bool(torch.equal(g_outs[k], fulls[k])))
                        for k in range(2))
         del graph
+        # More ranks than rows: rank 1's shard is empty and still takes part in the exchange.
+        wt = rng.standard_normal((1, COLS)).astype(np.float16)
+        b1, e1 = shard.shard_rows(1, world, rank)
+        tiny = shard.P2PShardedGemv(torch.from_numpy(wt[b1:e1].copy()).cuda(), 1, world, rank)
+        tok = tiny(xs[0])
+        y1 = tiny.output()
+        torch.cuda.synchronize()
+        tiny.check()
+        full1 = torch.empty(1, dtype=torch.float32, device="cuda")
+        nodes.mat_vec_f16(nodes.mat_vec_params(COLS, 1), torch.from_numpy(wt).cuda(), xs[0], full1)
+        torch.cuda.synchronize()
+        out.append((int(tok.item()), 0, bool(torch.equal(y1, full1))))
+        tiny.close()
         # rank 1 sits one call out: rank 0's wait for its flag must expire and be reported
         dist.barrier()
         timed_out = None
@@ -207,7 +220,8 @@ def test_fused_gemv_allgather_two_gpus(cuda):
     pairs and flags through peer memory. The full output is bit-identical to one GPU's GEMV on
     every rank, and the token is the planted first-index maximum, also for back-to-back calls with a
     different maximum each (the output and pair slots alternate by call) and for calls replayed from a
-    CUDA graph (the call count lives on the device). A rank that skips a call
+    CUDA graph (the call count lives on the device), and with more ranks than rows (an empty shard
+    takes part in the exchange). A rank that skips a call
     makes the others' bounded wait expire with MUYO_ETIMEOUT (no hang), after which the group
     refuses further calls (MUYO_ESTATE)."""
     import torch
