@@ -1,4 +1,4 @@
-"""The multi-GPU row-sharded GEMV + cross-rank greedy pick (muyo_llm_b200.shard), run as world-size-2
+"""The multi-GPU row-sharded GEMV + cross-rank greedy pick (muyo_llm_b200.shard), run as world-size-2 and -4
 gloo ranks on CPU. Each rank computes its row range with the oracle (the CPU stand-in for the CUDA
 kernel); the partition, padding, gather and pair reduction are the product code."""
 from __future__ import annotations
@@ -81,13 +81,15 @@ def _rank(rank, world, port, rows, cols, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("rows", [1001, 4096, 3])
-def test_row_sharded_gemv_world2(rows):
+@pytest.mark.parametrize("rows,world", [(1001, 2), (4096, 2), (3, 2), (1001, 4), (3, 4)])
+def test_row_sharded_gemv_gloo(rows, world):
+    """Every rank ends with the full output and the first-index maximum, also with ragged shards
+    and with more ranks than rows (empty shards)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
 
     oracle.build()
-    cols, world = 96, 2
+    cols = 96
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
