@@ -887,6 +887,10 @@ struct MuyoModel {
     int lm_grid = 0;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
+    // kGraphSteps consecutive steps in one graph: inside it each step's first kernel starts under the
+    // previous step's LM head (programmatic launch), which separate graph launches do not allow
+    cudaGraph_t graph_n = nullptr;
+    cudaGraphExec_t exec_n = nullptr;
     cudaStream_t cap_stream = nullptr;
     int32_t* pinned = nullptr;  // host staging for prompt/output (generate/step synchronise before reuse)
     size_t pinned_ints = 0;
@@ -1384,6 +1388,10 @@ static void free_model(MuyoModel* m)
         cudaGraphExecDestroy(m->exec);
     if (m->graph)
         cudaGraphDestroy(m->graph);
+    if (m->exec_n)
+        cudaGraphExecDestroy(m->exec_n);
+    if (m->graph_n)
+        cudaGraphDestroy(m->graph_n);
     if (m->cap_stream)
         cudaStreamDestroy(m->cap_stream);
     cudaFree(m->rope_cs);
@@ -1558,18 +1566,24 @@ extern "C" int muyo_model_set_tensor(MuyoModel* m, const char* name, const void*
 }
 
 // (Re)records the decode-step graph.
-static int record_graph(MuyoModel* m)
+constexpr int kGraphSteps = 8;
+
+// Captures `steps` decode steps into one graph (a step is position-invariant: the position and the
+// fed token live in device memory).
+static int capture_steps(MuyoModel* m, int steps, cudaGraph_t& graph, cudaGraphExec_t& exec)
 {
-    if (m->exec) {
-        cudaGraphExecDestroy(m->exec);
-        m->exec = nullptr;
+    if (exec) {
+        cudaGraphExecDestroy(exec);
+        exec = nullptr;
     }
-    if (m->graph) {
-        cudaGraphDestroy(m->graph);
-        m->graph = nullptr;
+    if (graph) {
+        cudaGraphDestroy(graph);
+        graph = nullptr;
     }
     MUYO_CUDA_TRY(cudaStreamBeginCapture(m->cap_stream, cudaStreamCaptureModeThreadLocal));
-    int rc = record_step(m, m->cap_stream);
+    int rc = MUYO_OK;
+    for (int i = 0; i < steps && rc == MUYO_OK; ++i)
+        rc = record_step(m, m->cap_stream);
     cudaGraph_t g = nullptr;
     cudaError_t e = cudaStreamEndCapture(m->cap_stream, &g);
     if (rc != MUYO_OK) {
@@ -1578,9 +1592,15 @@ static int record_graph(MuyoModel* m)
         return rc;
     }
     MUYO_CUDA_TRY(e);
-    m->graph = g;
-    MUYO_CUDA_TRY(cudaGraphInstantiate(&m->exec, g, 0));
+    graph = g;
+    MUYO_CUDA_TRY(cudaGraphInstantiate(&exec, g, 0));
     return MUYO_OK;
+}
+
+static int record_graph(MuyoModel* m)
+{
+    const int rc = capture_steps(m, 1, m->graph, m->exec);
+    return rc != MUYO_OK ? rc : capture_steps(m, kGraphSteps, m->graph_n, m->exec_n);
 }
 
 extern "C" int muyo_model_finalize(MuyoModel* m, void* stream)
@@ -1644,7 +1664,8 @@ extern "C" int muyo_model_reset(MuyoModel* m, void* stream)
 }
 
 // Sets the control block for `n_steps` steps starting at the current position, with prompt ids
-// forced up to `prompt_end`, and replays the step graph n_steps times.
+// forced up to `prompt_end`, and runs n_steps steps: the kGraphSteps-step graph while that many are
+// left, then the one-step graph.
 static int run_steps(MuyoModel* m, int prompt_end, int total, int n_steps, cudaStream_t st)
 {
     if (m->engine == 0 && m->sampling) {
@@ -1664,7 +1685,10 @@ static int run_steps(MuyoModel* m, int prompt_end, int total, int n_steps, cudaS
         if (rc)
             return rc;
     } else {
-        for (int i = 0; i < n_steps; ++i)
+        int i = 0;
+        for (; i + kGraphSteps <= n_steps; i += kGraphSteps)
+            MUYO_CUDA_TRY(cudaGraphLaunch(m->exec_n, st));
+        for (; i < n_steps; ++i)
             MUYO_CUDA_TRY(cudaGraphLaunch(m->exec, st));
     }
     m->host_pos += n_steps;
