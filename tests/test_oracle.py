@@ -13,6 +13,7 @@ from __future__ import annotations
 
 import json
 import math
+import sys
 import os
 
 import numpy as np
@@ -252,6 +253,32 @@ def test_sampler_restatement_matches_the_reference_sampler(oracle_mod, case):
         assert ta == tb, (case, step, ta, tb)
         assert np.array_equal(la, lb)
         history.append(ta)
+
+
+def test_sampler_restatement_matches_reference_fixtures(oracle_mod):
+    """oracle_sample against tests/golden/sampler_cases.json, the reference's own Sampler's draws on
+    the same seeded inputs (written by tests/golden/make_sampler_golden.py): every drawn id and the
+    bits of the logits the sampler leaves behind, for 5 parameter sets x 40 consecutive draws. This
+    pins the restatement where the reference tree (and so oracle/_ref) is absent."""
+    import hashlib
+    import json
+
+    sys.path.insert(0, GOLDEN)
+    import make_sampler_golden as msg
+
+    doc = json.load(open(os.path.join(GOLDEN, "sampler_cases.json")))
+    assert len(doc["cases"]) == len(msg.CASES)
+    for c, case in enumerate(doc["cases"]):
+        kw = dict(case["params"], seed=int(case["params"]["seed"]))
+        assert kw == msg.CASES[c]
+        ours = oracle_mod.Sampler(**kw)
+        history, next_logits = msg.inputs(c)
+        for step, (tok, digest) in enumerate(zip(case["tokens"], case["logits_sha256"])):
+            logits = next_logits()
+            t = ours.sample(logits, history)
+            assert t == tok, (c, step, t, tok)
+            assert hashlib.sha256(logits.tobytes()).hexdigest() == digest, (c, step)
+            history.append(t)
 
 
 def test_mt19937_64_known_answer(oracle_mod):
