@@ -6,6 +6,7 @@ the checker or as the timed CPU baseline. The product path never does.
 from __future__ import annotations
 
 import ctypes as C
+import json
 import os
 import subprocess
 
@@ -269,8 +270,15 @@ REF_TOKENIZER = os.path.join(HERE, "_ref", "libtokenizer_ref.so")
 
 
 def reference_tree() -> str | None:
-    """The muyo-llm source tree named by the environment variable MUYO_REFERENCE, if it is there."""
+    """The muyo-llm source tree named by the environment variable MUYO_REFERENCE, else by the
+    "reference_path" of the repository's BASELINE.json; None unless its sources are there."""
     ref = os.environ.get("MUYO_REFERENCE")
+    if not ref:
+        try:
+            with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+                ref = json.load(f).get("reference_path")
+        except (OSError, ValueError):
+            ref = None
     return ref if ref and os.path.exists(os.path.join(ref, "src", "Sampler.cpp")) else None
 
 
