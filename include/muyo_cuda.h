@@ -258,9 +258,10 @@ int muyo_cuda_layer_step(const MuyoQwen2Config* c, const MuyoLayerWeights* w, vo
 /* ---- whole model (RunFullModel's engine) ---------------------------------------------------------
  * Replaces RunFullModel's graph build, weight upload and per-token feedToken/sampleNext loop
  * (src/FullModel.cpp:487-1291, header src/FullModel.h:34). The model owns its device weights, KV
- * cache and scratch (allocated once, in create/finalize - never per token). One decode step is one
- * CUDA-graph replay of 5*layers+1 kernels; the position, the fed token and the greedy pick live in
- * device memory, so a whole prompt + generation is a loop of replays with no host round trip. */
+ * cache and scratch (allocated once, in create/finalize - never per token). One decode step is
+ * 5*layers+1 kernels captured in a CUDA graph (graphs of one and of eight steps, replayed in turn);
+ * the position, the fed token and the greedy pick live in device memory, so a whole prompt +
+ * generation is a loop of replays with no host round trip. */
 typedef struct MuyoModel MuyoModel;
 int muyo_model_create(const MuyoQwen2Config* c, int device, MuyoModel** out);
 /* Upload one tensor by its GGUF name (src/FullModel.cpp:582-601), from host memory: F16 matrices
@@ -272,7 +273,7 @@ int muyo_model_load_gguf(MuyoModel* m, const char* path);
  * rope base of a GGUF file, and the vocabulary size as the length of tokenizer.ggml.tokens; the
  * cache capacity and KV type are the caller's. Reads the metadata only (no device work). */
 int muyo_gguf_read_qwen2_config(const char* path, uint32_t max_seq, uint32_t kv_dtype, MuyoQwen2Config* out);
-/* Check every tensor is present and build the step graph. */
+/* Check every tensor is present and build the step graphs. */
 int muyo_model_finalize(MuyoModel* m, void* stream);
 /* Empty the KV cache (positions restart at 0). */
 int muyo_model_reset(MuyoModel* m, void* stream);
